@@ -1,0 +1,8 @@
+"""B200-native grouped multi-LoRA apply (drop-in for the WarpPipeEngine of
+vac014/AdapterSlotsPlusPlus). Compute runs in libwp_b200.so (sm_100a)."""
+
+from .config import WarpPipeConfig
+from .engine import WarpPipeEngine
+from .scheduler_bridge import AdapterIdMap, segments_to_warp_pipe
+
+__all__ = ["WarpPipeConfig", "WarpPipeEngine", "AdapterIdMap", "segments_to_warp_pipe"]

@@ -1,0 +1,127 @@
+"""ctypes binding of libwp_b200.so (the C ABI in include/wp_api.h).
+
+The library is the only compute path: there is no CPU or stock-kernel
+fallback. Importing this module does not need a GPU; loading the library
+does not either (it links the CUDA runtime statically and calls nothing at
+load time). Any call that needs a device fails loudly when there is none.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from pathlib import Path
+
+PKG = Path(__file__).resolve().parent
+LIB_PATH = PKG / "libwp_b200.so"
+
+WP_OK = 0
+WP_NOT_HANDLED = 1
+WP_ERR_INVALID = -1
+WP_ERR_CUDA = -2
+WP_ERR_UNKNOWN_ADAPTER = -3
+WP_ERR_CAPACITY = -4
+WP_ERR_NCCL = -5
+WP_ERR_DEVICE_TIMEOUT = -6
+
+WP_DTYPE_F16 = 0
+WP_DTYPE_BF16 = 1
+WP_DTYPE_F32 = 2
+WP_DTYPE_I32 = 3
+WP_DTYPE_I64 = 4
+
+WP_TABLE_LIVE = 0
+WP_TABLE_REGISTRY = 1
+
+
+class WpConfig(ctypes.Structure):
+    _fields_ = [
+        ("device", ctypes.c_int32),
+        ("max_tokens", ctypes.c_int32),
+        ("num_staging_slots", ctypes.c_int32),
+        ("slot_bytes", ctypes.c_int64),
+        ("ctas_per_sm", ctypes.c_int32),
+        ("use_pdl", ctypes.c_int32),
+    ]
+
+
+class WpSegment(ctypes.Structure):
+    _fields_ = [("adapter_id", ctypes.c_int32), ("token_start", ctypes.c_int32), ("token_count", ctypes.c_int32)]
+
+
+_vp = ctypes.c_void_p
+_i32 = ctypes.c_int32
+_i64 = ctypes.c_int64
+_f32 = ctypes.c_float
+_int = ctypes.c_int
+
+# name -> (restype, argtypes); every function declared in include/wp_api.h.
+SIGNATURES = {
+    "wp_create": (_int, [ctypes.POINTER(WpConfig), ctypes.POINTER(_vp)]),
+    "wp_destroy": (_int, [_vp]),
+    "wp_last_error": (ctypes.c_char_p, [_vp]),
+    "wp_rank_supported": (_int, [_i32]),
+    "wp_kernel_launch_count": (_i64, [_vp]),
+    "wp_register_adapter": (_int, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _i32]),
+    "wp_register_adapter_host": (_int, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _i32]),
+    "wp_evict_adapter": (_int, [_vp, _i32]),
+    "wp_build_segments": (_int, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32), _i32, _vp]),
+    "wp_build_seg_bounds": (_int, [_vp, _vp, _i32, _i32, _vp]),
+    "wp_read_seg_table": (_int, [_vp, _i32, ctypes.POINTER(WpSegment), _i32, ctypes.POINTER(_i32)]),
+    "wp_shrink": (_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]),
+    "wp_expand": (_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]),
+    "wp_add_lora": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _i32, _i32, _i32, _i32, _i64, _i64, _i32,
+                           _i32, _vp]),
+    "wp_add_lora_shrink": (_int, [_vp, _vp, _vp, _vp, _i64, _f32, _i32, _i32, _i32, _i64, _i32, _vp]),
+    "wp_add_lora_expand": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32, _i32, _vp]),
+    "wp_prefetch_adapter": (_i32, [_vp, _i32]),
+    "wp_prefetch_adapter_on": (_i32, [_vp, _i32, _vp]),
+    "wp_is_prefetch_ready": (_i32, [_vp, _i32]),
+    "wp_release_prefetch": (_int, [_vp, _i32]),
+    "wp_slot_stats": (_int, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
+    "wp_device_error": (_int, [_vp, _i32, ctypes.POINTER(_i32)]),
+    "wp_tp_unique_id_bytes": (_i32, []),
+    "wp_tp_get_unique_id": (_int, [_vp]),
+    "wp_tp_init": (_int, [_vp, _vp, _i32, _i32]),
+    "wp_tp_allreduce_f32": (_int, [_vp, _vp, _i64, _vp]),
+    "wp_tp_destroy": (_int, [_vp]),
+}
+
+_LIB = None
+
+
+class WarpPipeError(RuntimeError):
+    """An error status returned by libwp_b200.so."""
+
+    def __init__(self, code: int, msg: str):
+        super().__init__(f"[wp status {code}] {msg}")
+        self.code = code
+
+
+def load(build_if_missing: bool = True) -> ctypes.CDLL:
+    """Load libwp_b200.so, building it in-tree first when it is missing."""
+    global _LIB
+    if _LIB is not None:
+        return _LIB
+    if not LIB_PATH.exists() or os.environ.get("WP_REBUILD") == "1":
+        if not build_if_missing:
+            raise ImportError(f"{LIB_PATH} is not built; run python -m adapterslotsplusplus_b200.build")
+        from .build import build
+
+        build()
+    lib = ctypes.CDLL(str(LIB_PATH), mode=ctypes.RTLD_LOCAL)
+    for name, (res, args) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = res
+        fn.argtypes = args
+    _LIB = lib
+    return lib
+
+
+def check(rc: int, handle=None) -> int:
+    """Raise WarpPipeError for negative statuses; return rc otherwise."""
+    if rc < 0:
+        lib = load()
+        msg = lib.wp_last_error(handle).decode(errors="replace")
+        raise WarpPipeError(rc, msg)
+    return rc

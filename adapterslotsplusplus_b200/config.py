@@ -1,0 +1,25 @@
+"""Engine configuration (mirror of lora_warp_pipe/config.py:4-9 of the reference).
+
+The reference fields keep their meaning: ``rank`` is the default rank of
+register_adapter; ``num_staging_slots`` is the size of the staging pool (the
+reference hard-codes WP_MAX_STAGING = 8; here the field is honoured). The
+remaining fields size the device tables and tune the kernels.
+"""
+
+from dataclasses import dataclass
+
+
+@dataclass
+class WarpPipeConfig:
+    enabled: bool = True
+    rank: int = 32
+    num_staging_slots: int = 8
+    min_segment_tokens: int = 4  # kept for signature parity; the reference never reads it either
+    # capacity of the per-step tables: the largest token count of one step
+    max_tokens: int = 16384
+    # bytes of one staging slot (A and B of one adapter); 0 = rank 64 x 16384 x 2 matrices
+    slot_bytes: int = 0
+    # programmatic dependent launch between consecutive apply kernels
+    use_pdl: bool = True
+    # persistent CTAs per SM of the apply kernels
+    ctas_per_sm: int = 1

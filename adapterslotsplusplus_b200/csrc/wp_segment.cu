@@ -1,0 +1,124 @@
+// wp_segment.cu -- device segmenter: token -> adapter id vector to the
+// segment table, once per step, without a host sync.
+//
+// Output contract (bit-exact with build_seg_bounds_kernel,
+// csrc/kernels/warp_pipe_r32.cu:461-512 of the reference): walk the ids in
+// token order; a run starts at i == 0 or where idx[i] != idx[i-1]; runs with
+// id < 0 are dropped; every other run [s, e) becomes ceil((e-s)/32) entries
+// (id, s + 32*j, min(32, e - s - 32*j)); entries are ordered by token
+// position; num_segments is their count.
+//
+// Design: one CTA of 1024 threads walks the tokens in 1024-wide tiles with
+// two block-wide prefix sums. Pass 1 compacts run-start positions into
+// `run_starts` (a device workspace), pass 2 turns run k into its piece count
+// (its length is run_starts[k+1] - run_starts[k]) and scatters the pieces at
+// the exclusive prefix of the counts. Work is O(T) with no serial scan of a
+// run, so a 4096-token prefill run costs no more than 4096 one-token runs.
+// The reference's cap of 256 tokens (one thread per token) is lifted: T is
+// bounded only by the caller's table capacity.
+
+#include <cuda_runtime.h>
+#include <stdint.h>
+
+#include "wp_internal.h"
+
+namespace wp {
+
+constexpr int kSegThreads = 1024;
+
+// Block-wide exclusive scan of one int per thread; *total receives the sum.
+__device__ __forceinline__ int block_exclusive_scan(int v, int* warp_buf, int* total) {
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  int incl = v;
+#pragma unroll
+  for (int off = 1; off < 32; off <<= 1) {
+    const int n = __shfl_up_sync(0xffffffffu, incl, off);
+    if (lane >= off) incl += n;
+  }
+  if (lane == 31) warp_buf[warp] = incl;
+  __syncthreads();
+  if (warp == 0) {
+    int w = warp_buf[lane];  // 32 warps in a 1024-thread block
+    int wi = w;
+#pragma unroll
+    for (int off = 1; off < 32; off <<= 1) {
+      const int n = __shfl_up_sync(0xffffffffu, wi, off);
+      if (lane >= off) wi += n;
+    }
+    warp_buf[lane] = wi - w;  // exclusive prefix of warp totals
+    if (lane == 31) warp_buf[32] = wi;
+  }
+  __syncthreads();
+  const int excl = warp_buf[warp] + incl - v;
+  *total = warp_buf[32];
+  __syncthreads();  // warp_buf is reused by the next call
+  return excl;
+}
+
+template <typename I>
+__global__ void __launch_bounds__(kSegThreads, 1)
+    seg_bounds_kernel(const I* __restrict__ idx, int T, DevSeg* __restrict__ segs, int* __restrict__ num_segs,
+                      int* __restrict__ run_starts) {
+  __shared__ int warp_buf[33];
+  const int tid = threadIdx.x;
+
+  // Pass 1: positions where a run starts, compacted in token order.
+  int nruns = 0;
+  for (int base = 0; base < T; base += kSegThreads) {
+    const int i = base + tid;
+    int flag = 0;
+    if (i < T) flag = (i == 0) || (idx[i] != idx[i - 1]);
+    int total;
+    const int pos = block_exclusive_scan(flag, warp_buf, &total);
+    if (flag) run_starts[nruns + pos] = i;
+    nruns += total;
+  }
+  __syncthreads();  // run_starts written by other threads of this block
+
+  // Pass 2: each run -> ceil(len / 32) pieces, skipping id < 0.
+  int nseg = 0;
+  for (int base = 0; base < nruns; base += kSegThreads) {
+    const int k = base + tid;
+    int pieces = 0, start = 0, len = 0;
+    int32_t id = -1;
+    if (k < nruns) {
+      start = run_starts[k];
+      const int end = (k + 1 < nruns) ? run_starts[k + 1] : T;
+      len = end - start;
+      const I raw = idx[start];
+      if (raw >= 0) {
+        id = static_cast<int32_t>(raw);
+        pieces = (len + kSegTokens - 1) / kSegTokens;
+      }
+    }
+    int total;
+    const int slot = nseg + block_exclusive_scan(pieces, warp_buf, &total);
+    for (int j = 0; j < pieces; ++j) {
+      DevSeg s;
+      s.adapter_id = id;
+      s.token_start = start + j * kSegTokens;
+      s.token_count = min(kSegTokens, len - j * kSegTokens);
+      s.alpha = 0.f;
+      s.a = nullptr;
+      s.b = nullptr;
+      segs[slot + j] = s;
+    }
+    nseg += total;
+  }
+  if (tid == 0) *num_segs = nseg;
+}
+
+cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs,
+                              int* run_starts, cudaStream_t stream) {
+  if (idx_dtype == 4) {
+    seg_bounds_kernel<int64_t><<<1, kSegThreads, 0, stream>>>(static_cast<const int64_t*>(idx), T, segs,
+                                                               num_segs, run_starts);
+  } else {
+    seg_bounds_kernel<int32_t><<<1, kSegThreads, 0, stream>>>(static_cast<const int32_t*>(idx), T, segs,
+                                                               num_segs, run_starts);
+  }
+  return cudaGetLastError();
+}
+
+}  // namespace wp

@@ -1,0 +1,477 @@
+"""Benchmark: grouped multi-LoRA apply per decode step.
+
+Workload: a Llama-2-7B-shaped stack, 32 layers x 7
+LoRA projections (q,k,v,o: 4096->4096; gate,up: 4096->11008; down:
+11008->4096), rank 32, bf16, 64 resident adapters, 256 decode tokens, adapter
+popularity Zipf(1.1) with seed 1 (stable-sorted ids). One build_seg_bounds
+per step, then the 224 add_lora calls of the step replayed from one CUDA
+graph. Weights are random (seeded), activations synthetic.
+
+Metric: LoRA apply us per decode step (lower is better) and the HBM GB/s it
+implies against the measured peak. One JSON line on rank 0.
+
+  python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-sweep]
+
+--impl reference times the reference's CPU implementation of the path (its
+torch per-segment fp32 math, tests/correctness/reference_bgmv.py:4-18,
+restated in oracle/apply.py) on the host cores, on a bounded sample of the
+same workload (a few layers, extrapolated to 32).
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+import numpy as np
+import torch
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+from tests.golden.cases import zipf_ids  # noqa: E402  (seeded Zipf id generator)
+
+LAYERS = 32
+HIDDEN = 4096
+INTER = 11008
+RANK = 32
+TOKENS = 256
+RESIDENT = 64
+SEED = 1
+# (name, d_in, d_out, input activation)
+PROJS = [("q", HIDDEN, HIDDEN, "h"), ("k", HIDDEN, HIDDEN, "h"), ("v", HIDDEN, HIDDEN, "h"),
+         ("o", HIDDEN, HIDDEN, "attn"), ("gate", HIDDEN, INTER, "h"), ("up", HIDDEN, INTER, "h"),
+         ("down", INTER, HIDDEN, "inter")]
+WORKLOAD = "llama2-7b decode step: 32 layers x 7 LoRA projections, rank 32, bf16, 64 resident, 256 tokens, Zipf(1.1) seed 1"
+METRIC = "LoRA apply us/decode-step (HBM GB/s vs peak), 7B x 32 layers, r32, 64 resident, T=256"
+
+
+def algorithmic_bytes(U: int, T: int, d: int, o: int, r: int, elt: int = 2) -> tuple[int, int]:
+    """(shrink bytes, expand bytes) of one projection call: each active
+    adapter's weights once, X read, Y read+write, fp32 H written and read."""
+    shrink = U * d * r * elt + T * d * elt + T * r * 4
+    expand = U * o * r * elt + 2 * T * o * elt + T * r * 4
+    return shrink, expand
+
+
+def step_bytes(U: int, T: int, r: int = RANK) -> tuple[int, int]:
+    s = e = 0
+    for _, d, o, _ in PROJS:
+        bs, be = algorithmic_bytes(U, T, d, o, r)
+        s += bs
+        e += be
+    return s * LAYERS, e * LAYERS
+
+
+def measured_peaks() -> dict:
+    p = ROOT / "MEASURED_PEAKS.json"
+    if p.exists():
+        try:
+            return json.loads(p.read_text())
+        except Exception:
+            pass
+    return {}
+
+
+class ClockSampler:
+    """nvidia-smi SM clocks and throttle reasons sampled every 200 ms."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, index: int):
+        self.index = index
+        self.proc = None
+        self.lines: list[str] = []
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
+                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+        except Exception:
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except Exception:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], None, set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for ln in self.lines:
+            parts = [p.strip() for p in ln.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx = float(parts[2])
+            except ValueError:
+                continue
+            for n, v in zip(names, parts[5:9]):
+                if v.lower() == "active":
+                    reasons.add(n)
+        return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------------------
+# workload
+
+
+def make_ids(resident: int, T: int = TOKENS, seed: int = SEED) -> np.ndarray:
+    return zipf_ids(resident, T, seed=seed)
+
+
+class Stack:
+    """Device-resident stacked LoRA weights + activations of the 7B stack."""
+
+    def __init__(self, device, resident, layers=LAYERS, T=TOKENS, dtype=torch.bfloat16, seed=0):
+        g = torch.Generator(device=device).manual_seed(seed)
+        self.layers = []
+        for _ in range(layers):
+            L = {}
+            for name, d, o, _ in PROJS:
+                wa = torch.randn(resident, 1, RANK, d, device=device, dtype=dtype, generator=g) * 0.02
+                wb = torch.randn(resident, 1, o, RANK, device=device, dtype=dtype, generator=g) * 0.02
+                L[name] = (wa, wb, torch.zeros(T, o, device=device, dtype=dtype))
+            L["x"] = {"h": torch.randn(T, HIDDEN, device=device, dtype=dtype, generator=g) * 0.1,
+                      "attn": torch.randn(T, HIDDEN, device=device, dtype=dtype, generator=g) * 0.1,
+                      "inter": torch.randn(T, INTER, device=device, dtype=dtype, generator=g) * 0.1}
+            self.layers.append(L)
+
+    def calls(self):
+        for L in self.layers:
+            for name, d, o, src in PROJS:
+                wa, wb, y = L[name]
+                yield y, L["x"][src], wa, wb
+
+
+def capture(fn, warm=2):
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        for _ in range(warm):
+            fn()
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    g = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(g):
+        fn()
+    torch.cuda.synchronize()
+    return g
+
+
+def time_graph(g, pre, iters):
+    """Device time of `iters` replays (pre() runs before each, eagerly)."""
+    start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    start.record()
+    for _ in range(iters):
+        if pre is not None:
+            pre()
+        g.replay()
+    end.record()
+    torch.cuda.synchronize()
+    return start.elapsed_time(end) / iters  # ms
+
+
+def run_ours(args, rank, world, local_rank):
+    from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine, _lib
+
+    device = torch.device("cuda", local_rank)
+    torch.cuda.set_device(device)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096), device=device)
+    scale = 16.0 / RANK
+
+    ids = make_ids(RESIDENT)
+    U = int(np.unique(ids).size)
+    idx_dev = torch.as_tensor(ids, device=device)
+    stack = Stack(device, RESIDENT)
+    calls = list(stack.calls())
+
+    def full_step():
+        for y, x, wa, wb in calls:
+            eng.add_lora_packed(y, x, wa, wb, scale)
+
+    # kernel-only graphs: the shrink and expand halves of the same 224 calls
+    lib, h = _lib.load(), eng.handle
+    H = torch.zeros(4096, RANK, dtype=torch.float32, device=device)
+    stream_of = lambda: torch.cuda.current_stream(device).cuda_stream  # noqa: E731
+
+    def shrinks():
+        for y, x, wa, wb in calls:
+            _lib.check(lib.wp_add_lora_shrink(h, H.data_ptr(), x.data_ptr(), wa.data_ptr(), wa.stride(0), scale,
+                                              TOKENS, x.size(1), RANK, x.stride(0), _lib.WP_DTYPE_BF16, stream_of()), h)
+
+    def expands():
+        for y, x, wa, wb in calls:
+            _lib.check(lib.wp_add_lora_expand(h, y.data_ptr(), H.data_ptr(), wb.data_ptr(), wb.stride(0), TOKENS,
+                                               y.size(1), RANK, y.stride(0), 0, _lib.WP_DTYPE_BF16, stream_of()), h)
+
+    seg = lambda: eng.build_seg_bounds(idx_dev)  # noqa: E731
+    seg()
+    g_full = capture(full_step)
+    g_shr = capture(shrinks)
+    g_exp = capture(expands)
+
+    for _ in range(args.warmup):
+        seg()
+        g_full.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    torch.cuda.synchronize()
+
+    with ClockSampler(local_rank) as clk:
+        ms = time_graph(g_full, seg, args.steps)
+        ms_shr = time_graph(g_shr, None, max(3, args.steps))
+        ms_exp = time_graph(g_exp, None, max(3, args.steps))
+    torch.cuda.synchronize()
+    if world > 1:
+        t = torch.tensor([ms, ms_shr, ms_exp], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms, ms_shr, ms_exp = t.tolist()
+
+    # e2e through the public API: token ids from pinned host memory, the step,
+    # and a read back of one output row, all on the stream, every step.
+    ids_host = torch.as_tensor(ids).pin_memory()
+    out_host = torch.empty(HIDDEN, dtype=torch.bfloat16).pin_memory()
+    y_last = calls[-1][0]
+
+    def e2e_step():
+        idx_dev.copy_(ids_host, non_blocking=True)
+        eng.build_seg_bounds(idx_dev)
+        g_full.replay()
+        out_host.copy_(y_last[0, :HIDDEN], non_blocking=True)
+
+    for _ in range(2):
+        e2e_step()
+    torch.cuda.synchronize()
+    t0 = time.perf_counter()
+    st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    st.record()
+    for _ in range(args.steps):
+        e2e_step()
+    en.record()
+    torch.cuda.synchronize()
+    e2e_ms = max(st.elapsed_time(en), (time.perf_counter() - t0) * 1e3) / args.steps
+
+    shr_b, exp_b = step_bytes(U, TOKENS)
+    total_b = shr_b + exp_b
+    peaks = measured_peaks()
+    hbm = peaks.get("hbm_gbs")
+    peak_src = "measured" if hbm else "fallback"
+    hbm = hbm or 6650.0
+    # dominant kernel: the one with more device time per step
+    dom, dom_ms, dom_b = ("expand", ms_exp, exp_b) if ms_exp >= ms_shr else ("shrink", ms_shr, shr_b)
+    per_launch_ms = dom_ms / (LAYERS * len(PROJS))
+    per_launch_b = dom_b / (LAYERS * len(PROJS))
+    achieved = per_launch_b / (per_launch_ms * 1e-3) / 1e9
+    traffic = None
+    tf = ROOT / "profiles" / "traffic.json"
+    if tf.exists():
+        try:
+            traffic = json.loads(tf.read_text()).get(dom)
+        except Exception:
+            traffic = None
+
+    result = {
+        "metric": METRIC,
+        "value": round(ms * 1e3, 2),
+        "unit": "us/step",
+        "n_gpus": world,
+        "steps": args.steps,
+        "warmup": args.warmup,
+        "ms_per_step": round(ms, 4),
+        "higher_is_better": False,
+        "scaling": "weak",
+        "vs_baseline": None,
+        "dtype": "bf16",
+        "data": "synthetic (seeded random weights and activations, Zipf(1.1) routing)",
+        "config": {"workload": WORKLOAD, "layers": LAYERS, "projections": len(PROJS), "rank": RANK,
+                   "resident_adapters": RESIDENT, "active_adapters": U, "tokens": TOKENS,
+                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "l2": "inputs exceed L2 (10.2 GB of adapter weights per step), no flush needed"},
+        "step_gbs": round(total_b / (ms * 1e-3) / 1e9, 1),
+        "step_frac_of_hbm": round(total_b / (ms * 1e-3) / 1e9 / hbm, 4),
+        "step_bytes": total_b,
+        "kernels_ms_per_step": {"shrink": round(ms_shr, 4), "expand": round(ms_exp, 4)},
+        "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
+                     "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / hbm, 4),
+                     "traffic": traffic, "algorithmic_bytes_per_launch": int(per_launch_b),
+                     "launch_us": round(per_launch_ms * 1e3, 3)},
+        "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "us/step", "h2d_bytes_per_step": int(ids.nbytes),
+                "d2h_bytes_per_step": int(out_host.numel() * 2),
+                "path": "WarpPipeEngine.build_seg_bounds + graph of 224 add_lora_packed calls"},
+        "gpu_launches": args.steps * (1 + 2 * LAYERS * len(PROJS)),
+        "clocks": clk.summary(),
+    }
+    del g_full, g_shr, g_exp, stack, calls
+    torch.cuda.empty_cache()
+    return eng, result
+
+
+def sweep_resident(eng, device, counts, steps):
+    """Flatness: us/step and roofline-normalised time vs resident adapters."""
+    out = []
+    scale = 16.0 / RANK
+    hbm = measured_peaks().get("hbm_gbs", 6650.0)
+    for resident in counts:
+        ids = make_ids(resident)
+        U = int(np.unique(ids).size)
+        idx = torch.as_tensor(ids, device=device)
+        stack = Stack(device, resident, seed=resident)
+        calls = list(stack.calls())
+
+        def step():
+            for y, x, wa, wb in calls:
+                eng.add_lora_packed(y, x, wa, wb, scale)
+
+        eng.build_seg_bounds(idx)
+        g = capture(step, warm=1)
+        for _ in range(2):
+            g.replay()
+        ms = time_graph(g, lambda: eng.build_seg_bounds(idx), steps)
+        sb, eb = step_bytes(U, TOKENS)
+        roof_ms = (sb + eb) / (hbm * 1e9) * 1e3
+        out.append({"resident": resident, "active": U, "us_per_step": round(ms * 1e3, 1),
+                    "gb_per_step": round((sb + eb) / 1e9, 3), "roofline_us": round(roof_ms * 1e3, 1),
+                    "time_over_roofline": round(ms / roof_ms, 3)})
+        del g, stack, calls
+        torch.cuda.empty_cache()
+    if out:
+        base = out[0]
+        for r in out:
+            r["raw_growth"] = round(r["us_per_step"] / base["us_per_step"], 3)
+            r["normalised_growth"] = round(r["time_over_roofline"] / base["time_over_roofline"], 3)
+    return out
+
+
+# ---------------------------------------------------------------------------
+# CPU legs (oracle port of the reference's torch per-segment path)
+
+
+def cpu_reference_layers(n_layers: int, resident: int = RESIDENT, threads: int | None = None, reps: int = 1):
+    """Time the reference's CPU math on n_layers layers of the workload.
+    Returns (seconds per layer, threads used)."""
+    from oracle.apply import reference_bgmv_expand, reference_bgmv_shrink
+    from oracle.seg import seg_bounds
+
+    threads = threads or os.cpu_count() or 1
+    torch.set_num_threads(threads)
+    ids = make_ids(resident)
+    table = seg_bounds(ids)
+    g = torch.Generator().manual_seed(0)
+    weights = []
+    for _ in range(n_layers):
+        L = {}
+        for name, d, o, _ in PROJS:
+            L[name] = ((torch.randn(resident, RANK, d, generator=g) * 0.02).bfloat16(),
+                       (torch.randn(resident, o, RANK, generator=g) * 0.02).bfloat16(),
+                       (torch.randn(TOKENS, d, generator=g) * 0.1).bfloat16(),
+                       torch.zeros(TOKENS, o, dtype=torch.bfloat16))
+        weights.append(L)
+    scale = 16.0 / RANK
+
+    def one_layer(L):
+        for name, d, o, _ in PROJS:
+            wa, wb, x, y = L[name]
+            yf = y.float()
+            for aid, s, n in table:
+                h = reference_bgmv_shrink(x[s:s + n], wa[aid], scale)
+                yf[s:s + n] = reference_bgmv_expand(h, wb[aid], yf[s:s + n])
+            y.copy_(yf)
+
+    one_layer(weights[0])  # warm-up
+    t0 = time.perf_counter()
+    for _ in range(reps):
+        for L in weights:
+            one_layer(L)
+    dt = (time.perf_counter() - t0) / (reps * n_layers)
+    return dt, threads
+
+
+def run_reference(args, rank, world):
+    if rank != 0:
+        return None
+    for _ in range(args.warmup):
+        cpu_reference_layers(1, reps=1)
+    per_layer = []
+    threads = os.cpu_count() or 1
+    for _ in range(args.steps):
+        dt, threads = cpu_reference_layers(1, reps=1)
+        per_layer.append(dt)
+    us = float(np.median(per_layer)) * LAYERS * 1e6
+    sample = f"1 of {LAYERS} layers (7 projections) per step, extrapolated x{LAYERS}"
+    return {
+        "metric": METRIC, "value": round(us, 1), "unit": "us/step", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "weak",
+        "vs_baseline": None, "dtype": "bf16", "data": "synthetic", "impl": "reference",
+        "config": {"workload": WORKLOAD, "parallelism": "cpu"},
+        "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": round(us, 1), "unit": "us/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+    }
+
+
+def main():
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--gpus", type=int, default=1)
+    ap.add_argument("--steps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
+    ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    ap.add_argument("--no-sweep", action="store_true")
+    ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the cpu_baseline sample")
+    args = ap.parse_args()
+    args.warmup = max(args.warmup, 3)
+
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local_rank = int(os.environ.get("LOCAL_RANK", "0"))
+
+    if args.impl == "reference":
+        res = run_reference(args, rank, world)
+        if res is not None:
+            print(json.dumps(res), flush=True)
+        return
+
+    if world > 1:
+        torch.cuda.set_device(local_rank)
+        torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+    eng, result = run_ours(args, rank, world, local_rank)
+    if rank == 0 and world == 1:
+        if not args.no_sweep:
+            result["flatness"] = sweep_resident(eng, torch.device("cuda", local_rank), [1, 8, 64, 128, 512],
+                                                max(3, args.steps // 4))
+        dt, threads = cpu_reference_layers(args.cpu_layers)
+        result["cpu_baseline"] = {"value": round(dt * LAYERS * 1e6, 1), "unit": "us/step", "cores": threads,
+                                  "kind": "port",
+                                  "sample": f"{args.cpu_layers} of {LAYERS} layers timed, extrapolated x{LAYERS}"}
+    if world > 1:
+        torch.distributed.barrier()
+        torch.distributed.destroy_process_group()
+    if rank == 0:
+        print(json.dumps(result), flush=True)
+
+
+if __name__ == "__main__":
+    main()

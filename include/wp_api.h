@@ -1,0 +1,229 @@
+/* wp_api.h -- C ABI of the B200-native grouped multi-LoRA apply library
+ * (libwp_b200.so).
+ *
+ * The library replaces the reference's pybind extension `warp_pipe_ext`
+ * (csrc/pybind, csrc/dispatch, csrc/kernels, csrc/memory of
+ * vac014/AdapterSlotsPlusPlus). Every entry point below names the reference
+ * method it stands in for as `file:line` inside that project.
+ *
+ * Conventions
+ *   - Plain pointers and sizes only; no torch types. Device pointers are
+ *     CUDA device addresses on the handle's device; `stream` is a
+ *     cudaStream_t passed as void*.
+ *   - Return value: 0 = ok; >0 = "not handled" (the Python engine maps it to
+ *     a False return where the reference returns False); <0 = error (the
+ *     engine raises). wp_last_error() gives the message of the last error.
+ *   - One handle per device and thread; calls on one handle are not
+ *     thread-safe (the reference's WarpPipeExtension is not either).
+ *   - Math: A is stored [r, d] (rank-major), B is stored [o, r];
+ *     H[t,:] = alpha * X[t,:] . A^T  (fp32), Y[t,:] += H[t,:] . B^T, with
+ *     alpha applied once, in shrink (tests/correctness/reference_bgmv.py:4-18).
+ */
+#ifndef WP_API_H_
+#define WP_API_H_
+
+#include <stddef.h>
+#include <stdint.h>
+
+#ifdef __cplusplus
+extern "C" {
+#endif
+
+/* status codes */
+#define WP_OK 0
+#define WP_NOT_HANDLED 1
+#define WP_ERR_INVALID (-1)
+#define WP_ERR_CUDA (-2)
+#define WP_ERR_UNKNOWN_ADAPTER (-3)
+#define WP_ERR_CAPACITY (-4)
+#define WP_ERR_NCCL (-5)
+#define WP_ERR_DEVICE_TIMEOUT (-6)
+
+/* element types */
+#define WP_DTYPE_F16 0
+#define WP_DTYPE_BF16 1
+#define WP_DTYPE_F32 2
+#define WP_DTYPE_I32 3
+#define WP_DTYPE_I64 4
+
+/* which segment table wp_read_seg_table returns */
+#define WP_TABLE_LIVE 0     /* built by wp_build_seg_bounds */
+#define WP_TABLE_REGISTRY 1 /* built by wp_build_segments   */
+
+typedef struct wp_handle wp_handle;
+
+typedef struct wp_config {
+  int32_t device;            /* CUDA device ordinal                                  */
+  int32_t max_tokens;        /* capacity of the per-step tables (T), e.g. 16384       */
+  int32_t num_staging_slots; /* GPU staging slots (reference: WP_MAX_STAGING = 8)     */
+  int64_t slot_bytes;        /* bytes per slot for A+B together (0 = 2*64*16384*2)    */
+  int32_t ctas_per_sm;       /* persistent CTAs per SM for the apply kernels (0=auto) */
+  int32_t use_pdl;           /* 1 = programmatic dependent launch between kernels     */
+} wp_config;
+
+/* One entry of the segment table, as read back by wp_read_seg_table.
+ * Mirrors the three fields of SegmentDescriptor the live kernels read
+ * (csrc/bridge/warp_pipe_metadata.h:41-57). */
+typedef struct wp_segment {
+  int32_t adapter_id;
+  int32_t token_start;
+  int32_t token_count;
+} wp_segment;
+
+/* ---- lifetime ---------------------------------------------------------- */
+
+/* Replaces WarpPipeExtension::WarpPipeExtension (warp_pipe_bindings.cpp:20-34):
+ * allocates the device-resident segment tables, workspaces, staging slots and
+ * the private prefetch stream. */
+int wp_create(const wp_config* cfg, wp_handle** out);
+
+/* Replaces ~WarpPipeExtension (warp_pipe_bindings.cpp:36-39). */
+int wp_destroy(wp_handle* h);
+
+/* Message of the last failed call on this handle (or a global message when
+ * h is NULL). Never NULL. */
+const char* wp_last_error(const wp_handle* h);
+
+/* Replaces warp_pipe_rank_supported (csrc/dispatch/warp_pipe_dispatcher.cpp:18):
+ * 1 for r in {8,16,32,64}, else 0. */
+int wp_rank_supported(int32_t rank);
+
+/* Number of kernels this handle has launched so far (all entry points). */
+int64_t wp_kernel_launch_count(const wp_handle* h);
+
+/* ---- adapter store ----------------------------------------------------- */
+
+/* Replaces WarpPipeExtension::register_adapter (warp_pipe_bindings.cpp:110-119)
+ * and AdapterStore::register_adapter (csrc/memory/adapter_store.h:21-27).
+ * A [r,d] and B [o,r] are DEVICE pointers (16-byte aligned, the caller keeps
+ * them alive until eviction). Re-registering an id overwrites it. */
+int wp_register_adapter(wp_handle* h, int32_t adapter_id, const void* A, const void* B, int32_t rank,
+                        int32_t d_model, int32_t out_features, float alpha_scale, int32_t dtype);
+
+/* Pinned-host adapter store (no counterpart in the reference, which keeps
+ * every adapter on the device): A/B are HOST pointers; the library copies
+ * them into its own page-locked store. The adapter reaches the GPU through a
+ * staging slot (wp_prefetch_adapter, or on demand inside wp_build_segments). */
+int wp_register_adapter_host(wp_handle* h, int32_t adapter_id, const void* A_host, const void* B_host,
+                             int32_t rank, int32_t d_model, int32_t out_features, float alpha_scale,
+                             int32_t dtype);
+
+/* Replaces WarpPipeExtension::evict_adapter (warp_pipe_bindings.cpp:121-124).
+ * Unknown ids are a no-op. Frees the adapter's staging slot, if any. */
+int wp_evict_adapter(wp_handle* h, int32_t adapter_id);
+
+/* ---- segment tables ---------------------------------------------------- */
+
+/* Replaces WarpPipeExtension::build_segments (warp_pipe_bindings.cpp:128-130)
+ * -> build_segment_table (csrc/dispatch/segment_builder.cpp:5-50).
+ * K segments, seg_offsets has K+1 entries (host arrays). Errors on a size
+ * mismatch, K > max_tokens or an unknown id, like the reference. The table is
+ * uploaded on `stream`. Adapters that live only in the host store are staged
+ * into a slot on the prefetch stream and `stream` waits for that copy. */
+int wp_build_segments(wp_handle* h, const int32_t* sorted_adapter_ids, const int32_t* seg_offsets, int32_t K,
+                      void* stream);
+
+/* Replaces WarpPipeExtension::build_seg_bounds (warp_pipe_bindings.cpp:162-170)
+ * -> build_seg_bounds_kernel (csrc/kernels/warp_pipe_r32.cu:461-512).
+ * token_lora_indices: DEVICE array of T ints (idx_dtype WP_DTYPE_I32 or
+ * WP_DTYPE_I64). Builds the run-length table (runs of equal ids in token
+ * order, ids < 0 skipped, runs split into pieces of at most 32 tokens) on the
+ * device, without a host sync. Returns WP_NOT_HANDLED (the reference's False)
+ * only when T exceeds max_tokens; the reference's cap is 256. */
+int wp_build_seg_bounds(wp_handle* h, const void* token_lora_indices, int32_t idx_dtype, int32_t T,
+                        void* stream);
+
+/* Test readback of a segment table (the reference exposes none). Synchronises
+ * the handle's device. Writes up to `cap` entries, sets *num to the table's
+ * num_segments. */
+int wp_read_seg_table(wp_handle* h, int32_t which, wp_segment* out, int32_t cap, int32_t* num);
+
+/* ---- apply ------------------------------------------------------------- */
+
+/* Replaces WarpPipeExtension::shrink (warp_pipe_bindings.cpp:132-139) ->
+ * bgmv_shrink_kernel (warp_pipe_r32.cu:56-132, warp_pipe_rgen.cuh:42-135).
+ * Uses the registry table (wp_build_segments). X: device [T, d] (dtype),
+ * H: device [T, r] fp32, caller-zeroed; rows inside segments are written with
+ * alpha_scale(adapter) * X . A^T. */
+int wp_shrink(wp_handle* h, const void* X, void* H, int32_t d_model, int32_t rank, int32_t T, int32_t dtype,
+              void* stream);
+
+/* Replaces WarpPipeExtension::expand (warp_pipe_bindings.cpp:141-148) ->
+ * bgmv_expand_kernel (warp_pipe_r32.cu:141-200, warp_pipe_rgen.cuh:137-189).
+ * H: device [T, r] fp32; Y: device [T, o] (dtype), updated in place. */
+int wp_expand(wp_handle* h, const void* H, void* Y, int32_t out_features, int32_t rank, int32_t T,
+              int32_t dtype, void* stream);
+
+/* Replaces WarpPipeExtension::add_lora_packed (warp_pipe_bindings.cpp:195-234)
+ * -> bgmv_shrink_dsak_kernel + bgmv_expand_dsak_kernel (warp_pipe_r32.cu:280-423),
+ * and covers the sliced-output and non-rank-32 calls the reference sends back
+ * to the stock path (lora_warp_pipe/punica_wrapper.py:147-155).
+ * Uses the live table (wp_build_seg_bounds). For token t in a segment of
+ * adapter i:  y[t, y_offset + j] += (scale * x[t,:] . A_i^T) . B_i[j,:]
+ * with A_i = wa_base + i*wa_stride0 ([r,d] row-major), B_i = wb_base +
+ * i*wb_stride0 ([o,r] row-major), j < out_features. x row stride x_ld, y row
+ * stride y_ld (elements). Graph-capturable: fixed grids, the segment count is
+ * read on the device. */
+int wp_add_lora(wp_handle* h, void* y, const void* x, const void* wa_base, int64_t wa_stride0,
+                const void* wb_base, int64_t wb_stride0, float scale, int32_t T, int32_t d_model,
+                int32_t out_features, int32_t rank, int64_t x_ld, int64_t y_ld, int32_t y_offset,
+                int32_t dtype, void* stream);
+
+/* Shrink half of wp_add_lora, exported for tensor-parallel row-parallel
+ * layers: H [T, r] fp32 (device) receives scale * x . A^T for rows inside
+ * live segments; other rows are left untouched. */
+int wp_add_lora_shrink(wp_handle* h, void* H, const void* x, const void* wa_base, int64_t wa_stride0,
+                       float scale, int32_t T, int32_t d_model, int32_t rank, int64_t x_ld, int32_t dtype,
+                       void* stream);
+
+/* Expand half of wp_add_lora: y[t, y_offset + j] += H[t,:] . B_i[j,:]. */
+int wp_add_lora_expand(wp_handle* h, void* y, const void* H, const void* wb_base, int64_t wb_stride0,
+                       int32_t T, int32_t out_features, int32_t rank, int64_t y_ld, int32_t y_offset,
+                       int32_t dtype, void* stream);
+
+/* ---- staging slots / prefetch ------------------------------------------ */
+
+/* Replaces WarpPipeExtension::prefetch_adapter (warp_pipe_bindings.cpp:46-57)
+ * and StagingBufferPool::acquire_slot (csrc/memory/staging_buffer.h:62-73):
+ * copies the adapter's A/B into a staging slot on the private prefetch
+ * stream. Returns the slot index, or -1 (unknown id, or no free slot). Never
+ * fails otherwise. Re-prefetching an adapter returns its existing slot. */
+int32_t wp_prefetch_adapter(wp_handle* h, int32_t adapter_id);
+
+/* Same as wp_prefetch_adapter, but the copy is ordered after the work queued
+ * so far on `caller_stream` (the stream that produced the adapter's tensors),
+ * without blocking the host. */
+int32_t wp_prefetch_adapter_on(wp_handle* h, int32_t adapter_id, void* caller_stream);
+
+/* Replaces is_prefetch_ready (warp_pipe_bindings.cpp:59-62,
+ * staging_buffer.h:89-93): non-blocking event query. */
+int32_t wp_is_prefetch_ready(wp_handle* h, int32_t adapter_id);
+
+/* Replaces release_prefetch (warp_pipe_bindings.cpp:64, staging_buffer.h:75-79).
+ * Unknown ids are a no-op. */
+int wp_release_prefetch(wp_handle* h, int32_t adapter_id);
+
+/* Slot bookkeeping for tests and benches: number of slots, slots in use, and
+ * the device error flag raised by a timed-out wait inside a kernel (0 = none;
+ * reading it synchronises the device; `clear` resets it). */
+int wp_slot_stats(wp_handle* h, int32_t* num_slots, int32_t* slots_in_use);
+int wp_device_error(wp_handle* h, int32_t clear, int32_t* flag);
+
+/* ---- tensor parallel (no counterpart in the reference) ----------------- */
+
+/* Size of the opaque NCCL unique id blob (ncclUniqueId). */
+int32_t wp_tp_unique_id_bytes(void);
+/* Rank 0 fills `id` (wp_tp_unique_id_bytes() bytes); the caller broadcasts it. */
+int wp_tp_get_unique_id(void* id);
+/* Creates this handle's NCCL communicator over NVLink (one rank per GPU). */
+int wp_tp_init(wp_handle* h, const void* id, int32_t rank, int32_t world);
+/* In-place fp32 sum all-reduce of n floats on `stream` (row-parallel shrink
+ * partials [T, r]). Capturable in a CUDA graph. */
+int wp_tp_allreduce_f32(wp_handle* h, void* buf, int64_t n, void* stream);
+int wp_tp_destroy(wp_handle* h);
+
+#ifdef __cplusplus
+}
+#endif
+
+#endif /* WP_API_H_ */
