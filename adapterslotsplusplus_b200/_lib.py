@@ -42,6 +42,7 @@ class WpConfig(ctypes.Structure):
         ("slot_bytes", ctypes.c_int64),
         ("ctas_per_sm", ctypes.c_int32),
         ("use_pdl", ctypes.c_int32),
+        ("prefetch_weights", ctypes.c_int32),
     ]
 
 
@@ -70,9 +71,9 @@ SIGNATURES = {
     "wp_read_seg_table": (_int, [_vp, _i32, ctypes.POINTER(WpSegment), _i32, ctypes.POINTER(_i32)]),
     "wp_shrink": (_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]),
     "wp_expand": (_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]),
-    "wp_add_lora": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _f32, _i32, _i32, _i32, _i32, _i64, _i64, _i32,
-                           _i32, _vp]),
-    "wp_add_lora_shrink": (_int, [_vp, _vp, _vp, _vp, _i64, _f32, _i32, _i32, _i32, _i64, _i32, _vp]),
+    "wp_add_lora": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _f32, _i32, _i32, _i32, _i32, _i64, _i64,
+                           _i32, _i32, _vp]),
+    "wp_add_lora_shrink": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _i32, _i32, _i32, _i64, _i32, _vp]),
     "wp_add_lora_expand": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32, _i32, _vp]),
     "wp_prefetch_adapter": (_i32, [_vp, _i32]),
     "wp_prefetch_adapter_on": (_i32, [_vp, _i32, _vp]),
@@ -80,6 +81,9 @@ SIGNATURES = {
     "wp_release_prefetch": (_int, [_vp, _i32]),
     "wp_slot_stats": (_int, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "wp_device_error": (_int, [_vp, _i32, ctypes.POINTER(_i32)]),
+    "wp_trace_enable": (_int, [_vp, _i32]),
+    "wp_trace_read": (_int, [_vp, _i32, ctypes.POINTER(ctypes.c_uint64), _i32, ctypes.POINTER(_i32)]),
+    "wp_apply_plan": (_int, [_vp, _i32, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "wp_tp_unique_id_bytes": (_i32, []),
     "wp_tp_get_unique_id": (_int, [_vp]),
     "wp_tp_init": (_int, [_vp, _vp, _i32, _i32]),

@@ -21,5 +21,9 @@ class WarpPipeConfig:
     slot_bytes: int = 0
     # programmatic dependent launch between consecutive apply kernels
     use_pdl: bool = True
-    # persistent CTAs per SM of the apply kernels
-    ctas_per_sm: int = 1
+    # with use_pdl: load adapter weights before the previous kernel on the
+    # stream has finished. Only valid when that kernel never writes the
+    # weights (serving: weights are static while a step runs).
+    prefetch_weights: bool = False
+    # cap on persistent CTAs per SM of the apply kernel (0 = as many as fit)
+    ctas_per_sm: int = 0

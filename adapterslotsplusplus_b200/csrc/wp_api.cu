@@ -1,10 +1,13 @@
 // wp_api.cu -- host side of libwp_b200.so: the C ABI declared in
 // include/wp_api.h. Owns the device segment tables, split-K workspaces, the
 // adapter store (device tensors or the library's own pinned-host copies), the
-// staging-slot pool with its private prefetch stream, and the optional NCCL
-// communicator for tensor-parallel shrink partials.
+// staging-slot pool with its private prefetch stream, the TMA descriptors of
+// every launch, and the optional NCCL communicator for tensor-parallel shrink
+// partials.
 
+#include <cuda.h>
 #include <cuda_runtime.h>
+#include <cudaTypedefs.h>
 #include <nccl.h>
 
 #include <algorithm>
@@ -63,18 +66,15 @@ struct wp_handle {
   DevSeg* d_reg = nullptr;
   int* d_reg_num = nullptr;
   DevSeg* h_reg_stage = nullptr;  // pinned upload buffer (cap + 1 entries, count in the tail)
+  CUtensorMap* d_reg_maps = nullptr;  // TMA descriptors of the registry table's A matrices
+  CUtensorMap* h_reg_maps = nullptr;  // pinned upload buffer of the descriptors
   cudaEvent_t reg_uploaded = nullptr;
   std::vector<wp_segment> reg_table;
   std::vector<DevSeg> reg_pieces;
   int reg_rank = 0;
   int reg_dtype = -1;
 
-  // workspaces
-  float* d_partial = nullptr;
-  int64_t partial_floats = 0;
-  uint32_t* d_counters = nullptr;
-  float* d_live_h = nullptr;  // [max_tokens, 64] fp32 H of wp_add_lora
-  int* d_err = nullptr;
+  int* d_err = nullptr;  // device error word (wp::kErr* bits)
 
   // store + slots
   std::unordered_map<int32_t, Adapter> store;
@@ -85,6 +85,13 @@ struct wp_handle {
   cudaEvent_t registry_done = nullptr;  // after the latest registry kernels
   bool registry_used = false;
   uint64_t generation = 0;
+
+  // apply kernel plan per (dtype, rank): cluster size and persistent grid
+  int plan_cluster[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  int plan_grid[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  // optional per-CTA phase traces of the latest launch (0: fused/shrink, 1: expand-only)
+  unsigned long long* d_trace[2] = {nullptr, nullptr};
+  bool trace_on = false;
 
   // launch bookkeeping
   int64_t launches = 0;
@@ -134,23 +141,58 @@ struct DeviceGuard {
   }
 };
 
-// Split-K plan for shrink: splits of d, each a multiple of the stage width.
-void shrink_plan(const wp_handle* h, int d, int T, int rank, int* nsplit, int* split_len) {
-  const int kc = wp::shrink_chunk_k(rank);
-  int len = std::max(512, ((d + 15) / 16 + kc - 1) / kc * kc);
-  int ns = (d + len - 1) / len;
-  const int64_t plane = static_cast<int64_t>(h->cfg.max_tokens) * rank;
-  const int64_t max_planes = plane > 0 ? h->partial_floats / plane : 1;
-  while (ns > 1 && ns > max_planes) {
-    len += kc;
-    ns = (d + len - 1) / len;
+// cuTensorMapEncodeTiled through the runtime's driver entry point (no link
+// dependency on libcuda).
+PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
+  static PFN_cuTensorMapEncodeTiled_v12000 fn = nullptr;
+  if (!fn) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &p, cudaEnableDefault, &q) == cudaSuccess &&
+        q == cudaDriverEntryPointSuccess)
+      fn = reinterpret_cast<PFN_cuTensorMapEncodeTiled_v12000>(p);
   }
-  (void)T;
-  *nsplit = ns;
-  *split_len = len;
+  return fn;
 }
 
-int grid_size(const wp_handle* h) { return h->num_sms * std::max(1, h->cfg.ctas_per_sm); }
+// Tiled map over 16-bit elements with the 128-byte swizzle. dims[0] is the
+// innermost (contiguous) dimension; strides are in bytes for dims 1..rank-1.
+bool encode_map(CUtensorMap* m, int dtype, int rank, const void* base, const uint64_t* dims,
+                const uint64_t* strides, const uint32_t* box) {
+  auto fn = encode_fn();
+  if (!fn) return false;
+  cuuint64_t gd[3], gs[2];
+  cuuint32_t bx[3], es[3] = {1, 1, 1};
+  for (int i = 0; i < rank; ++i) {
+    gd[i] = dims[i];
+    bx[i] = box[i];
+  }
+  for (int i = 0; i < rank - 1; ++i) gs[i] = strides[i];
+  const CUtensorMapDataType dt =
+      dtype == WP_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
+  CUresult r = fn(m, dt, rank, const_cast<void*>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
+                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  return r == CUDA_SUCCESS;
+}
+
+// A stack [L, r, d] (row stride d, adapter stride `stride0` elements): box 64 x r x 1.
+bool encode_a_map(CUtensorMap* m, int dtype, const void* base, int d, int r, int64_t L, int64_t stride0) {
+  const uint64_t dims[3] = {static_cast<uint64_t>(d), static_cast<uint64_t>(r), static_cast<uint64_t>(L)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(d) * 2, static_cast<uint64_t>(stride0) * 2};
+  const uint32_t box[3] = {static_cast<uint32_t>(wp::kBoxCols), static_cast<uint32_t>(r), 1};
+  return encode_map(m, dtype, 3, base, dims, strides, box);
+}
+
+// Activation rows [T, cols] with row stride ld elements: box 64 x box_rows.
+bool encode_rows_map(CUtensorMap* m, int dtype, const void* base, int cols, int T, int64_t ld, int box_rows) {
+  const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(T)};
+  const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 2};
+  const uint32_t box[2] = {static_cast<uint32_t>(wp::kBoxCols), static_cast<uint32_t>(box_rows)};
+  return encode_map(m, dtype, 2, base, dims, strides, box);
+}
+
+// Upper bound on the CTAs of one apply launch (sizes the trace buffers).
+int grid_size(const wp_handle* h) { return h->num_sms * 4; }
 
 size_t slot_b_offset(size_t a_bytes) { return (a_bytes + 255) / 256 * 256; }
 
@@ -218,7 +260,7 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
   if (cfg.num_staging_slots < 0) cfg.num_staging_slots = 0;
   if (cfg.slot_bytes <= 0) cfg.slot_bytes = static_cast<int64_t>(2) * 64 * 16384 * 2;
   cfg.slot_bytes = (cfg.slot_bytes + 255) / 256 * 256;
-  if (cfg.ctas_per_sm <= 0) cfg.ctas_per_sm = 1;
+  if (cfg.ctas_per_sm < 0) cfg.ctas_per_sm = 0;
 
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
@@ -245,16 +287,12 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
   if ((e = cudaMalloc(&h->d_reg_num, sizeof(int) * 4)) != cudaSuccess) return bail("registry count", e);
   if ((e = cudaHostAlloc(&h->h_reg_stage, sizeof(DevSeg) * (cap + 1), cudaHostAllocDefault)) != cudaSuccess)
     return bail("registry upload buffer", e);
-  // Split-K partials: up to 16 planes of [max_tokens, 64] fp32.
-  h->partial_floats = static_cast<int64_t>(16) * cap * 64;
-  if ((e = cudaMalloc(&h->d_partial, sizeof(float) * h->partial_floats)) != cudaSuccess) return bail("partials", e);
-  if ((e = cudaMalloc(&h->d_counters, sizeof(uint32_t) * cap)) != cudaSuccess) return bail("counters", e);
+  if ((e = cudaMalloc(&h->d_reg_maps, sizeof(CUtensorMap) * cap)) != cudaSuccess) return bail("registry maps", e);
+  if ((e = cudaHostAlloc(&h->h_reg_maps, sizeof(CUtensorMap) * cap, cudaHostAllocDefault)) != cudaSuccess)
+    return bail("registry map upload buffer", e);
   if ((e = cudaMalloc(&h->d_err, sizeof(int) * 4)) != cudaSuccess) return bail("error word", e);
-  if ((e = cudaMalloc(&h->d_live_h, sizeof(float) * static_cast<size_t>(cap) * 64)) != cudaSuccess)
-    return bail("H scratch", e);
   cudaMemset(h->d_live_num, 0, sizeof(int) * 4);
   cudaMemset(h->d_reg_num, 0, sizeof(int) * 4);
-  cudaMemset(h->d_counters, 0, sizeof(uint32_t) * cap);
   cudaMemset(h->d_err, 0, sizeof(int) * 4);
   if ((e = cudaStreamCreateWithFlags(&h->prefetch_stream, cudaStreamNonBlocking)) != cudaSuccess)
     return bail("prefetch stream", e);
@@ -288,10 +326,11 @@ int wp_destroy(wp_handle* h) {
   cudaFree(h->d_reg);
   cudaFree(h->d_reg_num);
   if (h->h_reg_stage) cudaFreeHost(h->h_reg_stage);
-  cudaFree(h->d_partial);
-  cudaFree(h->d_counters);
+  cudaFree(h->d_reg_maps);
+  if (h->h_reg_maps) cudaFreeHost(h->h_reg_maps);
+  cudaFree(h->d_trace[0]);
+  cudaFree(h->d_trace[1]);
   cudaFree(h->d_err);
-  cudaFree(h->d_live_h);
   if (h->reg_uploaded) cudaEventDestroy(h->reg_uploaded);
   if (h->caller_ready) cudaEventDestroy(h->caller_ready);
   if (h->registry_done) cudaEventDestroy(h->registry_done);
@@ -460,8 +499,6 @@ int wp_device_error(wp_handle* h, int32_t clear, int32_t* flag) {
   if (flag) *flag = v;
   if (clear) {
     WP_CUDA(h, cudaMemset(h->d_err, 0, sizeof(int)));
-    // a kernel that gave up may have left split-K counters raised
-    WP_CUDA(h, cudaMemset(h->d_counters, 0, sizeof(uint32_t) * h->cfg.max_tokens));
   }
   return WP_OK;
 }
@@ -481,6 +518,8 @@ int wp_build_segments(wp_handle* h, const int32_t* ids, const int32_t* offs, int
   std::vector<DevSeg> pieces;
   pieces.reserve(K);
   std::vector<int> wait_slots;
+  std::vector<CUtensorMap> maps;  // one TMA descriptor per distinct A matrix
+  std::unordered_map<const void*, int> map_of;
   int rank = 0, dtype = -1;
   for (int i = 0; i < K; ++i) {
     auto it = h->store.find(ids[i]);
@@ -531,13 +570,21 @@ int wp_build_segments(wp_handle* h, const int32_t* ids, const int32_t* offs, int
       pb = h->slots[si].b;
     }
     if (si >= 0) h->slots[si].last_use = h->generation;
+    auto mit = map_of.find(pa);
+    if (mit == map_of.end()) {
+      CUtensorMap m;
+      if (!encode_a_map(&m, ad.dtype, pa, ad.d, ad.r, 1, static_cast<int64_t>(ad.r) * ad.d))
+        return fail(h, WP_ERR_CUDA, "build_segments: cuTensorMapEncodeTiled failed for adapter %d", ids[i]);
+      mit = map_of.emplace(pa, static_cast<int>(maps.size())).first;
+      maps.push_back(m);
+    }
     for (int p = 0; p < count; p += wp::kSegTokens) {
       DevSeg s;
       s.adapter_id = ids[i];
       s.token_start = start + p;
       s.token_count = std::min(wp::kSegTokens, count - p);
       s.alpha = ad.alpha;
-      s.a = pa;
+      s.a = h->d_reg_maps + mit->second;  // the kernel reads A through this descriptor
       s.b = pb;
       pieces.push_back(s);
     }
@@ -553,6 +600,11 @@ int wp_build_segments(wp_handle* h, const int32_t* ids, const int32_t* offs, int
   int* cnt = reinterpret_cast<int*>(h->h_reg_stage + h->cfg.max_tokens);
   *cnt = np;
   if (np) WP_CUDA(h, cudaMemcpyAsync(h->d_reg, h->h_reg_stage, sizeof(DevSeg) * np, cudaMemcpyHostToDevice, stream));
+  if (!maps.empty()) {
+    std::memcpy(h->h_reg_maps, maps.data(), sizeof(CUtensorMap) * maps.size());
+    WP_CUDA(h, cudaMemcpyAsync(h->d_reg_maps, h->h_reg_maps, sizeof(CUtensorMap) * maps.size(),
+                               cudaMemcpyHostToDevice, stream));
+  }
   WP_CUDA(h, cudaMemcpyAsync(h->d_reg_num, cnt, sizeof(int), cudaMemcpyHostToDevice, stream));
   WP_CUDA(h, cudaEventRecord(h->reg_uploaded, stream));
   h->reg_table.swap(table);
@@ -603,58 +655,95 @@ int wp_read_seg_table(wp_handle* h, int32_t which, wp_segment* out, int32_t cap,
 
 // ---- apply -------------------------------------------------------------------
 
-static int do_shrink(wp_handle* h, const void* x, int64_t x_ld, float* H, const DevSeg* segs, const int* nseg,
-                     const void* wa, int64_t wa_stride, float scale, int registry, int T, int d, int r, int dtype,
-                     cudaStream_t stream) {
-  wp::ShrinkArgs a{};
-  a.x = x;
-  a.x_ld = x_ld;
-  a.h = H;
-  a.partial = h->d_partial;
-  a.counters = h->d_counters;
+}  // extern "C"
+
+namespace {
+
+// Cluster size and persistent grid of the apply kernel for (dtype, rank):
+// the largest cluster whose co-resident grid keeps at least 95% of the CTAs
+// that the best cluster size achieves (cached per handle).
+void apply_plan(wp_handle* h, int dtype, int r, int* cluster, int* grid) {
+  const int key = (dtype == WP_DTYPE_BF16 ? 4 : 0) + (r == 8 ? 0 : r == 16 ? 1 : r == 32 ? 2 : 3);
+  if (h->plan_grid[key] == 0) {
+    const int sizes[4] = {8, 4, 2, 1};
+    int g[4], best = 0;
+    for (int i = 0; i < 4; ++i) {
+      g[i] = wp::apply_max_grid(dtype, r, sizes[i]);
+      if (h->cfg.ctas_per_sm > 0) g[i] = std::min(g[i], h->num_sms * h->cfg.ctas_per_sm / sizes[i] * sizes[i]);
+      best = std::max(best, g[i]);
+    }
+    int pick = 3;
+    for (int i = 0; i < 4; ++i)
+      if (g[i] > 0 && g[i] * 100 >= best * 95) {
+        pick = i;
+        break;
+      }
+    h->plan_cluster[key] = sizes[pick];
+    h->plan_grid[key] = std::max(g[pick], sizes[pick]);
+  }
+  *cluster = h->plan_cluster[key];
+  *grid = h->plan_grid[key];
+}
+
+int round_up(int v, int m) { return (v + m - 1) / m * m; }
+
+// One apply launch. mode: wp::kModeShrink / kModeExpand / kModeFused.
+int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int* nseg, int T, int r, int dtype,
+             const void* x, int64_t x_ld, int d, const void* wa, int64_t wa_stride, int64_t num_adapters, float scale,
+             void* y, int64_t y_ld, int y_off, int o, const void* wb, int64_t wb_stride, float* H,
+             cudaStream_t stream) {
+  if (T == 0) return WP_OK;  // no rows: nothing to launch
+  wp::ApplyArgs a{};
   a.segs = segs;
   a.num_segs = nseg;
-  a.wa_base = wa;
-  a.wa_stride = wa_stride;
-  a.scale = scale;
+  a.h = H;
+  a.mode = mode;
   a.registry = registry;
-  a.d = d;
-  shrink_plan(h, d, T, r, &a.nsplit, &a.split_len);
-  a.cap_t = h->cfg.max_tokens;
+  a.scale = scale;
   a.err = h->d_err;
-  wp::LaunchCfg lc{grid_size(h), stream, h->cfg.use_pdl != 0 && !h->last_was_segmenter};
-  cudaError_t e = wp::launch_shrink(dtype, r, a, lc);
-  if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "shrink launch: %s", cudaGetErrorString(e));
+  a.trace = h->trace_on ? h->d_trace[mode == wp::kModeExpand ? 1 : 0] : nullptr;
+  if (mode & wp::kModeShrink) {
+    a.d = d;
+    for (int i = 0; i < 3; ++i)
+      if (!encode_rows_map(&a.tmap_x[i], dtype, x, d, T, x_ld, 8 << i))
+        return fail(h, WP_ERR_CUDA, "apply: cuTensorMapEncodeTiled(x) failed");
+    if (!registry && !encode_a_map(&a.tmap_a, dtype, wa, d, r, std::max<int64_t>(1, num_adapters), wa_stride))
+      return fail(h, WP_ERR_CUDA, "apply: cuTensorMapEncodeTiled(wa_t_all) failed");
+  }
+  if (mode & wp::kModeExpand) {
+    a.y = y;
+    a.y_ld = y_ld;
+    a.y_off = y_off;
+    a.o = o;
+    a.wb_base = wb;
+    a.wb_stride = wb_stride;
+    a.y_tma = al16(y) && (y_ld % 8 == 0) && (y_off % 8 == 0);
+    for (int i = 0; a.y_tma && i < 3; ++i)
+      if (!encode_rows_map(&a.tmap_y[i], dtype, static_cast<const char*>(y) + static_cast<int64_t>(y_off) * 2, o, T,
+                           y_ld, 8 << i))
+        return fail(h, WP_ERR_CUDA, "apply: cuTensorMapEncodeTiled(y) failed");
+  }
+  int cluster = 1, grid = 1;
+  apply_plan(h, dtype, r, &cluster, &grid);
+  a.split_len = round_up((std::max(d, 1) + cluster - 1) / cluster, wp::kStageK);
+  a.oslice = round_up((std::max(o, 1) + cluster - 1) / cluster, wp::kStageCols);
+  const bool pdl = h->cfg.use_pdl != 0;
+  // Without PDL the kernel starts after its predecessor completed, so the
+  // table and weights can always be read first. With PDL that needs the
+  // caller's promise (prefetch_weights) that the preceding kernel writes no
+  // adapter weights, and a preceding kernel that is not the segmenter.
+  a.prefetch_weights = !pdl || (h->cfg.prefetch_weights != 0 && !h->last_was_segmenter);
+  wp::LaunchCfg lc{grid, cluster, stream, pdl};
+  cudaError_t e = wp::launch_apply(dtype, r, a, lc);
+  if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "apply launch: %s", cudaGetErrorString(e));
   ++h->launches;
   h->last_was_segmenter = false;
   return WP_OK;
 }
 
-static int do_expand(wp_handle* h, void* y, int64_t y_ld, int y_off, const float* H, const DevSeg* segs,
-                     const int* nseg, const void* wb, int64_t wb_stride, int registry, int o, int r, int dtype,
-                     cudaStream_t stream) {
-  wp::ExpandArgs a{};
-  a.h = H;
-  a.y = y;
-  a.y_ld = y_ld;
-  a.y_off = y_off;
-  a.segs = segs;
-  a.num_segs = nseg;
-  a.wb_base = wb;
-  a.wb_stride = wb_stride;
-  a.registry = registry;
-  a.o = o;
-  const int W = wp::expand_chunk_cols(r);
-  a.n_ochunks = (o + W - 1) / W;
-  a.y_bulk = al16(y) && (y_ld % 8 == 0) && (y_off % 8 == 0);
-  a.err = h->d_err;
-  wp::LaunchCfg lc{grid_size(h), stream, h->cfg.use_pdl != 0 && !h->last_was_segmenter};
-  cudaError_t e = wp::launch_expand(dtype, r, a, lc);
-  if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "expand launch: %s", cudaGetErrorString(e));
-  ++h->launches;
-  h->last_was_segmenter = false;
-  return WP_OK;
-}
+}  // namespace
+
+extern "C" {
 
 int wp_shrink(wp_handle* h, const void* X, void* H, int32_t d_model, int32_t rank, int32_t T, int32_t dtype,
               void* stream_v) {
@@ -678,8 +767,8 @@ int wp_shrink(wp_handle* h, const void* X, void* H, int32_t d_model, int32_t ran
   }
   DeviceGuard dg(h->device);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
-  int rc = do_shrink(h, X, d_model, static_cast<float*>(H), h->d_reg, h->d_reg_num, nullptr, 0, 0.f, 1, T,
-                     d_model, rank, dtype, stream);
+  int rc = do_apply(h, wp::kModeShrink, 1, h->d_reg, h->d_reg_num, T, rank, dtype, X, d_model, d_model, nullptr, 0,
+                    0, 0.f, nullptr, 0, 0, 0, nullptr, 0, static_cast<float*>(H), stream);
   if (rc) return rc;
   cudaEventRecord(h->registry_done, stream);
   h->registry_used = true;
@@ -706,8 +795,9 @@ int wp_expand(wp_handle* h, const void* H, void* Y, int32_t out_features, int32_
   }
   DeviceGuard dg(h->device);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
-  int rc = do_expand(h, Y, out_features, 0, static_cast<const float*>(H), h->d_reg, h->d_reg_num, nullptr, 0, 1,
-                     out_features, rank, dtype, stream);
+  int rc = do_apply(h, wp::kModeExpand, 1, h->d_reg, h->d_reg_num, T, rank, dtype, nullptr, 0, 0, nullptr, 0, 0, 0.f,
+                    Y, out_features, 0, out_features, nullptr, 0, const_cast<float*>(static_cast<const float*>(H)),
+                    stream);
   if (rc) return rc;
   cudaEventRecord(h->registry_done, stream);
   h->registry_used = true;
@@ -721,17 +811,39 @@ static int check_live(wp_handle* h, int32_t T, int32_t rank, int32_t dtype) {
   return WP_OK;
 }
 
-int wp_add_lora_shrink(wp_handle* h, void* H, const void* x, const void* wa_base, int64_t wa_stride0, float scale,
-                       int32_t T, int32_t d_model, int32_t rank, int64_t x_ld, int32_t dtype, void* stream_v) {
+static int check_shrink_args(wp_handle* h, const void* x, int64_t x_ld, int32_t d_model, const void* wa_base,
+                             int64_t wa_stride0, int32_t num_adapters) {
+  if (d_model <= 0 || d_model % 8) return fail(h, WP_ERR_INVALID, "add_lora: d_model must be a positive multiple of 8");
+  if (num_adapters < 1) return fail(h, WP_ERR_INVALID, "add_lora: num_adapters must be >= 1");
+  if (!al16(x) || !al16(wa_base) || x_ld % 8 || x_ld < d_model || wa_stride0 % 8)
+    return fail(h, WP_ERR_INVALID, "add_lora: x and wa_t_all need 16-byte aligned rows");
+  return WP_OK;
+}
+
+static int check_expand_args(wp_handle* h, const void* y, int64_t y_ld, int32_t y_offset, int32_t out_features,
+                             const void* wb_base, int64_t wb_stride0) {
+  if (out_features <= 0 || out_features % 8)
+    return fail(h, WP_ERR_INVALID, "add_lora: out_features must be a positive multiple of 8");
+  if (y_offset < 0 || y_ld < y_offset + out_features)
+    return fail(h, WP_ERR_INVALID, "add_lora: y slice [%d, %d) exceeds the row length %lld", y_offset,
+                y_offset + out_features, static_cast<long long>(y_ld));
+  if (!al16(wb_base) || wb_stride0 % 8 || (reinterpret_cast<uintptr_t>(y) & 1))
+    return fail(h, WP_ERR_INVALID, "add_lora: wb_t_all needs 16-byte alignment and y 2-byte alignment");
+  return WP_OK;
+}
+
+int wp_add_lora_shrink(wp_handle* h, void* H, const void* x, const void* wa_base, int64_t wa_stride0,
+                       int32_t num_adapters, float scale, int32_t T, int32_t d_model, int32_t rank, int64_t x_ld,
+                       int32_t dtype, void* stream_v) {
   if (!h) return fail(nullptr, WP_ERR_INVALID, "add_lora_shrink: NULL handle");
   int rc = check_live(h, T, rank, dtype);
+  if (!rc) rc = check_shrink_args(h, x, x_ld, d_model, wa_base, wa_stride0, num_adapters);
   if (rc) return rc;
-  if (d_model <= 0 || d_model % 8) return fail(h, WP_ERR_INVALID, "add_lora: d_model must be a positive multiple of 8");
-  if (!al16(x) || !al16(wa_base) || !al16(H) || x_ld % 8 || wa_stride0 % 8)
-    return fail(h, WP_ERR_INVALID, "add_lora: x, wa_t_all and H need 16-byte aligned rows");
+  if (!al16(H)) return fail(h, WP_ERR_INVALID, "add_lora_shrink: H must be 16-byte aligned");
   DeviceGuard dg(h->device);
-  return do_shrink(h, x, x_ld, static_cast<float*>(H), h->d_live, h->d_live_num, wa_base, wa_stride0, scale, 0, T,
-                   d_model, rank, dtype, static_cast<cudaStream_t>(stream_v));
+  return do_apply(h, wp::kModeShrink, 0, h->d_live, h->d_live_num, T, rank, dtype, x, x_ld, d_model, wa_base,
+                  wa_stride0, num_adapters, scale, nullptr, 0, 0, 0, nullptr, 0, static_cast<float*>(H),
+                  static_cast<cudaStream_t>(stream_v));
 }
 
 int wp_add_lora_expand(wp_handle* h, void* y, const void* H, const void* wb_base, int64_t wb_stride0, int32_t T,
@@ -739,32 +851,70 @@ int wp_add_lora_expand(wp_handle* h, void* y, const void* H, const void* wb_base
                        void* stream_v) {
   if (!h) return fail(nullptr, WP_ERR_INVALID, "add_lora_expand: NULL handle");
   int rc = check_live(h, T, rank, dtype);
+  if (!rc) rc = check_expand_args(h, y, y_ld, y_offset, out_features, wb_base, wb_stride0);
   if (rc) return rc;
-  if (out_features <= 0 || out_features % 8)
-    return fail(h, WP_ERR_INVALID, "add_lora: out_features must be a positive multiple of 8");
-  if (y_offset < 0 || y_ld < y_offset + out_features)
-    return fail(h, WP_ERR_INVALID, "add_lora: y slice [%d, %d) exceeds the row length %lld", y_offset,
-                y_offset + out_features, static_cast<long long>(y_ld));
-  if (!al16(wb_base) || !al16(H) || wb_stride0 % 8 || (reinterpret_cast<uintptr_t>(y) & 1))
-    return fail(h, WP_ERR_INVALID, "add_lora: wb_t_all and H need 16-byte alignment");
+  if (!al16(H)) return fail(h, WP_ERR_INVALID, "add_lora_expand: H must be 16-byte aligned");
   DeviceGuard dg(h->device);
-  return do_expand(h, y, y_ld, y_offset, static_cast<const float*>(H), h->d_live, h->d_live_num, wb_base,
-                   wb_stride0, 0, out_features, rank, dtype, static_cast<cudaStream_t>(stream_v));
+  return do_apply(h, wp::kModeExpand, 0, h->d_live, h->d_live_num, T, rank, dtype, nullptr, 0, 0, nullptr, 0, 0, 0.f, y,
+                  y_ld, y_offset, out_features, wb_base, wb_stride0, const_cast<float*>(static_cast<const float*>(H)),
+                  static_cast<cudaStream_t>(stream_v));
+}
+
+int wp_add_lora(wp_handle* h, void* y, const void* x, const void* wa_base, int64_t wa_stride0, const void* wb_base,
+                int64_t wb_stride0, int32_t num_adapters, float scale, int32_t T, int32_t d_model,
+                int32_t out_features, int32_t rank, int64_t x_ld, int64_t y_ld, int32_t y_offset, int32_t dtype,
+                void* stream_v) {
+  if (!h) return fail(nullptr, WP_ERR_INVALID, "add_lora: NULL handle");
+  int rc = check_live(h, T, rank, dtype);
+  if (!rc) rc = check_shrink_args(h, x, x_ld, d_model, wa_base, wa_stride0, num_adapters);
+  if (!rc) rc = check_expand_args(h, y, y_ld, y_offset, out_features, wb_base, wb_stride0);
+  if (rc) return rc;
+  DeviceGuard dg(h->device);
+  return do_apply(h, wp::kModeFused, 0, h->d_live, h->d_live_num, T, rank, dtype, x, x_ld, d_model, wa_base,
+                  wa_stride0, num_adapters, scale, y, y_ld, y_offset, out_features, wb_base, wb_stride0, nullptr,
+                  static_cast<cudaStream_t>(stream_v));
+}
+
+// ---- tracing -------------------------------------------------------------------
+
+int wp_trace_enable(wp_handle* h, int32_t enable) {
+  if (!h) return fail(nullptr, WP_ERR_INVALID, "trace_enable: NULL handle");
+  DeviceGuard dg(h->device);
+  if (enable && !h->d_trace[0]) {
+    const size_t n = static_cast<size_t>(grid_size(h)) * wp::kTraceSlots;
+    for (int k = 0; k < 2; ++k) {
+      WP_CUDA(h, cudaMalloc(&h->d_trace[k], n * sizeof(unsigned long long)));
+      WP_CUDA(h, cudaMemset(h->d_trace[k], 0, n * sizeof(unsigned long long)));
+    }
+  }
+  h->trace_on = enable != 0;
+  return WP_OK;
+}
+
+int wp_trace_read(wp_handle* h, int32_t kernel, uint64_t* out, int32_t cap, int32_t* n) {
+  if (!h) return fail(nullptr, WP_ERR_INVALID, "trace_read: NULL handle");
+  if (kernel < 0 || kernel > 1 || !h->d_trace[kernel]) return fail(h, WP_ERR_INVALID, "trace_read: tracing is off");
+  DeviceGuard dg(h->device);
+  const int total = grid_size(h) * wp::kTraceSlots;
+  if (n) *n = total;
+  WP_CUDA(h, cudaDeviceSynchronize());
+  if (out && cap > 0)
+    WP_CUDA(h, cudaMemcpy(out, h->d_trace[kernel], sizeof(uint64_t) * std::min(cap, total), cudaMemcpyDeviceToHost));
+  return WP_OK;
+}
+
+int wp_apply_plan(wp_handle* h, int32_t dtype, int32_t rank, int32_t* cluster, int32_t* grid) {
+  if (!h) return fail(nullptr, WP_ERR_INVALID, "apply_plan: NULL handle");
+  if (!rank_ok(rank) || !dtype16(dtype)) return fail(h, WP_ERR_INVALID, "apply_plan: bad rank or dtype");
+  DeviceGuard dg(h->device);
+  int c = 0, g = 0;
+  apply_plan(h, dtype, rank, &c, &g);
+  if (cluster) *cluster = c;
+  if (grid) *grid = g;
+  return WP_OK;
 }
 
 }  // extern "C"
-
-extern "C" int wp_add_lora(wp_handle* h, void* y, const void* x, const void* wa_base, int64_t wa_stride0,
-                           const void* wb_base, int64_t wb_stride0, float scale, int32_t T, int32_t d_model,
-                           int32_t out_features, int32_t rank, int64_t x_ld, int64_t y_ld, int32_t y_offset,
-                           int32_t dtype, void* stream_v) {
-  if (!h) return fail(nullptr, WP_ERR_INVALID, "add_lora: NULL handle");
-  DeviceGuard dg(h->device);
-  float* H = h->d_live_h;
-  int rc = wp_add_lora_shrink(h, H, x, wa_base, wa_stride0, scale, T, d_model, rank, x_ld, dtype, stream_v);
-  if (rc) return rc;
-  return wp_add_lora_expand(h, y, H, wb_base, wb_stride0, T, out_features, rank, y_ld, y_offset, dtype, stream_v);
-}
 
 // ---- tensor parallel ---------------------------------------------------------
 

@@ -56,12 +56,13 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
 
 // Waits for phase `parity` of `bar` to complete, for at most kWaitTimeoutNs.
 // Returns false (and raises kErrWaitTimeout in *err) when the bound is hit.
-__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err) {
+__device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
+                                                  unsigned long long timeout_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   while (true) {
     if (mbar_try_wait(bar, parity)) return true;
-    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+    if (global_timer_ns() - t0 > timeout_ns) {
       if (err) atomicOr(err, kErrWaitTimeout);
       return false;
     }
@@ -94,6 +95,140 @@ __device__ __forceinline__ uint64_t l2_policy_evict_first() {
   uint64_t p;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
   return p;
+}
+
+// ---- TMA tiled tensor loads (cp.async.bulk.tensor) -------------------------
+// `tmap` is the generic address of a CUtensorMap in param (__grid_constant__)
+// or global memory. The innermost coordinate c0 times the element size must
+// be a multiple of 16 bytes. Out-of-range elements are zero-filled and still
+// count toward the transaction bytes.
+
+__device__ __forceinline__ void tma_load_2d(void* dst_smem, const void* tmap, int c0, int c1, uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.2d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3}], "
+      "[%4];" ::"r"(smem_u32(dst_smem)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(smem_u32(bar))
+      : "memory");
+}
+
+__device__ __forceinline__ void tma_load_3d(void* dst_smem, const void* tmap, int c0, int c1, int c2,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4}], "
+      "[%5];" ::"r"(smem_u32(dst_smem)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Pulls a tensor map into the TMA descriptor cache ahead of its first use.
+__device__ __forceinline__ void prefetch_tmap(const void* tmap) {
+  asm volatile("prefetch.tensormap [%0];" ::"l"(tmap) : "memory");
+}
+
+// Byte offset of 16-bit element (row, col) inside a 128B-swizzled box of
+// 64-element rows (the layout CU_TENSOR_MAP_SWIZZLE_128B writes): the 16-byte
+// chunk index is XORed with (row & 7).
+__device__ __forceinline__ uint32_t sw128(int row, int col) {
+  return static_cast<uint32_t>(row * 128 + ((((col >> 3) ^ row) & 7) << 4) + ((col & 7) << 1));
+}
+
+// ---- named barriers (a subset of the CTA's warps) --------------------------
+
+__device__ __forceinline__ void named_sync(int id, int nthreads) {
+  asm volatile("bar.sync %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+
+// ---- thread-block clusters and distributed shared memory -----------------
+
+__device__ __forceinline__ uint32_t cluster_ctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_ctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_nctarank() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%cluster_nctarank;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_id_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%clusterid.x;" : "=r"(r));
+  return r;
+}
+__device__ __forceinline__ uint32_t cluster_count_x() {
+  uint32_t r;
+  asm volatile("mov.u32 %0, %%nclusterid.x;" : "=r"(r));
+  return r;
+}
+
+// Hardware cluster barrier (all threads of every CTA of the cluster).
+__device__ __forceinline__ void cluster_sync_hw() {
+  asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
+}
+
+// shared::cluster address of the variable at `local` in CTA `rank` of the cluster.
+__device__ __forceinline__ uint32_t mapa(uint32_t local, uint32_t rank) {
+  uint32_t r;
+  asm volatile("mapa.shared::cluster.u32 %0, %1, %2;" : "=r"(r) : "r"(local), "r"(rank));
+  return r;
+}
+
+__device__ __forceinline__ float2 ld_dsmem_f2(uint32_t addr) {
+  float2 v;
+  asm volatile("ld.shared::cluster.v2.f32 {%0, %1}, [%2];" : "=f"(v.x), "=f"(v.y) : "r"(addr) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_dsmem_f2(uint32_t addr, float2 v) {
+  asm volatile("st.shared::cluster.v2.f32 [%0], {%1, %2};" ::"r"(addr), "f"(v.x), "f"(v.y) : "memory");
+}
+
+__device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
+__device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity)
+      : "memory");
+  return ok != 0;
+}
+
+// Bounded cluster-wide barrier among the `nthreads` compute threads (named
+// barrier `bar_id`) of every CTA of the cluster, built on an mbarrier with
+// count = cluster size in every CTA: after the CTA-local barrier, thread 0
+// arrives (release, cluster scope) on the barrier of every CTA; every thread
+// then waits (acquire, cluster scope) for its own barrier's phase. Shared-
+// memory writes made before the call by any compute thread of any CTA are
+// visible to every compute thread after it. Gives up after kWaitTimeoutNs
+// (raising kErrWaitTimeout) instead of hanging; returns false then.
+__device__ __forceinline__ bool cluster_barrier_bounded(uint64_t* bar, uint32_t parity, uint32_t ncta, int bar_id,
+                                                        int nthreads, int* err) {
+  named_sync(bar_id, nthreads);
+  if (threadIdx.x == 0) {
+    asm volatile("fence.acq_rel.cluster;" ::: "memory");
+    const uint32_t local = smem_u32(bar);
+    for (uint32_t r = 0; r < ncta; ++r) mbar_arrive_remote(mapa(local, r));
+  }
+  bool ok = mbar_try_wait_cluster(bar, parity);
+  if (!ok) {
+    const unsigned long long t0 = global_timer_ns();
+    while (!(ok = mbar_try_wait_cluster(bar, parity))) {
+      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        if (err) atomicOr(err, kErrWaitTimeout);
+        break;
+      }
+    }
+  }
+  return ok;
 }
 
 // ---- programmatic dependent launch ----------------------------------------

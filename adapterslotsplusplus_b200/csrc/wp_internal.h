@@ -2,6 +2,7 @@
 // its kernels. Not part of the public C ABI (include/wp_api.h).
 #pragma once
 
+#include <cuda.h>
 #include <cuda_runtime.h>
 #include <stdint.h>
 
@@ -15,9 +16,10 @@ constexpr int kSegTokens = 32;
 
 // One entry of a device segment table (32 bytes).
 //   live table (build_seg_bounds): adapter_id/token_start/token_count only; the
-//     apply kernels resolve weights as base + adapter_id * stride.
-//   registry table (build_segments): a/b/alpha carry the resolved weight
-//     pointers (original tensors or a staging slot) and the adapter's scale.
+//     apply kernel resolves weights as base + adapter_id * stride.
+//   registry table (build_segments): `a` is the device address of a TMA
+//     descriptor of the adapter's A [r, d], `b` the address of its B [o, r]
+//     (original tensor or staging slot), alpha the adapter's scale.
 struct DevSeg {
   int32_t adapter_id;
   int32_t token_start;
@@ -28,54 +30,64 @@ struct DevSeg {
 };
 static_assert(sizeof(DevSeg) == 32, "DevSeg is 32 bytes");
 
-struct ShrinkArgs {
-  const void* x;  // [T, d] rows of x_ld elements
-  int64_t x_ld;
-  float* h;  // [T, R] fp32 output (ld = R)
-  float* partial;  // [nsplit][cap_t][R] split-K partials
-  uint32_t* counters;  // per-segment arrival counters (zero between calls)
+// Columns of one TMA box (128 bytes of 16-bit elements).
+constexpr int kBoxCols = 64;
+// K elements per shrink stage and output columns per expand stage (4 boxes).
+constexpr int kStageK = 256;
+constexpr int kStageCols = 256;
+
+// Which halves of the apply one launch runs.
+enum : int { kModeShrink = 1, kModeExpand = 2, kModeFused = 3 };
+
+// Arguments of one apply launch. Tensor maps (TMA descriptors, 64-byte
+// aligned) come first; index i of tmap_x / tmap_y is the map whose box is
+// (8 << i) rows high (8, 16, 32), so a segment loads only the rows it needs.
+struct ApplyArgs {
+  CUtensorMap tmap_x[3];  // x [T, d]: boxes of 64 columns, 128B swizzle
+  CUtensorMap tmap_y[3];  // y columns [y_off, y_off + o) x T rows, 128B swizzle
+  CUtensorMap tmap_a;  // live mode: A stack [L, r, d], box 64 x r x 1
   const DevSeg* segs;
   const int* num_segs;
-  const void* wa_base;  // live mode: A_i = wa_base + i * wa_stride
-  int64_t wa_stride;
-  float scale;
-  int registry;  // 1: weights and alpha from the table entries
-  int d;
-  int nsplit;
-  int split_len;  // elements of d per split (multiple of 8)
-  int cap_t;  // row capacity of one partial plane
-  int* err;
-};
-
-struct ExpandArgs {
-  const float* h;  // [T, R] fp32
+  float* h;  // shrink-only: H [T, r] fp32 written; expand-only: read
   void* y;  // [T, y_ld]; columns y_off .. y_off+o are updated
   int64_t y_ld;
   int y_off;
-  const DevSeg* segs;
-  const int* num_segs;
-  const void* wb_base;  // live mode: B_i = wb_base + i * wb_stride
+  const void* wb_base;  // live mode: B_i = wb_base + i * wb_stride ([o, r] row-major)
   int64_t wb_stride;
-  int registry;
+  float scale;  // live mode alpha
+  int mode;  // kModeShrink | kModeExpand
+  int registry;  // 1: A through DevSeg.a, B from DevSeg.b, alpha from DevSeg.alpha
+  int d;
   int o;
-  int n_ochunks;
-  int y_bulk;  // 1: y rows can be bulk-copied (16-byte aligned rows and offset)
+  int split_len;  // d elements per cluster rank (multiple of kStageK)
+  int oslice;  // o columns per cluster rank (multiple of kStageCols)
+  int y_tma;  // 1: tmap_y is valid; else y is read and written directly
+  int prefetch_weights;  // 1: table and weight loads may start before the dependency wait
   int* err;
+  unsigned long long* trace;  // optional per-CTA phase timestamps (kTraceSlots per CTA), else null
 };
+
+// Per-CTA trace record (globaltimer ns): start, after the dependency wait,
+// first stage ready, end, stages consumed, ns consumers spent waiting for
+// stages, ns the producer spent waiting for free stages, 0; then, for the
+// first kTraceUnits stages, 4 timestamps each: before the stage wait, after
+// it, after the compute, after the stage was handed back.
+constexpr int kTraceUnits = 16;
+constexpr int kTraceSlots = 8 + 4 * kTraceUnits;
 
 struct LaunchCfg {
   int grid;
+  int cluster;
   cudaStream_t stream;
   bool pdl;
 };
 
-// dtype: 0 = f16, 1 = bf16 (WP_DTYPE_*). Return a cudaError_t.
-cudaError_t launch_shrink(int dtype, int rank, const ShrinkArgs& a, const LaunchCfg& lc);
-cudaError_t launch_expand(int dtype, int rank, const ExpandArgs& a, const LaunchCfg& lc);
-// Column chunk width of one expand work item.
-int expand_chunk_cols(int rank);
-// K elements per pipeline stage of the shrink kernel.
-int shrink_chunk_k(int rank);
+// dtype: 0 = f16, 1 = bf16 (WP_DTYPE_*). Launches the clustered apply kernel
+// on `lc.grid` CTAs in clusters of `lc.cluster`. Returns a cudaError_t.
+cudaError_t launch_apply(int dtype, int rank, const ApplyArgs& a, const LaunchCfg& lc);
+// Largest co-resident persistent grid for the apply kernel of (dtype, rank)
+// with clusters of `cluster` CTAs (0 if that cluster size cannot be scheduled).
+int apply_max_grid(int dtype, int rank, int cluster);
 
 // idx_dtype: WP_DTYPE_I32 or WP_DTYPE_I64.
 cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs,

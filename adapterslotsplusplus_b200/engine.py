@@ -59,6 +59,7 @@ class WarpPipeEngine:
             slot_bytes=int(self.config.slot_bytes),
             ctas_per_sm=int(self.config.ctas_per_sm),
             use_pdl=1 if self.config.use_pdl else 0,
+            prefetch_weights=1 if self.config.prefetch_weights else 0,
         )
         handle = ctypes.c_void_p()
         _lib.check(self._lib.wp_create(ctypes.byref(cfg), ctypes.byref(handle)), None)
@@ -201,8 +202,27 @@ class WarpPipeEngine:
             raise RuntimeError("add_lora_packed: y.size(-1) must equal wb_t_all.size(-2)")
         self._check(self._lib.wp_add_lora(
             self._h, y2d.data_ptr(), x2d.data_ptr(), wa_t_all.data_ptr(), int(wa_t_all.stride(0)),
-            wb_t_all.data_ptr(), int(wb_t_all.stride(0)), float(scale), T, d_model, out_features, rank,
+            wb_t_all.data_ptr(), int(wb_t_all.stride(0)), int(wa_t_all.size(0)), float(scale), T, d_model,
+            out_features, rank,
             int(x2d.stride(0)), int(y2d.stride(0)), off, dt, _stream_ptr(x.device)))
+        return True
+
+    def add_lora_strided(self, y_view, x, wa_t_all, wb_t_all, scale) -> bool:
+        """add_lora onto a column view of a wider row-major y (e.g. a
+        tensor-parallel output shard): the view's row stride is used as is."""
+        base = y_view
+        if y_view.stride(-1) != 1:
+            raise RuntimeError("add_lora_strided: the view's columns must be contiguous")
+        rank = int(wb_t_all.size(-1))
+        if not self.rank_supported(rank):
+            return False
+        dt = _dtype_code(x, "add_lora: x/y")
+        x2d = x.reshape(-1, x.size(-1))
+        self._check(self._lib.wp_add_lora(
+            self._h, base.data_ptr(), x2d.data_ptr(), wa_t_all.data_ptr(), int(wa_t_all.stride(0)),
+            wb_t_all.data_ptr(), int(wb_t_all.stride(0)), int(wa_t_all.size(0)), float(scale), int(x2d.size(0)),
+            int(x2d.size(1)), int(wb_t_all.size(-2)), rank, int(x2d.stride(0)), int(base.stride(0)), 0, dt,
+            _stream_ptr(x.device)))
         return True
 
     # -- staging slots (engine.py:44-54) -----------------------------------------
@@ -238,6 +258,12 @@ class WarpPipeEngine:
         flag = ctypes.c_int32()
         self._check(self._lib.wp_device_error(self._h, 1 if clear else 0, ctypes.byref(flag)))
         return flag.value
+
+    def apply_plan(self, dtype=torch.bfloat16, rank: int = 32) -> Tuple[int, int]:
+        """(cluster size, CTAs) of the apply kernel for this dtype and rank."""
+        c, g = ctypes.c_int32(), ctypes.c_int32()
+        self._check(self._lib.wp_apply_plan(self._h, _DTYPES[dtype], int(rank), ctypes.byref(c), ctypes.byref(g)))
+        return c.value, g.value
 
     def kernel_launches(self) -> int:
         return int(self._lib.wp_kernel_launch_count(self._h))

@@ -1,0 +1,116 @@
+"""Tensor-parallel grouped LoRA apply (one process per GPU, NCCL over NVLink).
+
+The reference is single-GPU; this is the sharding of the apply path for a
+tensor-parallel base model:
+
+  column-parallel layers (q, k, v, gate, up): x and A are replicated, B and
+    the output y are split along out_features. Each rank shrinks the full
+    [T, r] H and expands only its own output columns -- no collective.
+  row-parallel layers (o, down): x and A are split along d_model. Each rank
+    shrinks its slice into a partial fp32 H_p [T, r]; one NCCL all-reduce
+    (sum, fp32, T*r values) over the tensor-parallel group gives H on every
+    rank; each rank then expands with the full B onto its replica of y.
+
+The shrink, all-reduce and expand are three launches on the caller's stream
+(libwp_b200.so: wp_add_lora_shrink, wp_tp_allreduce_f32, wp_add_lora_expand),
+so a whole step can be captured in one CUDA graph.
+
+The sharding helpers are pure tensor slicing and run anywhere; the apply
+methods need the CUDA engine.
+"""
+
+from __future__ import annotations
+
+import ctypes
+from typing import Optional
+
+import torch
+
+from . import _lib
+
+
+def _span(n: int, rank: int, world: int) -> tuple[int, int]:
+    if n % world:
+        raise ValueError(f"dimension {n} does not split over {world} ranks")
+    step = n // world
+    return rank * step, (rank + 1) * step
+
+
+def shard_column(wb_t_all: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """This rank's out_features slice of B ([L, 1, o, r] -> [L, 1, o/world, r]), contiguous."""
+    a, b = _span(wb_t_all.size(-2), rank, world)
+    return wb_t_all[..., a:b, :].contiguous()
+
+
+def shard_column_output(y: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    a, b = _span(y.size(-1), rank, world)
+    return y[..., a:b]
+
+
+def shard_row(wa_t_all: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    """This rank's d_model slice of A ([L, 1, r, d] -> [L, 1, r, d/world]), contiguous."""
+    a, b = _span(wa_t_all.size(-1), rank, world)
+    return wa_t_all[..., a:b].contiguous()
+
+
+def shard_row_input(x: torch.Tensor, rank: int, world: int) -> torch.Tensor:
+    a, b = _span(x.size(-1), rank, world)
+    return x[..., a:b].contiguous()
+
+
+class TensorParallelApply:
+    """Grouped LoRA apply over a tensor-parallel group of `world` GPUs.
+
+    Needs torch.distributed initialised (any backend; it only carries the
+    NCCL unique id) and one WarpPipeEngine on this rank's device. Every rank
+    runs build_seg_bounds on identical indices (the table is replicated, not
+    exchanged)."""
+
+    def __init__(self, engine, rank: Optional[int] = None, world: Optional[int] = None, group=None):
+        import torch.distributed as dist
+
+        self.engine = engine
+        self.rank = dist.get_rank(group) if rank is None else rank
+        self.world = dist.get_world_size(group) if world is None else world
+        lib = _lib.load()
+        self._lib = lib
+        nbytes = int(lib.wp_tp_unique_id_bytes())
+        uid = (ctypes.c_char * nbytes)()
+        if self.rank == 0:
+            _lib.check(lib.wp_tp_get_unique_id(uid), None)
+        obj = [bytes(uid)] if self.rank == 0 else [None]
+        dist.broadcast_object_list(obj, src=0, group=group)
+        uid = (ctypes.c_char * nbytes).from_buffer_copy(obj[0])
+        _lib.check(lib.wp_tp_init(engine.handle, uid, self.rank, self.world), engine.handle)
+        self._H = torch.empty(engine.config.max_tokens * 64, dtype=torch.float32, device=engine.device)
+
+    def close(self):
+        self._lib.wp_tp_destroy(self.engine.handle)
+
+    def column_parallel(self, y_shard, x, wa_t_all, wb_shard, scale) -> bool:
+        """y_shard[t] += (x[t] . A^T * scale) . B_shard^T; no collective.
+        y_shard may be a column slice of a wider y."""
+        full = y_shard
+        if y_shard.stride(0) != y_shard.size(-1):
+            return self.engine.add_lora_strided(y_shard, x, wa_t_all, wb_shard, scale)
+        return self.engine.add_lora_packed(full, x, wa_t_all, wb_shard, scale)
+
+    def row_parallel(self, y, x_shard, wa_shard, wb_t_all, scale) -> bool:
+        """Partial shrink on this rank's d slice, fp32 all-reduce of H, full expand."""
+        eng, lib = self.engine, self._lib
+        r = int(wb_t_all.size(-1))
+        if not eng.rank_supported(r):
+            return False
+        x2d = x_shard.reshape(-1, x_shard.size(-1))
+        y2d = y.view(-1, y.size(-1))
+        T, d = int(x2d.size(0)), int(x2d.size(1))
+        dt = _lib.WP_DTYPE_BF16 if x2d.dtype == torch.bfloat16 else _lib.WP_DTYPE_F16
+        H = self._H[:T * r].view(T, r)
+        stream = torch.cuda.current_stream(eng.device).cuda_stream
+        h = eng.handle
+        _lib.check(lib.wp_add_lora_shrink(h, H.data_ptr(), x2d.data_ptr(), wa_shard.data_ptr(), wa_shard.stride(0),
+                                          int(wa_shard.size(0)), float(scale), T, d, r, x2d.stride(0), dt, stream), h)
+        _lib.check(lib.wp_tp_allreduce_f32(h, H.data_ptr(), T * r, stream), h)
+        _lib.check(lib.wp_add_lora_expand(h, y2d.data_ptr(), H.data_ptr(), wb_t_all.data_ptr(), wb_t_all.stride(0),
+                                          T, int(wb_t_all.size(-2)), r, y2d.stride(0), 0, dt, stream), h)
+        return True

@@ -54,9 +54,10 @@ METRIC = "LoRA apply us/decode-step (HBM GB/s vs peak), 7B x 32 layers, r32, 64 
 
 def algorithmic_bytes(U: int, T: int, d: int, o: int, r: int, elt: int = 2) -> tuple[int, int]:
     """(shrink bytes, expand bytes) of one projection call: each active
-    adapter's weights once, X read, Y read+write, fp32 H written and read."""
-    shrink = U * d * r * elt + T * d * elt + T * r * 4
-    expand = U * o * r * elt + 2 * T * o * elt + T * r * 4
+    adapter's A and B once, x read, y read and written. H stays on chip (the
+    fused kernel reduces it in distributed shared memory)."""
+    shrink = U * d * r * elt + T * d * elt
+    expand = U * o * r * elt + 2 * T * o * elt
     return shrink, expand
 
 
@@ -195,11 +196,15 @@ def time_graph(g, pre, iters):
 
 
 def run_ours(args, rank, world, local_rank):
-    from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine, _lib
+    from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096), device=device)
+    # prefetch_weights: the serving contract (adapter weights are static during
+    # a step) lets each apply launch start streaming weights while the
+    # previous launch finishes.
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    plan = eng.apply_plan(torch.bfloat16, RANK)
     scale = 16.0 / RANK
 
     ids = make_ids(RESIDENT)
@@ -212,26 +217,9 @@ def run_ours(args, rank, world, local_rank):
         for y, x, wa, wb in calls:
             eng.add_lora_packed(y, x, wa, wb, scale)
 
-    # kernel-only graphs: the shrink and expand halves of the same 224 calls
-    lib, h = _lib.load(), eng.handle
-    H = torch.zeros(4096, RANK, dtype=torch.float32, device=device)
-    stream_of = lambda: torch.cuda.current_stream(device).cuda_stream  # noqa: E731
-
-    def shrinks():
-        for y, x, wa, wb in calls:
-            _lib.check(lib.wp_add_lora_shrink(h, H.data_ptr(), x.data_ptr(), wa.data_ptr(), wa.stride(0), scale,
-                                              TOKENS, x.size(1), RANK, x.stride(0), _lib.WP_DTYPE_BF16, stream_of()), h)
-
-    def expands():
-        for y, x, wa, wb in calls:
-            _lib.check(lib.wp_add_lora_expand(h, y.data_ptr(), H.data_ptr(), wb.data_ptr(), wb.stride(0), TOKENS,
-                                               y.size(1), RANK, y.stride(0), 0, _lib.WP_DTYPE_BF16, stream_of()), h)
-
     seg = lambda: eng.build_seg_bounds(idx_dev)  # noqa: E731
     seg()
     g_full = capture(full_step)
-    g_shr = capture(shrinks)
-    g_exp = capture(expands)
 
     for _ in range(args.warmup):
         seg()
@@ -242,14 +230,13 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
 
     with ClockSampler(local_rank) as clk:
-        ms = time_graph(g_full, seg, args.steps)
-        ms_shr = time_graph(g_shr, None, max(3, args.steps))
-        ms_exp = time_graph(g_exp, None, max(3, args.steps))
+        ms = time_graph(g_full, seg, args.steps)  # the step: segmenter + 224 apply launches
+        ms_apply = time_graph(g_full, None, args.steps)  # the 224 apply launches alone
     torch.cuda.synchronize()
     if world > 1:
-        t = torch.tensor([ms, ms_shr, ms_exp], device=device)
+        t = torch.tensor([ms, ms_apply], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, ms_shr, ms_exp = t.tolist()
+        ms, ms_apply = t.tolist()
 
     # e2e through the public API: token ids from pinned host memory, the step,
     # and a read back of one output row, all on the stream, every step.
@@ -281,10 +268,11 @@ def run_ours(args, rank, world, local_rank):
     hbm = peaks.get("hbm_gbs")
     peak_src = "measured" if hbm else "fallback"
     hbm = hbm or 6650.0
-    # dominant kernel: the one with more device time per step
-    dom, dom_ms, dom_b = ("expand", ms_exp, exp_b) if ms_exp >= ms_shr else ("shrink", ms_shr, shr_b)
-    per_launch_ms = dom_ms / (LAYERS * len(PROJS))
-    per_launch_b = dom_b / (LAYERS * len(PROJS))
+    # dominant kernel: apply_kernel (one launch per call; the segmenter is one
+    # launch per step). Per launch: the mean over the 224 calls of the step.
+    dom = "apply_kernel"
+    per_launch_ms = ms_apply / (LAYERS * len(PROJS))
+    per_launch_b = total_b / (LAYERS * len(PROJS))
     achieved = per_launch_b / (per_launch_ms * 1e-3) / 1e9
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
@@ -314,7 +302,8 @@ def run_ours(args, rank, world, local_rank):
         "step_gbs": round(total_b / (ms * 1e-3) / 1e9, 1),
         "step_frac_of_hbm": round(total_b / (ms * 1e-3) / 1e9 / hbm, 4),
         "step_bytes": total_b,
-        "kernels_ms_per_step": {"shrink": round(ms_shr, 4), "expand": round(ms_exp, 4)},
+        "kernels_ms_per_step": {"apply_kernel": round(ms_apply, 4), "segmenter_and_gaps": round(ms - ms_apply, 4)},
+        "apply_plan": {"cluster": plan[0], "ctas": plan[1]},
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
                      "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / hbm, 4),
                      "traffic": traffic, "algorithmic_bytes_per_launch": int(per_launch_b),
@@ -322,10 +311,10 @@ def run_ours(args, rank, world, local_rank):
         "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "us/step", "h2d_bytes_per_step": int(ids.nbytes),
                 "d2h_bytes_per_step": int(out_host.numel() * 2),
                 "path": "WarpPipeEngine.build_seg_bounds + graph of 224 add_lora_packed calls"},
-        "gpu_launches": args.steps * (1 + 2 * LAYERS * len(PROJS)),
+        "gpu_launches": args.steps * (1 + LAYERS * len(PROJS)),
         "clocks": clk.summary(),
     }
-    del g_full, g_shr, g_exp, stack, calls
+    del g_full, stack, calls
     torch.cuda.empty_cache()
     return eng, result
 

@@ -57,8 +57,13 @@ typedef struct wp_config {
   int32_t max_tokens;        /* capacity of the per-step tables (T), e.g. 16384       */
   int32_t num_staging_slots; /* GPU staging slots (reference: WP_MAX_STAGING = 8)     */
   int64_t slot_bytes;        /* bytes per slot for A+B together (0 = 2*64*16384*2)    */
-  int32_t ctas_per_sm;       /* persistent CTAs per SM for the apply kernels (0=auto) */
+  int32_t ctas_per_sm;       /* cap on persistent CTAs per SM of the apply kernel (0=auto) */
   int32_t use_pdl;           /* 1 = programmatic dependent launch between kernels     */
+  int32_t prefetch_weights;  /* 1 = with use_pdl, start loading adapter weights before the
+                                previous kernel on the stream finishes. The caller promises
+                                that the kernel right before an apply call never writes the
+                                adapter weights (true in serving: weights are static during
+                                a step). 0 = strict stream order. */
 } wp_config;
 
 /* One entry of the segment table, as read back by wp_read_seg_table.
@@ -165,7 +170,7 @@ int wp_expand(wp_handle* h, const void* H, void* Y, int32_t out_features, int32_
  * stride y_ld (elements). Graph-capturable: fixed grids, the segment count is
  * read on the device. */
 int wp_add_lora(wp_handle* h, void* y, const void* x, const void* wa_base, int64_t wa_stride0,
-                const void* wb_base, int64_t wb_stride0, float scale, int32_t T, int32_t d_model,
+                const void* wb_base, int64_t wb_stride0, int32_t num_adapters, float scale, int32_t T, int32_t d_model,
                 int32_t out_features, int32_t rank, int64_t x_ld, int64_t y_ld, int32_t y_offset,
                 int32_t dtype, void* stream);
 
@@ -173,8 +178,8 @@ int wp_add_lora(wp_handle* h, void* y, const void* x, const void* wa_base, int64
  * layers: H [T, r] fp32 (device) receives scale * x . A^T for rows inside
  * live segments; other rows are left untouched. */
 int wp_add_lora_shrink(wp_handle* h, void* H, const void* x, const void* wa_base, int64_t wa_stride0,
-                       float scale, int32_t T, int32_t d_model, int32_t rank, int64_t x_ld, int32_t dtype,
-                       void* stream);
+                       int32_t num_adapters, float scale, int32_t T, int32_t d_model, int32_t rank, int64_t x_ld,
+                       int32_t dtype, void* stream);
 
 /* Expand half of wp_add_lora: y[t, y_offset + j] += H[t,:] . B_i[j,:]. */
 int wp_add_lora_expand(wp_handle* h, void* y, const void* H, const void* wb_base, int64_t wb_stride0,
@@ -208,6 +213,20 @@ int wp_release_prefetch(wp_handle* h, int32_t adapter_id);
  * reading it synchronises the device; `clear` resets it). */
 int wp_slot_stats(wp_handle* h, int32_t* num_slots, int32_t* slots_in_use);
 int wp_device_error(wp_handle* h, int32_t clear, int32_t* flag);
+
+/* ---- tracing and launch plan (no counterpart in the reference) --------- */
+
+/* Turns per-CTA phase tracing of the apply kernel on or off. When on, each
+ * launch (kernel 0: fused or shrink-only, kernel 1: expand-only) records, per
+ * CTA, 8 + 4*16 uint64: start, after the dependency wait, first stage ready,
+ * end (globaltimer ns), stages consumed, ns waited for stages, 0, 0, then
+ * (before wait, after wait, after compute, after hand-back) for the first 16
+ * stages. */
+int wp_trace_enable(wp_handle* h, int32_t enable);
+/* Copies the record of the latest launch of `kernel` (synchronises). */
+int wp_trace_read(wp_handle* h, int32_t kernel, uint64_t* out, int32_t cap, int32_t* n);
+/* Cluster size and persistent grid the apply kernel uses for (dtype, rank). */
+int wp_apply_plan(wp_handle* h, int32_t dtype, int32_t rank, int32_t* cluster, int32_t* grid);
 
 /* ---- tensor parallel (no counterpart in the reference) ----------------- */
 
