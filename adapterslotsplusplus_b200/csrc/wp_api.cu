@@ -158,7 +158,8 @@ PFN_cuTensorMapEncodeTiled_v12000 encode_fn() {
 // Tiled map over 16-bit elements with the 128-byte swizzle. dims[0] is the
 // innermost (contiguous) dimension; strides are in bytes for dims 1..rank-1.
 bool encode_map(CUtensorMap* m, int dtype, int rank, const void* base, const uint64_t* dims,
-                const uint64_t* strides, const uint32_t* box) {
+                const uint64_t* strides, const uint32_t* box,
+                CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (!fn) return false;
   cuuint64_t gd[3], gs[2];
@@ -171,7 +172,7 @@ bool encode_map(CUtensorMap* m, int dtype, int rank, const void* base, const uin
   const CUtensorMapDataType dt =
       dtype == WP_DTYPE_BF16 ? CU_TENSOR_MAP_DATA_TYPE_BFLOAT16 : CU_TENSOR_MAP_DATA_TYPE_FLOAT16;
   CUresult r = fn(m, dt, rank, const_cast<void*>(base), gd, gs, bx, es, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                  CU_TENSOR_MAP_SWIZZLE_128B, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+                  swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   return r == CUDA_SUCCESS;
 }
 
@@ -181,6 +182,17 @@ bool encode_a_map(CUtensorMap* m, int dtype, const void* base, int d, int r, int
   const uint64_t strides[2] = {static_cast<uint64_t>(d) * 2, static_cast<uint64_t>(stride0) * 2};
   const uint32_t box[3] = {static_cast<uint32_t>(wp::kBoxCols), static_cast<uint32_t>(r), 1};
   return encode_map(m, dtype, 3, base, dims, strides, box);
+}
+
+// B stack [L, o, r] (row stride r, adapter stride `stride0` elements): box
+// r x 128 x 1 with the swizzle whose span is one 2r-byte row (r >= 16).
+bool encode_b_map(CUtensorMap* m, int dtype, const void* base, int o, int r, int64_t L, int64_t stride0) {
+  const uint64_t dims[3] = {static_cast<uint64_t>(r), static_cast<uint64_t>(o), static_cast<uint64_t>(L)};
+  const uint64_t strides[2] = {static_cast<uint64_t>(r) * 2, static_cast<uint64_t>(stride0) * 2};
+  const uint32_t box[3] = {static_cast<uint32_t>(r), 128, 1};
+  const CUtensorMapSwizzle sw =
+      r == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : (r == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
+  return encode_map(m, dtype, 3, base, dims, strides, box, sw);
 }
 
 // Activation rows [T, cols] with row stride ld elements: box 64 x box_rows.
@@ -572,11 +584,17 @@ int wp_build_segments(wp_handle* h, const int32_t* ids, const int32_t* offs, int
     if (si >= 0) h->slots[si].last_use = h->generation;
     auto mit = map_of.find(pa);
     if (mit == map_of.end()) {
-      CUtensorMap m;
-      if (!encode_a_map(&m, ad.dtype, pa, ad.d, ad.r, 1, static_cast<int64_t>(ad.r) * ad.d))
+      // maps[2k] describes A of the k-th distinct adapter, maps[2k + 1] its B (ranks >= 16)
+      CUtensorMap m[2];
+      std::memset(m, 0, sizeof(m));
+      if (!encode_a_map(&m[0], ad.dtype, pa, ad.d, ad.r, 1, static_cast<int64_t>(ad.r) * ad.d) ||
+          (ad.r >= 16 && !encode_b_map(&m[1], ad.dtype, pb, ad.o, ad.r, 1, static_cast<int64_t>(ad.o) * ad.r)))
         return fail(h, WP_ERR_CUDA, "build_segments: cuTensorMapEncodeTiled failed for adapter %d", ids[i]);
-      mit = map_of.emplace(pa, static_cast<int>(maps.size())).first;
-      maps.push_back(m);
+      if (2 * maps.size() + 2 > static_cast<size_t>(h->cfg.max_tokens))
+        return fail(h, WP_ERR_CAPACITY, "build_segments: too many distinct adapters in one table");
+      mit = map_of.emplace(pa, static_cast<int>(maps.size())).first;  // index of A's map
+      maps.push_back(m[0]);
+      maps.push_back(m[1]);
     }
     for (int p = 0; p < count; p += wp::kSegTokens) {
       DevSeg s;
@@ -585,7 +603,7 @@ int wp_build_segments(wp_handle* h, const int32_t* ids, const int32_t* offs, int
       s.token_count = std::min(wp::kSegTokens, count - p);
       s.alpha = ad.alpha;
       s.a = h->d_reg_maps + mit->second;  // the kernel reads A through this descriptor
-      s.b = pb;
+      s.b = ad.r >= 16 ? static_cast<const void*>(h->d_reg_maps + mit->second + 1) : pb;
       pieces.push_back(s);
     }
   }
@@ -718,6 +736,8 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
     a.wb_base = wb;
     a.wb_stride = wb_stride;
     a.y_tma = al16(y) && (y_ld % 8 == 0) && (y_off % 8 == 0);
+    if (!registry && r >= 16 && !encode_b_map(&a.tmap_b, dtype, wb, o, r, std::max<int64_t>(1, num_adapters), wb_stride))
+      return fail(h, WP_ERR_CUDA, "apply: cuTensorMapEncodeTiled(wb_t_all) failed");
     for (int i = 0; a.y_tma && i < 3; ++i)
       if (!encode_rows_map(&a.tmap_y[i], dtype, static_cast<const char*>(y) + static_cast<int64_t>(y_off) * 2, o, T,
                            y_ld, 8 << i))

@@ -13,7 +13,7 @@
 // segments c, c + G, c + 2G, ... of the device-resident table. For one segment
 // the CL CTAs of the cluster
 //   1. split d in CL slices: CTA q streams A[:, slice q] and x[segment rows,
-//      slice q] and accumulates a [<=32 x r] fp32 partial with mma.sync;
+//      slice q] and accumulates a [r x <=32] fp32 partial in tensor memory;
 //   2. reduce the partials through distributed shared memory: after a
 //      cluster barrier, CTA q sums rows [q*n/CL, (q+1)*n/CL) over the CL
 //      partials (fixed order: deterministic) and writes the scaled rows into
@@ -27,25 +27,34 @@
 //
 // Warp roles: warp 8 is the producer. Its lane 0 issues every TMA load of the
 // CTA into a ring of STAGES shared-memory stages, each completing on a "full"
-// mbarrier, and refills a stage as soon as the 8 compute warps have arrived
-// on its "empty" mbarrier. The compute warps never wait for one another
-// inside the stage loop, and the producer keeps loading (across segment and
-// phase boundaries -- the expand-phase loads of B and y do not depend on H)
-// while the compute warps run the cluster reduction.
+// mbarrier, and refills a stage as soon as its "empty" mbarrier fires (the
+// MMA commit for shrink stages, compute thread 0 for expand stages). The
+// producer keeps loading across segment and phase boundaries -- the
+// expand-phase loads of B and y do not depend on H -- while the compute warps
+// run the cluster reduction.
 //
 // Data movement: A and x arrive as tiled tensor loads (cp.async.bulk.tensor)
 // of 64-column boxes with the 128-byte swizzle -- conflict-free fragment
 // loads, zero fill past the ends of d and T; x and y boxes are 8, 16 or 32
-// rows high to match the segment. B (contiguous per column chunk) arrives as
-// one 1-D bulk copy (cp.async.bulk). One stage carries 256 elements of d
-// (shrink) or 256 output columns (expand). The cluster's segment descriptors
+// rows high to match the segment. B arrives as tensor boxes of 128 rows whose
+// swizzle matches its 2r-byte rows (rank 8: one 1-D bulk copy). One stage
+// carries 256 elements of d (shrink) or 256 output columns (expand). The cluster's segment descriptors
 // are cached in shared memory once per launch.
 //
-// Math: mma.sync m16n8k16 (bf16/fp16 in, fp32 accumulate). Decode segments are
-// 1..32 tokens, far below the 128-row tiles of the tcgen05 unit, and the
-// kernel is bound by HBM bandwidth. In the expand, H enters the MMA split into
-// a 16-bit high part and a 16-bit residual, which keeps ~16 mantissa bits of
-// the fp32 H.
+// Math on the 5th-generation tensor cores (tcgen05.mma, issued by one thread,
+// accumulating in tensor memory):
+//   shrink: D[rank, t] += A[rank, k] . x[t, k]^T per 64-column box, M = 128
+//     (rows past r are never read back), N = 16 or 32 tokens, K = 16 per
+//     instruction, over the CTA's slice of d. The MMA commit itself frees the
+//     stage for the producer, so the compute warps do no per-stage work.
+//   expand (ranks 16-64): D[o, t] = B[o, :] . H[t, :]^T with M = 128 output
+//     columns, N = 16 or 32 tokens, K = r; B in shared memory in the TMA
+//     swizzle of its 2r-byte rows. The compute warps read D back with
+//     tcgen05.ld (one output column per lane), add y, stage the rows in shared
+//     memory and write them back with coalesced 16-byte stores.
+//   expand (rank 8, K < 16): mma.sync m16n8k8 on the CUDA-core warps.
+// H enters the expand MMAs as a 16-bit high part plus a 16-bit residual,
+// which keeps ~16 mantissa bits of the fp32 H; y is rounded once.
 //
 // Programmatic dependent launch: every thread waits on the predecessor
 // (griddepcontrol.wait) before it triggers the dependents, so the pre-wait
@@ -87,15 +96,21 @@ struct ApplyCfg {
   static constexpr int XBOX = 32 * 128;  // room for one 32-row x or y box
   static constexpr int STAGE = 4 * ABOX + 4 * XBOX;  // == 4 * XBOX + W * R * 2; multiple of 1024
   static_assert(STAGE == 4 * XBOX + W * R * 2, "shrink and expand stages have one size");
-  static constexpr int STAGES = R == 64 ? 3 : (R == 32 ? 5 : (R == 16 ? 7 : 8));
+  // sized so that two CTAs fit on one SM (~113 KB each): the second CTA
+  // overlaps the serialised wait / MMA / epilogue latencies of the first
+  static constexpr int STAGES = R == 64 ? 2 : (R == 32 ? 3 : 4);
   static constexpr int PITCH = R + 4;  // floats per row of the P / H tiles
   static constexpr int OFF_FLAGS = 448;
   static constexpr int OFF_DESC = 512;
-  static constexpr int OFF_RED = OFF_DESC + kDescCache * 32;
-  static constexpr int OFF_P = OFF_RED + kComputeWarps * 8 * 32 * 4;
+  static constexpr int OFF_P = OFF_DESC + kDescCache * 32;
   static constexpr int OFF_H = OFF_P + 32 * PITCH * 4;
   static constexpr int OFF_END = OFF_H + 32 * PITCH * 4;
-  static constexpr int SMEM = OFF_END + 1024 + STAGES * STAGE;
+  static constexpr bool TC = R >= 16;  // expand on tcgen05 (K = r must be a multiple of 16)
+  static constexpr int HT = 32 * R * 2;  // one 16-bit H tile (hi or lo), swizzled like B
+  static constexpr int SWZ_BYTES = R * 2;  // B / H row bytes = swizzle span
+  static constexpr uint32_t SWZ_MASK = R == 64 ? 0x70u : (R == 32 ? 0x30u : 0x10u);
+  static constexpr uint32_t UMMA_LAYOUT = R == 64 ? 2u : (R == 32 ? 4u : 6u);
+  static constexpr int SMEM = OFF_END + 1024 + (TC ? 2 * HT : 0) + STAGES * STAGE;
 };
 
 __device__ __forceinline__ DevSeg unpack_seg(int4 v0, int4 v1) {
@@ -178,9 +193,6 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   using C = ApplyCfg<R>;
   using E = Elem<T>;
   constexpr int S = C::STAGES;
-  constexpr int NT = R / 8;  // shrink: n-tiles of 8 rank columns
-  constexpr int KP = kComputeWarps / NT;  // shrink: warps sharing one n-tile (split over k-steps)
-  constexpr int KS = C::KC / 16;  // shrink: k16 steps per stage
   constexpr int NTW = C::W / 8 / kComputeWarps;  // expand: n-tiles of 8 columns per warp
   constexpr int KE = R >= 16 ? R / 16 : 1;  // expand: k-steps over the rank
   constexpr int PITCH = C::PITCH;
@@ -192,10 +204,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   volatile int* s_bad = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS);
   volatile int* s_issued = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS + 4);
   int4* sdesc = reinterpret_cast<int4*>(smem + C::OFF_DESC);
-  float* red = reinterpret_cast<float*>(smem + C::OFF_RED);
   float* Ps = reinterpret_cast<float*>(smem + C::OFF_P);
   float* Hs = reinterpret_cast<float*>(smem + C::OFF_H);
-  uint8_t* stage_base = align1024(smem + C::OFF_END);
+  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(smem + 320);
+  uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + 336);
+  uint8_t* ht_base = align1024(smem + C::OFF_END);  // H hi / lo tiles (tcgen05 expand)
+  uint8_t* stage_base = ht_base + (C::TC ? 2 * C::HT : 0);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
@@ -211,9 +225,10 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], kComputeWarps);
+      mbar_init(&empty[s], 1);
     }
     mbar_init(cbar, CL);
+    mbar_init(mma_bar, 1);
     *s_bad = 0;
     *s_issued = 0;
     fence_mbar_init();
@@ -225,8 +240,14 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
     if ((a.mode & kModeExpand) && a.y_tma)
       for (int i = 0; i < 3; ++i) prefetch_tmap(&a.tmap_y[i]);
+    if ((a.mode & kModeExpand) && C::TC && !a.registry) prefetch_tmap(&a.tmap_b);
   }
+  // TMEM: shrink accumulator (32 columns) + two expand accumulators (32 each)
+  const bool use_tmem = (a.mode & kModeShrink) || (C::TC && (a.mode & kModeExpand));
+  if (use_tmem && warp == 0) tmem_alloc(s_tmem, 128);
+  if (use_tmem) tc_fence_before();
   __syncthreads();
+  if (use_tmem) tc_fence_after();
   cluster_sync_hw();  // every CTA's cluster barrier is initialised before anyone arrives on it
 
   const bool do_sh = (a.mode & kModeShrink) != 0;
@@ -292,11 +313,20 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           const int oc = oB0 + (sub - nA) * C::W;
           const int wc = min(C::W, a.o - oc);
           if (parts & 1) {
-            mbar_arrive_expect_tx(bar, wc * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
-            const T* B = a.registry ? static_cast<const T*>(s.b)
-                                    : static_cast<const T*>(a.wb_base) +
-                                          static_cast<int64_t>(s.adapter_id) * a.wb_stride;
-            bulk_g2s(st + 4 * C::XBOX, B + static_cast<int64_t>(oc) * R, wc * R * 2, bar);
+            if constexpr (C::TC) {
+              // two 128-row boxes of B, rows past o zero-filled
+              mbar_arrive_expect_tx(bar, 2 * 128 * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
+              const void* bmap = a.registry ? s.b : static_cast<const void*>(&a.tmap_b);
+              const int bid = a.registry ? 0 : s.adapter_id;
+              tma_load_3d(st + 4 * C::XBOX, bmap, 0, oc, bid, bar);
+              tma_load_3d(st + 4 * C::XBOX + 128 * R * 2, bmap, 0, oc + 128, bid, bar);
+            } else {
+              mbar_arrive_expect_tx(bar, wc * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
+              const T* B = a.registry ? static_cast<const T*>(s.b)
+                                      : static_cast<const T*>(a.wb_base) +
+                                            static_cast<int64_t>(s.adapter_id) * a.wb_stride;
+              bulk_g2s(st + 4 * C::XBOX, B + static_cast<int64_t>(oc) * R, wc * R * 2, bar);
+            }
           }
           if ((parts & 2) && a.y_tma) {
 #pragma unroll
@@ -337,12 +367,18 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   }
   const int g = lane >> 2;
   const int c = lane & 3;
+  const int quarter = warp & 3;  // TMEM lane quarter this warp may read
+  const int half = warp >> 2;
   int kc = 0;  // next stage-unit to consume
-  uint32_t cph = 0;
+  uint32_t cph = 0;  // cluster barrier phase
+  uint32_t mph = 0;  // MMA completion barrier phase
+  const uint32_t tbase = use_tmem ? *s_tmem : 0u;
+  const uint32_t t_sh = tbase;  // shrink accumulator: 128 lanes x 32 columns
+  const uint32_t t_ex = tbase + 32;  // expand accumulators: 2 x (128 lanes x 32 columns)
+  constexpr uint32_t kAbf = E::is_bf16 ? 1u : 0u;
 
-  // Wait for the next stage; true when its data may be used.
-  auto acquire = [&](int& stage) -> bool {
-    stage = kc % S;
+  // Wait for stage `kc` (calling threads only); false after an error.
+  auto wait_full = [&](int stage) -> bool {
     if (*s_bad) return false;
     const unsigned long long tw = tr.before_wait();
     const bool ok = mbar_wait_bounded(&full[stage], (kc / S) & 1, a.err);
@@ -350,13 +386,13 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     if (!ok) *s_bad = 1;
     return ok;
   };
-  // Hand the stage back to the producer.
-  auto release = [&](int stage) {
-    tr.mark(2);
-    __syncwarp();
-    if (lane == 0) mbar_arrive(&empty[stage]);
-    tr.mark(3);
-    ++kc;
+  // Wait for the MMAs committed to mma_bar (all compute threads).
+  auto wait_mma = [&]() -> bool {
+    bool ok = !*s_bad && mbar_wait_bounded(mma_bar, mph, a.err);
+    mph ^= 1u;
+    if (!ok) *s_bad = 1;
+    tc_fence_after();
+    return ok;
   };
 
   for (int sj = 0; sj < nmine; ++sj) {
@@ -366,81 +402,61 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     const float alpha = a.registry ? s.alpha : a.scale;
 
     if (do_sh) {
-      // ---- 1. partial shrink over this CTA's slice of d -------------------
-      const int nt = warp % NT;
-      const int kp = warp / NT;
-      float acc[2][2][4];  // [independent chain][m-tile][fragment]
+      // ---- 1. partial shrink over this CTA's slice of d on tcgen05 -----------
+      // D[rank, t] (TMEM) += A_box[rank, k] . x_box[t, k]^T: M = 128 (rows past
+      // r read neighbouring shared memory and are never used), N = 16 or 32
+      // tokens, K = 16 per instruction. Thread 0 issues; the commit frees the
+      // stage for the producer, so no other thread takes part per stage.
+      const uint32_t Nsh = n > 16 ? 32u : 16u;
+      const uint32_t idesc = umma_idesc(kAbf, 128, Nsh);
+      if (tid == 0) {
+        for (int i = 0; i < nA; ++i, ++kc) {
+          const int stage = kc % S;
+          const bool ok = wait_full(stage);
+          if (ok && n > 0) {
+            tc_fence_after();
+            const uint32_t st = smem_u32(stage_base + stage * C::STAGE);
 #pragma unroll
-      for (int x = 0; x < 2; ++x)
+            for (int j = 0; j < 4; ++j)
 #pragma unroll
-        for (int m = 0; m < 2; ++m)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) acc[x][m][j] = 0.f;
-      const bool m1 = n > 16;
-      for (int i = 0; i < nA; ++i) {
-        int stage;
-        if (acquire(stage) && n > 0) {
-          const uint8_t* st = stage_base + stage * C::STAGE;
-          const int arow = nt * 8 + g;
-#pragma unroll
-          for (int it = 0; it < KS / KP; ++it) {
-            const int ks = kp + it * KP;
-            const int box = ks >> 2;
-            const int col = (ks & 3) * 16 + 2 * c;
-            const uint8_t* ab = st + box * C::ABOX;
-            const uint8_t* xb = st + 4 * C::ABOX + box * C::XBOX;
-            const uint32_t b0 = lds32(ab + sw128(arow, col));
-            const uint32_t b1 = lds32(ab + sw128(arow, col + 8));
-            uint32_t af[4];
-            af[0] = lds32(xb + sw128(g, col));
-            af[1] = lds32(xb + sw128(g + 8, col));
-            af[2] = lds32(xb + sw128(g, col + 8));
-            af[3] = lds32(xb + sw128(g + 8, col + 8));
-            mma_k16<T>(acc[it & 1][0], af, b0, b1);
-            if (m1) {
-              af[0] = lds32(xb + sw128(g + 16, col));
-              af[1] = lds32(xb + sw128(g + 24, col));
-              af[2] = lds32(xb + sw128(g + 16, col + 8));
-              af[3] = lds32(xb + sw128(g + 24, col + 8));
-              mma_k16<T>(acc[it & 1][1], af, b0, b1);
-            }
+              for (int ks = 0; ks < 4; ++ks)
+                umma_f16(t_sh, umma_desc(st + j * C::ABOX + ks * 32, 1024, 2),
+                         umma_desc(st + 4 * C::ABOX + j * C::XBOX + ks * 32, 1024, 2), idesc,
+                         (i > 0 || j > 0 || ks > 0) ? 1u : 0u);
+            umma_commit(&empty[stage]);  // the stage is free once these MMAs have read it
+          } else {
+            mbar_arrive(&empty[stage]);
           }
         }
-        release(stage);
+        if (nA > 0 && n > 0 && !*s_bad) umma_commit(mma_bar);
+      } else {
+        kc += nA;
       }
+      // partial tile -> Ps[token][rank] (zeros when this CTA owns no slice of d)
+      const bool have = nA > 0 && n > 0;
+      if (have) {
+        named_sync(kBarCompute, kComputeThreads);  // thread 0 has committed
+        wait_mma();
+      }
+      if (half == 0 && quarter * 32 < R) {
+        float v[32];
+        // warp-uniform: the tcgen05 loads are .sync.aligned
+        if (__shfl_sync(0xffffffffu, (have && !*s_bad) ? 1 : 0, 0)) {
+          const uint32_t ta = t_sh + (static_cast<uint32_t>(quarter * 32) << 16);
+          tmem_ld16(ta, *reinterpret_cast<float(*)[16]>(v));
+          tmem_ld16(ta + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+        } else {
 #pragma unroll
-      for (int m = 0; m < 2; ++m)
+          for (int j = 0; j < 32; ++j) v[j] = 0.f;
+        }
+        const int r = quarter * 32 + lane;
+        if (r < R) {
 #pragma unroll
-        for (int j = 0; j < 4; ++j) acc[0][m][j] += acc[1][m][j];
-      // combine the KP warps of each n-tile, then publish the partial tile
-      if constexpr (KP > 1) {
-        float* mine = red + warp * 8 * 32;
-#pragma unroll
-        for (int m = 0; m < 2; ++m)
-#pragma unroll
-          for (int j = 0; j < 4; ++j) mine[(m * 4 + j) * 32 + lane] = acc[0][m][j];
-        named_sync(kBarCompute, kComputeThreads);
-        if (kp == 0) {
-#pragma unroll
-          for (int w2 = 1; w2 < KP; ++w2) {
-            const float* other = red + (nt + w2 * NT) * 8 * 32;
-#pragma unroll
-            for (int m = 0; m < 2; ++m)
-#pragma unroll
-              for (int j = 0; j < 4; ++j) acc[0][m][j] += other[(m * 4 + j) * 32 + lane];
-          }
+          for (int j = 0; j < 32; ++j) Ps[j * PITCH + r] = v[j];
         }
       }
-      if (kp == 0) {
-#pragma unroll
-        for (int m = 0; m < 2; ++m)
-#pragma unroll
-          for (int hf = 0; hf < 2; ++hf) {
-            const int row = m * 16 + g + hf * 8;
-            *reinterpret_cast<float2*>(Ps + row * PITCH + nt * 8 + 2 * c) =
-                make_float2(acc[0][m][hf * 2], acc[0][m][hf * 2 + 1]);
-          }
-      }
+      tc_fence_before();
+      tr.mark(2);
       // ---- 2. reduce-scatter + all-gather of the partials over the cluster
       if (!cluster_barrier_bounded(cbar, cph, CL, kBarCompute, kComputeThreads, a.err)) *s_bad = 1;
       cph ^= 1u;
@@ -481,8 +497,102 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       named_sync(kBarCompute, kComputeThreads);
     }
 
-    if (do_ex && nB > 0) {
-      // ---- 3. expand over this CTA's slice of o ----------------------------
+    if (!do_ex || nB == 0) continue;
+    T* yg = static_cast<T*>(a.y);
+
+    if constexpr (C::TC) {
+      // ---- 3. expand over this CTA's slice of o on tcgen05 -------------------
+      // D[o, t] (TMEM, fp32) = B[o, :] . H_hi[t, :]^T + B[o, :] . H_lo[t, :]^T
+      // with M = 128 output columns per MMA, N = 16 or 32 tokens, K = r.
+      const int N = n > 16 ? 32 : 16;
+      for (int e = tid; e < N * (R / 2); e += kComputeThreads) {
+        const int row = e / (R / 2);
+        const int k = (e % (R / 2)) * 2;
+        float2 v = make_float2(0.f, 0.f);
+        if (row < n) v = *reinterpret_cast<const float2*>(Hs + row * PITCH + k);
+        const uint32_t hv = E::pack2(v.x, v.y);
+        const float2 r2 = E::unpack2(hv);
+        const uint32_t lv = E::pack2(v.x - r2.x, v.y - r2.y);
+        uint32_t lin = static_cast<uint32_t>(row * C::SWZ_BYTES + k * 2);
+        lin ^= (lin >> 3) & C::SWZ_MASK;
+        *reinterpret_cast<uint32_t*>(ht_base + lin) = hv;
+        *reinterpret_cast<uint32_t*>(ht_base + C::HT + lin) = lv;
+      }
+      fence_proxy_async_smem();
+      const uint32_t idesc = umma_idesc(kAbf, 128, static_cast<uint32_t>(N));
+      for (int i = 0; i < nB; ++i, ++kc) {
+        const int stage = kc % S;
+        wait_full(stage);
+        tc_fence_before();
+        named_sync(kBarCompute, kComputeThreads);  // stage seen, H tiles written, TMEM free
+        // warp-uniform: the tcgen05 loads below are .sync.aligned
+        const bool go = __shfl_sync(0xffffffffu, (!*s_bad && n > 0) ? 1 : 0, 0) != 0;
+        uint8_t* st = stage_base + stage * C::STAGE;
+        const int oc = oB0 + i * C::W;
+        const int wc = min(C::W, a.o - oc);
+        if (go && tid == 0) {
+          tc_fence_after();
+          const uint32_t hhi = smem_u32(ht_base), hlo = hhi + C::HT;
+#pragma unroll
+          for (int hh = 0; hh < 2; ++hh) {
+            const uint32_t bsm = smem_u32(st + 4 * C::XBOX + hh * 128 * R * 2);
+#pragma unroll
+            for (int ks = 0; ks < R / 16; ++ks)
+              umma_f16(t_ex + hh * 32, umma_desc(bsm + ks * 32, 16 * R, C::UMMA_LAYOUT),
+                       umma_desc(hhi + ks * 32, 16 * R, C::UMMA_LAYOUT), idesc, ks > 0 ? 1u : 0u);
+#pragma unroll
+            for (int ks = 0; ks < R / 16; ++ks)
+              umma_f16(t_ex + hh * 32, umma_desc(bsm + ks * 32, 16 * R, C::UMMA_LAYOUT),
+                       umma_desc(hlo + ks * 32, 16 * R, C::UMMA_LAYOUT), idesc, 1u);
+          }
+          umma_commit(mma_bar);
+        }
+        if (go) {
+          wait_mma();
+          // this lane: output column ol of the stage, every token of the segment
+          const int ol = half * 128 + quarter * 32 + lane;
+          const uint32_t ta = t_ex + (static_cast<uint32_t>(quarter * 32) << 16) + half * 32;
+          float v[32];
+          tmem_ld16(ta, *reinterpret_cast<float(*)[16]>(v));
+          if (N > 16) tmem_ld16(ta + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+          tr.mark(2);
+          if (a.y_tma) {
+            // y from the stage (swizzled boxes) -> registers; results -> the
+            // same region, linear rows of 256 columns; one bulk store per row
+            float yv[32];
+            const uint8_t* yb = st + (ol >> 6) * C::XBOX;
+            const int cl = ol & 63;
+#pragma unroll
+            for (int j = 0; j < 32; ++j) yv[j] = j < n ? E::to_f(*reinterpret_cast<const T*>(yb + sw128(j, cl))) : 0.f;
+            named_sync(kBarCompute, kComputeThreads);  // every y read is done
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < n) *reinterpret_cast<T*>(st + j * (C::W * 2) + ol * 2) = E::from_f(yv[j] + v[j]);
+            named_sync(kBarCompute, kComputeThreads);
+            // rows -> global with 16-byte stores (wc is a multiple of 8)
+            T* y0 = yg + static_cast<int64_t>(s.token_start) * a.y_ld + a.y_off + oc;
+            const int vec_per_row = wc / 8;
+            for (int e = tid; e < n * vec_per_row; e += kComputeThreads) {
+              const int j = e / vec_per_row, cv = e % vec_per_row;
+              *reinterpret_cast<int4*>(y0 + static_cast<int64_t>(j) * a.y_ld + cv * 8) =
+                  *reinterpret_cast<const int4*>(st + j * (C::W * 2) + cv * 16);
+            }
+          } else if (ol < wc) {
+            T* yc = yg + static_cast<int64_t>(s.token_start) * a.y_ld + a.y_off + oc + ol;
+            float yv[32];
+#pragma unroll
+            for (int j = 0; j < 32; ++j) yv[j] = j < n ? E::to_f(yc[static_cast<int64_t>(j) * a.y_ld]) : 0.f;
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < n) yc[static_cast<int64_t>(j) * a.y_ld] = E::from_f(yv[j] + v[j]);
+          }
+        }
+        named_sync(kBarCompute, kComputeThreads);
+        if (tid == 0) mbar_arrive(&empty[stage]);
+        tr.mark(3);
+      }
+    } else {
+      // ---- 3. expand (rank 8) over this CTA's slice of o with mma.sync -------
       // H fragments (16-bit high part + residual) of both 16-row tiles.
       uint32_t hi[2][KE][4], lo[2][KE][4];
 #pragma unroll
@@ -495,12 +605,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           float2 x[4];
           x[0] = *reinterpret_cast<const float2*>(h0 + k0);
           x[1] = *reinterpret_cast<const float2*>(h1 + k0);
-          if (R >= 16) {
-            x[2] = *reinterpret_cast<const float2*>(h0 + k0 + 8);
-            x[3] = *reinterpret_cast<const float2*>(h1 + k0 + 8);
-          } else {
-            x[2] = x[3] = make_float2(0.f, 0.f);
-          }
+          x[2] = x[3] = make_float2(0.f, 0.f);
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             hi[m][ks][e] = E::pack2(x[e].x, x[e].y);
@@ -510,10 +615,9 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         }
       }
       const bool m1 = n > 16;
-      T* yg = static_cast<T*>(a.y);
-      for (int i = 0; i < nB; ++i) {
-        int stage;
-        if (acquire(stage) && n > 0) {
+      for (int i = 0; i < nB; ++i, ++kc) {
+        const int stage = kc % S;
+        if (wait_full(stage) && n > 0) {
           const uint8_t* st = stage_base + stage * C::STAGE;
           const uint8_t* Bs = st + 4 * C::XBOX;
           const int oc = oB0 + i * C::W;
@@ -529,30 +633,37 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           for (int j = 0; j < NTW; ++j) {
             const int nt = warp * NTW + j;
             if (nt * 8 < wc) {
-#pragma unroll
-              for (int ks = 0; ks < KE; ++ks) {
-                const uint8_t* brow = Bs + (nt * 8 + g) * (R * 2) + ks * 32 + c * 4;
-                const uint32_t b0 = lds32(brow);
-                if constexpr (R == 8) {
-                  mma_k8<T>(acc[0][j], hi[0][ks][0], hi[0][ks][1], b0);
-                  mma_k8<T>(acc[0][j], lo[0][ks][0], lo[0][ks][1], b0);
-                  if (m1) {
-                    mma_k8<T>(acc[1][j], hi[1][ks][0], hi[1][ks][1], b0);
-                    mma_k8<T>(acc[1][j], lo[1][ks][0], lo[1][ks][1], b0);
-                  }
-                } else {
-                  const uint32_t b1 = lds32(brow + 16);
-                  mma_k16<T>(acc[0][j], hi[0][ks], b0, b1);
-                  mma_k16<T>(acc[0][j], lo[0][ks], b0, b1);
-                  if (m1) {
-                    mma_k16<T>(acc[1][j], hi[1][ks], b0, b1);
-                    mma_k16<T>(acc[1][j], lo[1][ks], b0, b1);
-                  }
-                }
+              const uint32_t b0 = lds32(Bs + (nt * 8 + g) * (R * 2) + c * 4);
+              mma_k8<T>(acc[0][j], hi[0][0][0], hi[0][0][1], b0);
+              mma_k8<T>(acc[0][j], lo[0][0][0], lo[0][0][1], b0);
+              if (m1) {
+                mma_k8<T>(acc[1][j], hi[1][0][0], hi[1][0][1], b0);
+                mma_k8<T>(acc[1][j], lo[1][0][0], lo[1][0][1], b0);
               }
             }
           }
-          // y += acc, one rounding
+          // y += acc, one rounding (all y reads first, then the stores)
+          float yv[2][NTW][2][2];
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int j = 0; j < NTW; ++j)
+#pragma unroll
+              for (int hf = 0; hf < 2; ++hf) {
+                const int row = m * 16 + g + hf * 8;
+                const int col = (warp * NTW + j) * 8 + 2 * c;
+                float2 v2 = make_float2(0.f, 0.f);
+                if (row < n && col < wc) {
+                  if (a.y_tma) {
+                    v2 = E::unpack2(lds32(st + (col >> 6) * C::XBOX + sw128(row, col & 63)));
+                  } else {
+                    const T* yp = yg + static_cast<int64_t>(s.token_start + row) * a.y_ld + a.y_off + oc + col;
+                    v2 = make_float2(E::to_f(yp[0]), E::to_f(yp[1]));
+                  }
+                }
+                yv[m][j][hf][0] = v2.x;
+                yv[m][j][hf][1] = v2.y;
+              }
 #pragma unroll
           for (int m = 0; m < 2; ++m)
 #pragma unroll
@@ -563,18 +674,18 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
                 const int col = (warp * NTW + j) * 8 + 2 * c;
                 if (row < n && col < wc) {
                   T* yp = yg + static_cast<int64_t>(s.token_start + row) * a.y_ld + a.y_off + oc + col;
-                  const float v0 = acc[m][j][hf * 2], v1 = acc[m][j][hf * 2 + 1];
+                  const float v0 = yv[m][j][hf][0] + acc[m][j][hf * 2], v1 = yv[m][j][hf][1] + acc[m][j][hf * 2 + 1];
                   if (a.y_tma) {
-                    const float2 yv = E::unpack2(lds32(st + (col >> 6) * C::XBOX + sw128(row, col & 63)));
-                    *reinterpret_cast<uint32_t*>(yp) = E::pack2(yv.x + v0, yv.y + v1);
+                    *reinterpret_cast<uint32_t*>(yp) = E::pack2(v0, v1);
                   } else {
-                    yp[0] = E::from_f(E::to_f(yp[0]) + v0);
-                    yp[1] = E::from_f(E::to_f(yp[1]) + v1);
+                    yp[0] = E::from_f(v0);
+                    yp[1] = E::from_f(v1);
                   }
                 }
               }
         }
-        release(stage);
+        named_sync(kBarCompute, kComputeThreads);
+        if (tid == 0) mbar_arrive(&empty[stage]);
       }
     }
   }
@@ -585,6 +696,14 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     if (tid == 0) {
       const int issued = *s_issued;
       for (int u = kc; u < issued; ++u) mbar_wait_bounded(&full[u % S], (u / S) & 1, nullptr, kDrainNs);
+    }
+  }
+  if (use_tmem) {
+    tc_fence_before();
+    named_sync(kBarCompute, kComputeThreads);  // every TMEM read and MMA is done
+    if (warp == 0) {
+      tc_fence_after();
+      tmem_dealloc(*s_tmem, 128);
     }
   }
   tr.finish();

@@ -18,8 +18,9 @@ constexpr int kSegTokens = 32;
 //   live table (build_seg_bounds): adapter_id/token_start/token_count only; the
 //     apply kernel resolves weights as base + adapter_id * stride.
 //   registry table (build_segments): `a` is the device address of a TMA
-//     descriptor of the adapter's A [r, d], `b` the address of its B [o, r]
-//     (original tensor or staging slot), alpha the adapter's scale.
+//     descriptor of the adapter's A [r, d]; `b` is, for r >= 16, the address
+//     of a TMA descriptor of its B [o, r] and, for r = 8, B's address
+//     (original tensor or staging slot); alpha is the adapter's scale.
 struct DevSeg {
   int32_t adapter_id;
   int32_t token_start;
@@ -46,6 +47,7 @@ struct ApplyArgs {
   CUtensorMap tmap_x[3];  // x [T, d]: boxes of 64 columns, 128B swizzle
   CUtensorMap tmap_y[3];  // y columns [y_off, y_off + o) x T rows, 128B swizzle
   CUtensorMap tmap_a;  // live mode: A stack [L, r, d], box 64 x r x 1
+  CUtensorMap tmap_b;  // live mode, r >= 16: B stack [L, o, r], box r x 128 x 1, swizzle = 2r bytes
   const DevSeg* segs;
   const int* num_segs;
   float* h;  // shrink-only: H [T, r] fp32 written; expand-only: read
