@@ -68,6 +68,8 @@ SIGNATURES = {
     "wp_evict_adapter": (_int, [_vp, _i32]),
     "wp_build_segments": (_int, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32), _i32, _vp]),
     "wp_build_seg_bounds": (_int, [_vp, _vp, _i32, _i32, _vp]),
+    "wp_build_seg_bounds_noalloc": (_int, [_vp, _i32, _i32, _vp, _vp, _vp]),
+    "wp_seg_bounds_noalloc_max_tokens": (_int, []),
     "wp_read_seg_table": (_int, [_vp, _i32, ctypes.POINTER(WpSegment), _i32, ctypes.POINTER(_i32)]),
     "wp_shrink": (_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]),
     "wp_expand": (_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]),

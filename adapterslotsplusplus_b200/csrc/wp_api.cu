@@ -259,6 +259,11 @@ extern "C" {
 
 const char* wp_last_error(const wp_handle* h) { return h ? h->err.c_str() : g_err.c_str(); }
 
+int wp_set_global_error(int code, const char* msg) {
+  g_err = msg ? msg : "";
+  return code;
+}
+
 int wp_rank_supported(int32_t rank) { return rank_ok(rank) ? 1 : 0; }
 
 int64_t wp_kernel_launch_count(const wp_handle* h) { return h ? h->launches : 0; }

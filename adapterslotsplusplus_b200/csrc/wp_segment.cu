@@ -122,3 +122,111 @@ cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* seg
 }
 
 }  // namespace wp
+
+// ---------------------------------------------------------------------------
+// Allocation-free variant of the segmenter.
+//
+// Some callers cannot allocate device memory at all: a plugin that runs inside
+// another inference framework's memory plan, or code that must not call
+// cudaMalloc because it synchronises the device and bypasses the host
+// framework's allocator. Such a caller cannot create a wp_handle (wp_create
+// allocates the tables), so this entry point takes the output table from the
+// caller and keeps its one scratch buffer -- the compacted run starts -- in a
+// fixed array in the library's own device memory image.
+
+// Records the message returned by wp_last_error(NULL) (defined in wp_api.cu).
+extern "C" int wp_set_global_error(int code, const char* msg);
+static int wp_noalloc_fail(int code, const char* msg) { return wp_set_global_error(code, msg); }
+
+namespace {
+
+constexpr int kNoAllocMaxTokens = 65536;  // 256 KB of run starts per device
+__device__ __align__(256) int g_seg_scratch[kNoAllocMaxTokens];
+
+// Same algorithm as seg_bounds_kernel, writing (adapter_id, token_start,
+// token_count) triples of int32 to the caller's table.
+template <typename I>
+__global__ void __launch_bounds__(wp::kSegThreads, 1)
+    seg_bounds_triples_kernel(const I* __restrict__ idx, int T, int32_t* __restrict__ table, int* __restrict__ num,
+                              int* __restrict__ run_starts) {
+  __shared__ int warp_buf[33];
+  const int tid = threadIdx.x;
+  int nruns = 0;
+  for (int base = 0; base < T; base += wp::kSegThreads) {
+    const int i = base + tid;
+    int flag = 0;
+    if (i < T) flag = (i == 0) || (idx[i] != idx[i - 1]);
+    int total;
+    const int pos = wp::block_exclusive_scan(flag, warp_buf, &total);
+    if (flag) run_starts[nruns + pos] = i;
+    nruns += total;
+  }
+  __syncthreads();
+  int nseg = 0;
+  for (int base = 0; base < nruns; base += wp::kSegThreads) {
+    const int k = base + tid;
+    int pieces = 0, start = 0, len = 0;
+    int32_t id = -1;
+    if (k < nruns) {
+      start = run_starts[k];
+      const int end = (k + 1 < nruns) ? run_starts[k + 1] : T;
+      len = end - start;
+      const I raw = idx[start];
+      if (raw >= 0) {
+        id = static_cast<int32_t>(raw);
+        pieces = (len + wp::kSegTokens - 1) / wp::kSegTokens;
+      }
+    }
+    int total;
+    const int slot = nseg + wp::block_exclusive_scan(pieces, warp_buf, &total);
+    for (int j = 0; j < pieces; ++j) {
+      int32_t* e = table + 3 * (slot + j);
+      e[0] = id;
+      e[1] = start + j * wp::kSegTokens;
+      e[2] = min(wp::kSegTokens, len - j * wp::kSegTokens);
+    }
+    nseg += total;
+  }
+  if (tid == 0) *num = nseg;
+}
+
+// Device address of g_seg_scratch, looked up once per device.
+int* g_scratch_ptr[64] = {nullptr};
+
+}  // namespace
+
+extern "C" int wp_seg_bounds_noalloc_max_tokens(void) { return kNoAllocMaxTokens; }
+
+// Declared in include/wp_api.h. The first call on a device looks up the
+// scratch array's device address (cudaGetSymbolAddress, with that device
+// current); make that first call before any stream capture. Calls on one
+// device share the scratch array: calls that overlap on the GPU (different
+// streams, no ordering between them) race on it.
+extern "C" int wp_build_seg_bounds_noalloc(const void* token_lora_indices, int32_t idx_dtype, int32_t T,
+                                           int32_t* out_table, int32_t* out_num, void* stream) {
+  if (idx_dtype != 3 && idx_dtype != 4) return wp_noalloc_fail(-1, "build_seg_bounds_noalloc: ids must be int32 or int64");
+  if (T < 0) return wp_noalloc_fail(-1, "build_seg_bounds_noalloc: negative token count");
+  if (T > kNoAllocMaxTokens)
+    return wp_noalloc_fail(-4, "build_seg_bounds_noalloc: T exceeds the fixed scratch of 65536 tokens");
+  if (!out_num || (T > 0 && (!token_lora_indices || !out_table)))
+    return wp_noalloc_fail(-1, "build_seg_bounds_noalloc: NULL pointer");
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64)
+    return wp_noalloc_fail(-2, "build_seg_bounds_noalloc: no current CUDA device");
+  if (!g_scratch_ptr[dev]) {
+    int* p = nullptr;
+    const cudaError_t e = cudaGetSymbolAddress(reinterpret_cast<void**>(&p), g_seg_scratch);
+    if (e != cudaSuccess || !p) return wp_noalloc_fail(-2, "build_seg_bounds_noalloc: cudaGetSymbolAddress failed");
+    g_scratch_ptr[dev] = p;
+  }
+  cudaStream_t s = static_cast<cudaStream_t>(stream);
+  if (idx_dtype == 4)
+    seg_bounds_triples_kernel<int64_t><<<1, wp::kSegThreads, 0, s>>>(static_cast<const int64_t*>(token_lora_indices),
+                                                                      T, out_table, out_num, g_scratch_ptr[dev]);
+  else
+    seg_bounds_triples_kernel<int32_t><<<1, wp::kSegThreads, 0, s>>>(static_cast<const int32_t*>(token_lora_indices),
+                                                                      T, out_table, out_num, g_scratch_ptr[dev]);
+  const cudaError_t e = cudaGetLastError();
+  if (e != cudaSuccess) return wp_noalloc_fail(-2, cudaGetErrorString(e));
+  return 0;
+}

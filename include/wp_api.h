@@ -138,6 +138,27 @@ int wp_build_segments(wp_handle* h, const int32_t* sorted_adapter_ids, const int
 int wp_build_seg_bounds(wp_handle* h, const void* token_lora_indices, int32_t idx_dtype, int32_t T,
                         void* stream);
 
+/* Allocation-free segmenter (no counterpart in the reference). For callers
+ * that may not allocate device memory at all -- e.g. a plugin running inside
+ * another framework's pre-planned memory, where a cudaMalloc would synchronise
+ * the device and bypass that framework's allocator -- and therefore cannot
+ * create a wp_handle. Same table as wp_build_seg_bounds, written by the
+ * device as int32 triples (adapter_id, token_start, token_count) into the
+ * caller's DEVICE buffer out_table (room for T triples) and the count into
+ * the caller's DEVICE int32 *out_num, on `stream`, on the current device.
+ * Its only scratch (run starts) is a fixed array of
+ * wp_seg_bounds_noalloc_max_tokens() = 65536 ints inside the library's device
+ * image, held on every GPU that loads the library until the process exits;
+ * T above that is rejected (WP_ERR_CAPACITY, message in wp_last_error(NULL)).
+ * Nothing needs to start at zero: each call writes the scratch before reading
+ * it. The first call on a device looks the array's address up, so make it
+ * before any stream capture. All calls on a device share the array: calls
+ * that overlap on the GPU race. Calls no allocating routine. */
+int wp_build_seg_bounds_noalloc(const void* token_lora_indices, int32_t idx_dtype, int32_t T, int32_t* out_table,
+                                int32_t* out_num, void* stream);
+/* Largest T wp_build_seg_bounds_noalloc accepts (65536). */
+int wp_seg_bounds_noalloc_max_tokens(void);
+
 /* Test readback of a segment table (the reference exposes none). Synchronises
  * the handle's device. Writes up to `cap` entries, sets *num to the table's
  * num_segments. */
