@@ -62,7 +62,8 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     inc, libdir = nccl_paths()
     objdir = PKG / "_build"
     objdir.mkdir(exist_ok=True)
-    common = [nvcc, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", str(INCLUDE), "-I", inc]
+    common = [nvcc, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", str(INCLUDE), "-I", inc,
+              *os.environ.get("WP_NVCC_EXTRA", "").split()]
     objs = []
     for src in SOURCES:
         obj = objdir / (Path(src).stem + ".o")

@@ -25,13 +25,18 @@
 // tensor-parallel all-reduce and the registry-path shrink()) or the expand
 // alone (H read from global memory).
 //
-// Warp roles: warp 8 is the producer. Its lane 0 issues every TMA load of the
-// CTA into a ring of STAGES shared-memory stages, each completing on a "full"
-// mbarrier, and refills a stage as soon as its "empty" mbarrier fires (the
-// MMA commit for shrink stages, compute thread 0 for expand stages). The
-// producer keeps loading across segment and phase boundaries -- the
-// expand-phase loads of B and y do not depend on H -- while the compute warps
-// run the cluster reduction.
+// Warp roles, handing off only through mbarriers:
+//   warp 8 (producer): lane 0 issues every TMA load of the CTA into a ring of
+//     STAGES shared-memory stages ("full" barriers) and refills a stage when
+//     its "empty" barrier fires; it runs ahead across segment and phase
+//     boundaries (the expand-phase loads of B and y do not depend on H).
+//   warp 9 (MMA): lane 0 issues every tcgen05.mma. Shrink stages are freed by
+//     the MMA commit itself; accumulators are handed to the compute warps by
+//     commits ("sh_full", "acc_full") and handed back after their TMEM reads
+//     ("sh_free", "acc_free"); two expand accumulators let the MMAs of the
+//     next stage run while the compute warps drain the current one.
+//   warps 0-7 (compute): read accumulators, run the cluster reduction, write
+//     the H tiles ("ht_full"), add y and store, and free expand stages.
 //
 // Data movement: A and x arrive as tiled tensor loads (cp.async.bulk.tensor)
 // of 64-column boxes with the 128-byte swizzle -- conflict-free fragment
@@ -43,15 +48,16 @@
 //
 // Math on the 5th-generation tensor cores (tcgen05.mma, issued by one thread,
 // accumulating in tensor memory):
-//   shrink: D[rank, t] += A[rank, k] . x[t, k]^T per 64-column box, M = 128
-//     (rows past r are never read back), N = 16 or 32 tokens, K = 16 per
-//     instruction, over the CTA's slice of d. The MMA commit itself frees the
+//   shrink: D[rank, t] += A[rank, k] . x[t, k]^T per 64-column box, M = 64
+//     (rows past r are never read back), N = tokens rounded up to 8, K = 16
+//     per instruction, over the CTA's slice of d. The MMA commit itself frees the
 //     stage for the producer, so the compute warps do no per-stage work.
-//   expand (ranks 16-64): D[o, t] = B[o, :] . H[t, :]^T with M = 128 output
-//     columns, N = 16 or 32 tokens, K = r; B in shared memory in the TMA
-//     swizzle of its 2r-byte rows. The compute warps read D back with
-//     tcgen05.ld (one output column per lane), add y, stage the rows in shared
-//     memory and write them back with coalesced 16-byte stores.
+//   expand (ranks 16-64): D[t, o] = H[t, :] . B[o, :]^T with M = 128 rows
+//     (the segment's tokens, spread over the four TMEM lane quarters), N = 256
+//     output columns (a whole stage) and K = r; B in shared memory in the TMA
+//     swizzle of its 2r-byte rows. Each compute lane reads 32 consecutive
+//     output columns of one token with tcgen05.ld, adds y (16-byte reads of
+//     the swizzled y box) and stores 16 bytes at a time.
 //   expand (rank 8, K < 16): mma.sync m16n8k8 on the CUDA-core warps.
 // H enters the expand MMAs as a 16-bit high part plus a 16-bit residual,
 // which keeps ~16 mantissa bits of the fp32 H; y is rounded once.
@@ -83,7 +89,9 @@ namespace wp {
 
 constexpr int kComputeWarps = 8;
 constexpr int kComputeThreads = kComputeWarps * 32;
-constexpr int kThreads = kComputeThreads + 32;  // + the producer warp
+constexpr int kProducerWarp = kComputeWarps;  // TMA issue
+constexpr int kMmaWarp = kComputeWarps + 1;  // tcgen05.mma issue
+constexpr int kThreads = kComputeThreads + 64;  // + the producer and MMA warps
 constexpr int kBarCompute = 1;  // named barrier of the compute warps
 constexpr int kDescCache = 64;  // segment descriptors cached per CTA
 constexpr unsigned long long kDrainNs = 10000000ull;  // 10 ms per stage when draining after an error
@@ -96,9 +104,7 @@ struct ApplyCfg {
   static constexpr int XBOX = 32 * 128;  // room for one 32-row x or y box
   static constexpr int STAGE = 4 * ABOX + 4 * XBOX;  // == 4 * XBOX + W * R * 2; multiple of 1024
   static_assert(STAGE == 4 * XBOX + W * R * 2, "shrink and expand stages have one size");
-  // sized so that two CTAs fit on one SM (~113 KB each): the second CTA
-  // overlaps the serialised wait / MMA / epilogue latencies of the first
-  static constexpr int STAGES = R == 64 ? 2 : (R == 32 ? 3 : 4);
+  static constexpr int STAGES = R == 64 ? 2 : (R == 32 ? 5 : (R == 16 ? 7 : 8));
   static constexpr int PITCH = R + 4;  // floats per row of the P / H tiles
   static constexpr int OFF_FLAGS = 448;
   static constexpr int OFF_DESC = 512;
@@ -106,11 +112,13 @@ struct ApplyCfg {
   static constexpr int OFF_H = OFF_P + 32 * PITCH * 4;
   static constexpr int OFF_END = OFF_H + 32 * PITCH * 4;
   static constexpr bool TC = R >= 16;  // expand on tcgen05 (K = r must be a multiple of 16)
-  static constexpr int HT = 32 * R * 2;  // one 16-bit H tile (hi or lo), swizzled like B
+  static constexpr int HT = 32 * R * 2;  // one 16-bit H tile (hi or lo): 32 token rows, swizzled like B
   static constexpr int SWZ_BYTES = R * 2;  // B / H row bytes = swizzle span
   static constexpr uint32_t SWZ_MASK = R == 64 ? 0x70u : (R == 32 ? 0x30u : 0x10u);
   static constexpr uint32_t UMMA_LAYOUT = R == 64 ? 2u : (R == 32 ? 4u : 6u);
-  static constexpr int SMEM = OFF_END + 1024 + (TC ? 2 * HT : 0) + STAGES * STAGE;
+  static constexpr int DPITCH = 256 + 4;  // floats per row of the expand result tile Ds (bank-shifted rows)
+  static constexpr int DS = TC ? 32 * DPITCH * 4 : 0;
+  static constexpr int SMEM = OFF_END + DS + 1024 + (TC ? 2 * HT : 0) + STAGES * STAGE;
 };
 
 __device__ __forceinline__ DevSeg unpack_seg(int4 v0, int4 v1) {
@@ -161,7 +169,7 @@ struct Trace {
   __device__ unsigned long long before_wait() {
     if (!rec) return 0ull;
     const unsigned long long t = global_timer_ns();
-    if (units < kTraceUnits) rec[8 + 4 * units] = t;
+    if (units < kTraceUnits) rec[8 + kTraceMarks * units] = t;
     return t;
   }
   __device__ void after_wait(unsigned long long t0) {
@@ -169,12 +177,12 @@ struct Trace {
       const unsigned long long t = global_timer_ns();
       if (!t_first) t_first = t;
       waited += t - t0;
-      if (units < kTraceUnits) rec[8 + 4 * units + 1] = t;
+      if (units < kTraceUnits) rec[8 + kTraceMarks * units + 1] = t;
       ++units;
     }
   }
-  __device__ void mark(int k) {  // 2: compute done, 3: stage handed back
-    if (rec && units >= 1 && units <= kTraceUnits) rec[8 + 4 * (units - 1) + k] = global_timer_ns();
+  __device__ void mark(int k) {  // k = 2..5: phase marks of the latest stage
+    if (rec && units >= 1 && units <= kTraceUnits) rec[8 + kTraceMarks * (units - 1) + k] = global_timer_ns();
   }
   __device__ void finish() {
     if (rec) {
@@ -206,15 +214,21 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   int4* sdesc = reinterpret_cast<int4*>(smem + C::OFF_DESC);
   float* Ps = reinterpret_cast<float*>(smem + C::OFF_P);
   float* Hs = reinterpret_cast<float*>(smem + C::OFF_H);
-  uint64_t* mma_bar = reinterpret_cast<uint64_t*>(smem + 320);
+  // MMA warp <-> compute warps handoffs
+  uint64_t* sh_full = reinterpret_cast<uint64_t*>(smem + 264);  // shrink accumulator complete (commit)
+  uint64_t* sh_free = reinterpret_cast<uint64_t*>(smem + 272);  // shrink accumulator read (8 warps)
+  uint64_t* ht_full = reinterpret_cast<uint64_t*>(smem + 280);  // H tiles written (8 warps)
+  uint64_t* acc_full = reinterpret_cast<uint64_t*>(smem + 288);  // [2] expand accumulator complete (commit)
+  uint64_t* acc_free = reinterpret_cast<uint64_t*>(smem + 304);  // [2] expand accumulator read (8 warps)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + 336);
-  uint8_t* ht_base = align1024(smem + C::OFF_END);  // H hi / lo tiles (tcgen05 expand)
+  float* Ds = reinterpret_cast<float*>(smem + C::OFF_END);  // expand results of one stage (fp32)
+  uint8_t* ht_base = align1024(smem + C::OFF_END + C::DS);  // H hi / lo tiles (tcgen05 expand)
   uint8_t* stage_base = ht_base + (C::TC ? 2 * C::HT : 0);
 
   const int tid = threadIdx.x;
   const int warp = tid >> 5;
   const int lane = tid & 31;
-  const bool producer = warp == kComputeWarps;
+  const bool producer = warp == kProducerWarp;
   const uint32_t q = cluster_ctarank();
   const uint32_t CL = cluster_nctarank();
   const int cid = static_cast<int>(cluster_id_x());
@@ -228,7 +242,13 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       mbar_init(&empty[s], 1);
     }
     mbar_init(cbar, CL);
-    mbar_init(mma_bar, 1);
+    mbar_init(sh_full, 1);
+    mbar_init(sh_free, kComputeWarps);
+    mbar_init(ht_full, kComputeWarps);
+    for (int b = 0; b < 2; ++b) {
+      mbar_init(&acc_full[b], 1);
+      mbar_init(&acc_free[b], kComputeWarps);
+    }
     *s_bad = 0;
     *s_issued = 0;
     fence_mbar_init();
@@ -242,9 +262,10 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       for (int i = 0; i < 3; ++i) prefetch_tmap(&a.tmap_y[i]);
     if ((a.mode & kModeExpand) && C::TC && !a.registry) prefetch_tmap(&a.tmap_b);
   }
-  // TMEM: shrink accumulator (32 columns) + two expand accumulators (32 each)
+  // TMEM: shrink accumulator (columns 0-31) and two expand accumulators of two
+  // 128 x 32 halves each (columns 64-127 and 128-191)
   const bool use_tmem = (a.mode & kModeShrink) || (C::TC && (a.mode & kModeExpand));
-  if (use_tmem && warp == 0) tmem_alloc(s_tmem, 128);
+  if (use_tmem && warp == 0) tmem_alloc(s_tmem, 256);
   if (use_tmem) tc_fence_before();
   __syncthreads();
   if (use_tmem) tc_fence_after();
@@ -282,8 +303,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     read_table();
   }
   const int total = nmine * ups;
+  const uint32_t tbase = use_tmem ? *s_tmem : 0u;
+  const uint32_t t_sh = tbase;
+  constexpr uint32_t kAbf = E::is_bf16 ? 1u : 0u;
 
-  if (producer) {
+  if (warp == kProducerWarp) {
     // ======================= producer warp ===================================
     if (lane == 0) {
       // parts: 1 = arm the stage's barrier and load the weights, 2 = load the activations
@@ -359,7 +383,106 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     return;
   }
 
-  // ========================= compute warps ===================================
+  if (warp == kMmaWarp) {
+    // ========================= MMA warp ======================================
+    if (a.prefetch_weights) {
+      pdl_wait_prior();
+      pdl_launch_dependents();
+    }
+    if (lane != 0) return;
+    int u = 0;
+    uint32_t sh_uses = 0, ht_uses = 0, acc_uses[2] = {0u, 0u};
+    int ebuf = 0;
+    auto wait_ok = [&](uint64_t* bar, uint32_t parity) -> bool {
+      if (*s_bad) return false;
+      const bool ok = mbar_wait_bounded(bar, parity, a.err);
+      if (!ok) *s_bad = 1;
+      return ok;
+    };
+    for (int sj = 0; sj < nmine; ++sj) {
+      const DevSeg s = desc(sj);
+      const int n = clamp_rows(s.token_count);
+      if (do_sh) {
+        // shrink: D[rank, t] (TMEM) += A_box[rank, k] . x_box[t, k]^T, M = 64
+        // (rows past r read neighbouring shared memory and are never used),
+        // N = the segment's tokens rounded up to 8, K = 16 per instruction.
+        // Each stage's commit frees it for the producer.
+        const bool have = nA > 0 && n > 0;
+        if (have && sh_uses > 0) wait_ok(sh_free, (sh_uses - 1) & 1);
+        const uint32_t Nsh = static_cast<uint32_t>(max(8, (n + 7) & ~7));
+        const uint32_t idesc = umma_idesc(kAbf, 64, Nsh);
+        for (int i = 0; i < nA; ++i, ++u) {
+          const int stage = u % S;
+          const bool ok = wait_ok(&full[stage], (u / S) & 1);
+          if (ok && have) {
+            tc_fence_after();
+            const uint32_t st = smem_u32(stage_base + stage * C::STAGE);
+            // descriptors step through the stage by adding (byte offset >> 4)
+            // to their start-address field
+            const uint64_t da = umma_desc(st, 1024, 2), dx = umma_desc(st + 4 * C::ABOX, 1024, 2);
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+              for (int ks = 0; ks < 4; ++ks)
+                umma_f16(t_sh, da + static_cast<uint64_t>((j * C::ABOX + ks * 32) >> 4),
+                         dx + static_cast<uint64_t>((j * C::XBOX + ks * 32) >> 4), idesc,
+                         (i > 0 || j > 0 || ks > 0) ? 1u : 0u);
+            umma_commit(&empty[stage]);  // the stage is free once these MMAs have read it
+          } else {
+            mbar_arrive(&empty[stage]);
+          }
+        }
+        if (have) {
+          if (!*s_bad) umma_commit(sh_full);
+          ++sh_uses;
+        }
+      }
+      if constexpr (C::TC) {
+        if (do_ex && nB > 0) {
+          // expand: D[o, t] (TMEM) = B[o, :] . H_hi[t, :]^T + B[o, :] . H_lo[t, :]^T,
+          // two MMAs of M = 128 output columns per stage, N = 16 or 32 tokens, K = r
+          const bool go = n > 0;
+          if (go) {
+            wait_ok(ht_full, ht_uses & 1);
+            ++ht_uses;
+          }
+          const uint32_t N = n > 16 ? 32u : 16u;
+          const uint32_t idesc = umma_idesc(kAbf, 128, N);
+          const uint64_t dh = umma_desc(smem_u32(ht_base), 16 * R, C::UMMA_LAYOUT);
+          const uint64_t dl = umma_desc(smem_u32(ht_base) + C::HT, 16 * R, C::UMMA_LAYOUT);
+          for (int i = 0; i < nB; ++i, ++u) {
+            if (!go) continue;
+            const int stage = u % S;
+            const int b = ebuf;
+            ebuf ^= 1;
+            wait_ok(&full[stage], (u / S) & 1);
+            if (acc_uses[b] > 0) wait_ok(&acc_free[b], (acc_uses[b] - 1) & 1);
+            ++acc_uses[b];
+            if (*s_bad) continue;
+            tc_fence_after();
+            const uint32_t bsm = smem_u32(stage_base + stage * C::STAGE + 4 * C::XBOX);
+#pragma unroll
+            for (int hh = 0; hh < 2; ++hh) {
+              const uint32_t acc = tbase + 64 + 64 * b + 32 * hh;
+              const uint64_t db = umma_desc(bsm + hh * 128 * R * 2, 16 * R, C::UMMA_LAYOUT);
+#pragma unroll
+              for (int ks = 0; ks < R / 16; ++ks) umma_f16(acc, db + 2 * ks, dh + 2 * ks, idesc, ks > 0 ? 1u : 0u);
+#pragma unroll
+              for (int ks = 0; ks < R / 16; ++ks) umma_f16(acc, db + 2 * ks, dl + 2 * ks, idesc, 1u);
+            }
+            umma_commit(&acc_full[b]);
+          }
+        } else {
+          u += nB;
+        }
+      } else {
+        u += nB;
+      }
+    }
+    return;
+  }
+
+  // ======================== epilogue / compute warps ===========================
   if (a.prefetch_weights) {
     pdl_wait_prior();
     pdl_launch_dependents();
@@ -369,29 +492,23 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const int c = lane & 3;
   const int quarter = warp & 3;  // TMEM lane quarter this warp may read
   const int half = warp >> 2;
-  int kc = 0;  // next stage-unit to consume
+  int kc = 0;  // next stage-unit
   uint32_t cph = 0;  // cluster barrier phase
-  uint32_t mph = 0;  // MMA completion barrier phase
-  const uint32_t tbase = use_tmem ? *s_tmem : 0u;
-  const uint32_t t_sh = tbase;  // shrink accumulator: 128 lanes x 32 columns
-  const uint32_t t_ex = tbase + 32;  // expand accumulators: 2 x (128 lanes x 32 columns)
-  constexpr uint32_t kAbf = E::is_bf16 ? 1u : 0u;
-
-  // Wait for stage `kc` (calling threads only); false after an error.
+  uint32_t sh_ph = 0, acc_ph[2] = {0u, 0u};
+  int ebuf = 0;
+  auto wait_ok = [&](uint64_t* bar, uint32_t parity) -> bool {
+    if (*s_bad) return false;
+    const bool ok = mbar_wait_bounded(bar, parity, a.err);
+    if (!ok) *s_bad = 1;
+    return ok;
+  };
+  // Wait for stage `kc` (calling threads only), with the optional trace.
   auto wait_full = [&](int stage) -> bool {
     if (*s_bad) return false;
     const unsigned long long tw = tr.before_wait();
     const bool ok = mbar_wait_bounded(&full[stage], (kc / S) & 1, a.err);
     tr.after_wait(tw);
     if (!ok) *s_bad = 1;
-    return ok;
-  };
-  // Wait for the MMAs committed to mma_bar (all compute threads).
-  auto wait_mma = [&]() -> bool {
-    bool ok = !*s_bad && mbar_wait_bounded(mma_bar, mph, a.err);
-    mph ^= 1u;
-    if (!ok) *s_bad = 1;
-    tc_fence_after();
     return ok;
   };
 
@@ -402,43 +519,16 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     const float alpha = a.registry ? s.alpha : a.scale;
 
     if (do_sh) {
-      // ---- 1. partial shrink over this CTA's slice of d on tcgen05 -----------
-      // D[rank, t] (TMEM) += A_box[rank, k] . x_box[t, k]^T: M = 128 (rows past
-      // r read neighbouring shared memory and are never used), N = 16 or 32
-      // tokens, K = 16 per instruction. Thread 0 issues; the commit frees the
-      // stage for the producer, so no other thread takes part per stage.
-      const uint32_t Nsh = n > 16 ? 32u : 16u;
-      const uint32_t idesc = umma_idesc(kAbf, 128, Nsh);
-      if (tid == 0) {
-        for (int i = 0; i < nA; ++i, ++kc) {
-          const int stage = kc % S;
-          const bool ok = wait_full(stage);
-          if (ok && n > 0) {
-            tc_fence_after();
-            const uint32_t st = smem_u32(stage_base + stage * C::STAGE);
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-              for (int ks = 0; ks < 4; ++ks)
-                umma_f16(t_sh, umma_desc(st + j * C::ABOX + ks * 32, 1024, 2),
-                         umma_desc(st + 4 * C::ABOX + j * C::XBOX + ks * 32, 1024, 2), idesc,
-                         (i > 0 || j > 0 || ks > 0) ? 1u : 0u);
-            umma_commit(&empty[stage]);  // the stage is free once these MMAs have read it
-          } else {
-            mbar_arrive(&empty[stage]);
-          }
-        }
-        if (nA > 0 && n > 0 && !*s_bad) umma_commit(mma_bar);
-      } else {
-        kc += nA;
-      }
-      // partial tile -> Ps[token][rank] (zeros when this CTA owns no slice of d)
+      kc += nA;  // shrink stages are consumed by the MMA warp
+      // ---- 1. partial tile -> Ps[token][rank] (zeros when this CTA owns no slice of d)
       const bool have = nA > 0 && n > 0;
       if (have) {
-        named_sync(kBarCompute, kComputeThreads);  // thread 0 has committed
-        wait_mma();
+        wait_ok(sh_full, sh_ph);
+        sh_ph ^= 1u;
+        tc_fence_after();
       }
-      if (half == 0 && quarter * 32 < R) {
+      // M = 64 accumulator layout: rank r sits in TMEM lane (r % 16) + 32 * (r / 16)
+      if (half == 0 && quarter * 16 < R) {
         float v[32];
         // warp-uniform: the tcgen05 loads are .sync.aligned
         if (__shfl_sync(0xffffffffu, (have && !*s_bad) ? 1 : 0, 0)) {
@@ -449,13 +539,17 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
 #pragma unroll
           for (int j = 0; j < 32; ++j) v[j] = 0.f;
         }
-        const int r = quarter * 32 + lane;
-        if (r < R) {
+        const int r = quarter * 16 + lane;
+        if (lane < 16 && r < R) {
 #pragma unroll
           for (int j = 0; j < 32; ++j) Ps[j * PITCH + r] = v[j];
         }
       }
-      tc_fence_before();
+      if (have) {
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(sh_free);  // the MMA warp may start the next shrink
+      }
       tr.mark(2);
       // ---- 2. reduce-scatter + all-gather of the partials over the cluster
       if (!cluster_barrier_bounded(cbar, cph, CL, kBarCompute, kComputeThreads, a.err)) *s_bad = 1;
@@ -501,95 +595,94 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     T* yg = static_cast<T*>(a.y);
 
     if constexpr (C::TC) {
-      // ---- 3. expand over this CTA's slice of o on tcgen05 -------------------
-      // D[o, t] (TMEM, fp32) = B[o, :] . H_hi[t, :]^T + B[o, :] . H_lo[t, :]^T
-      // with M = 128 output columns per MMA, N = 16 or 32 tokens, K = r.
-      const int N = n > 16 ? 32 : 16;
-      for (int e = tid; e < N * (R / 2); e += kComputeThreads) {
-        const int row = e / (R / 2);
-        const int k = (e % (R / 2)) * 2;
-        float2 v = make_float2(0.f, 0.f);
-        if (row < n) v = *reinterpret_cast<const float2*>(Hs + row * PITCH + k);
-        const uint32_t hv = E::pack2(v.x, v.y);
-        const float2 r2 = E::unpack2(hv);
-        const uint32_t lv = E::pack2(v.x - r2.x, v.y - r2.y);
-        uint32_t lin = static_cast<uint32_t>(row * C::SWZ_BYTES + k * 2);
-        lin ^= (lin >> 3) & C::SWZ_MASK;
-        *reinterpret_cast<uint32_t*>(ht_base + lin) = hv;
-        *reinterpret_cast<uint32_t*>(ht_base + C::HT + lin) = lv;
+      // ---- 3. expand epilogue: TMEM accumulators (issued by the MMA warp) + y -> y
+      const bool go = n > 0;
+      if (go) {
+        // H tiles (16-bit high part + residual), rows = tokens, swizzled like B
+        const int N = n > 16 ? 32 : 16;
+        for (int e = tid; e < N * (R / 2); e += kComputeThreads) {
+          const int j = e / (R / 2);
+          const int k = (e % (R / 2)) * 2;
+          float2 v = make_float2(0.f, 0.f);
+          if (j < n) v = *reinterpret_cast<const float2*>(Hs + j * PITCH + k);
+          const uint32_t hv = E::pack2(v.x, v.y);
+          const float2 r2 = E::unpack2(hv);
+          const uint32_t lv = E::pack2(v.x - r2.x, v.y - r2.y);
+          uint32_t lin = static_cast<uint32_t>(j * C::SWZ_BYTES + k * 2);
+          lin ^= (lin >> 3) & C::SWZ_MASK;
+          *reinterpret_cast<uint32_t*>(ht_base + lin) = hv;
+          *reinterpret_cast<uint32_t*>(ht_base + C::HT + lin) = lv;
+        }
+        fence_proxy_async_smem();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(ht_full);
       }
-      fence_proxy_async_smem();
-      const uint32_t idesc = umma_idesc(kAbf, 128, static_cast<uint32_t>(N));
+      const int ol = half * 128 + quarter * 32 + lane;  // this lane's output column in the stage
       for (int i = 0; i < nB; ++i, ++kc) {
         const int stage = kc % S;
-        wait_full(stage);
-        tc_fence_before();
-        named_sync(kBarCompute, kComputeThreads);  // stage seen, H tiles written, TMEM free
-        // warp-uniform: the tcgen05 loads below are .sync.aligned
-        const bool go = __shfl_sync(0xffffffffu, (!*s_bad && n > 0) ? 1 : 0, 0) != 0;
-        uint8_t* st = stage_base + stage * C::STAGE;
+        wait_full(stage);  // y box of the stage
+        const uint8_t* st = stage_base + stage * C::STAGE;
         const int oc = oB0 + i * C::W;
         const int wc = min(C::W, a.o - oc);
-        if (go && tid == 0) {
-          tc_fence_after();
-          const uint32_t hhi = smem_u32(ht_base), hlo = hhi + C::HT;
-#pragma unroll
-          for (int hh = 0; hh < 2; ++hh) {
-            const uint32_t bsm = smem_u32(st + 4 * C::XBOX + hh * 128 * R * 2);
-#pragma unroll
-            for (int ks = 0; ks < R / 16; ++ks)
-              umma_f16(t_ex + hh * 32, umma_desc(bsm + ks * 32, 16 * R, C::UMMA_LAYOUT),
-                       umma_desc(hhi + ks * 32, 16 * R, C::UMMA_LAYOUT), idesc, ks > 0 ? 1u : 0u);
-#pragma unroll
-            for (int ks = 0; ks < R / 16; ++ks)
-              umma_f16(t_ex + hh * 32, umma_desc(bsm + ks * 32, 16 * R, C::UMMA_LAYOUT),
-                       umma_desc(hlo + ks * 32, 16 * R, C::UMMA_LAYOUT), idesc, 1u);
-          }
-          umma_commit(mma_bar);
-        }
         if (go) {
-          wait_mma();
-          // this lane: output column ol of the stage, every token of the segment
-          const int ol = half * 128 + quarter * 32 + lane;
-          const uint32_t ta = t_ex + (static_cast<uint32_t>(quarter * 32) << 16) + half * 32;
+          const int b = ebuf;
+          ebuf ^= 1;
+          const bool ok = wait_ok(&acc_full[b], acc_ph[b]);
+          acc_ph[b] ^= 1u;
+          tc_fence_after();
           float v[32];
-          tmem_ld16(ta, *reinterpret_cast<float(*)[16]>(v));
-          if (N > 16) tmem_ld16(ta + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-          tr.mark(2);
-          if (a.y_tma) {
-            // y from the stage (swizzled boxes) -> registers; results -> the
-            // same region, linear rows of 256 columns; one bulk store per row
-            float yv[32];
-            const uint8_t* yb = st + (ol >> 6) * C::XBOX;
-            const int cl = ol & 63;
-#pragma unroll
-            for (int j = 0; j < 32; ++j) yv[j] = j < n ? E::to_f(*reinterpret_cast<const T*>(yb + sw128(j, cl))) : 0.f;
-            named_sync(kBarCompute, kComputeThreads);  // every y read is done
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < n) *reinterpret_cast<T*>(st + j * (C::W * 2) + ol * 2) = E::from_f(yv[j] + v[j]);
-            named_sync(kBarCompute, kComputeThreads);
-            // rows -> global with 16-byte stores (wc is a multiple of 8)
-            T* y0 = yg + static_cast<int64_t>(s.token_start) * a.y_ld + a.y_off + oc;
-            const int vec_per_row = wc / 8;
-            for (int e = tid; e < n * vec_per_row; e += kComputeThreads) {
-              const int j = e / vec_per_row, cv = e % vec_per_row;
-              *reinterpret_cast<int4*>(y0 + static_cast<int64_t>(j) * a.y_ld + cv * 8) =
-                  *reinterpret_cast<const int4*>(st + j * (C::W * 2) + cv * 16);
-            }
-          } else if (ol < wc) {
-            T* yc = yg + static_cast<int64_t>(s.token_start) * a.y_ld + a.y_off + oc + ol;
-            float yv[32];
-#pragma unroll
-            for (int j = 0; j < 32; ++j) yv[j] = j < n ? E::to_f(yc[static_cast<int64_t>(j) * a.y_ld]) : 0.f;
-#pragma unroll
-            for (int j = 0; j < 32; ++j)
-              if (j < n) yc[static_cast<int64_t>(j) * a.y_ld] = E::from_f(yv[j] + v[j]);
+          if (__shfl_sync(0xffffffffu, (ok && !*s_bad) ? 1 : 0, 0)) {
+            const uint32_t ta = tbase + 64 + 64 * b + 32 * half + (static_cast<uint32_t>(quarter * 32) << 16);
+            tmem_ld16(ta, *reinterpret_cast<float(*)[16]>(v));
+            if (n > 16) tmem_ld16(ta + 16, *reinterpret_cast<float(*)[16]>(v + 16));
           }
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(&acc_free[b]);  // the MMA warp may reuse this accumulator
+          tr.mark(2);
+          // phase A: D column of this lane -> Ds[token][column]
+          if (ol < wc) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j)
+              if (j < n) Ds[j * C::DPITCH + ol] = v[j];
+          }
+          named_sync(kBarCompute, kComputeThreads);
+          tr.mark(3);
+          // phase B: every compute thread takes (token, 8-column chunk) pairs
+          const int nch = wc >> 3;
+          for (int e = tid; e < n * nch; e += kComputeThreads) {
+            const int t = e / nch;
+            const int col = (e - t * nch) * 8;
+            const float* dr = Ds + t * C::DPITCH + col;
+            const float4 d0 = reinterpret_cast<const float4*>(dr)[0];
+            const float4 d1 = reinterpret_cast<const float4*>(dr)[1];
+            const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+            T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + a.y_off + oc + col;
+            if (a.y_tma) {
+              const int cib = (col & 63) >> 3;  // 16-byte chunk inside the 128-byte box row
+              const int4 yv =
+                  *reinterpret_cast<const int4*>(st + (col >> 6) * C::XBOX + t * 128 + ((cib ^ (t & 7)) << 4));
+              const uint32_t* yw = reinterpret_cast<const uint32_t*>(&yv);
+              int4 out;
+              uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
+#pragma unroll
+              for (int p2 = 0; p2 < 4; ++p2) {
+                const float2 f = E::unpack2(yw[p2]);
+                ow[p2] = E::pack2(f.x + dv[2 * p2], f.y + dv[2 * p2 + 1]);
+              }
+              *reinterpret_cast<int4*>(yp) = out;
+            } else {
+              float yv[8];
+#pragma unroll
+              for (int x = 0; x < 8; ++x) yv[x] = E::to_f(yp[x]);
+#pragma unroll
+              for (int x = 0; x < 8; ++x) yp[x] = E::from_f(yv[x] + dv[x]);
+            }
+          }
+          tr.mark(4);
         }
         named_sync(kBarCompute, kComputeThreads);
         if (tid == 0) mbar_arrive(&empty[stage]);
-        tr.mark(3);
       }
     } else {
       // ---- 3. expand (rank 8) over this CTA's slice of o with mma.sync -------
@@ -695,7 +788,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     named_sync(kBarCompute, kComputeThreads);
     if (tid == 0) {
       const int issued = *s_issued;
-      for (int u = kc; u < issued; ++u) mbar_wait_bounded(&full[u % S], (u / S) & 1, nullptr, kDrainNs);
+      for (int u = max(0, issued - S); u < issued; ++u) mbar_wait_bounded(&full[u % S], (u / S) & 1, nullptr, kDrainNs);
     }
   }
   if (use_tmem) {
@@ -703,7 +796,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     named_sync(kBarCompute, kComputeThreads);  // every TMEM read and MMA is done
     if (warp == 0) {
       tc_fence_after();
-      tmem_dealloc(*s_tmem, 128);
+      tmem_dealloc(*s_tmem, 256);
     }
   }
   tr.finish();

@@ -72,10 +72,12 @@ struct ApplyArgs {
 // Per-CTA trace record (globaltimer ns): start, after the dependency wait,
 // first stage ready, end, stages consumed, ns consumers spent waiting for
 // stages, ns the producer spent waiting for free stages, 0; then, for the
-// first kTraceUnits stages, 4 timestamps each: before the stage wait, after
-// it, after the compute, after the stage was handed back.
+// first kTraceUnits stages, 6 timestamps each: before the stage wait, after
+// it, then four phase marks (for an expand stage: MMA done, results in shared
+// memory, after the barrier, results stored).
 constexpr int kTraceUnits = 16;
-constexpr int kTraceSlots = 8 + 4 * kTraceUnits;
+constexpr int kTraceMarks = 6;
+constexpr int kTraceSlots = 8 + kTraceMarks * kTraceUnits;
 
 struct LaunchCfg {
   int grid;
