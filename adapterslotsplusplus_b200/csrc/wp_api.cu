@@ -13,6 +13,7 @@
 #include <algorithm>
 #include <cstdarg>
 #include <cstdio>
+#include <cstdlib>
 #include <cstring>
 #include <string>
 #include <unordered_map>
@@ -701,6 +702,12 @@ void apply_plan(wp_handle* h, int dtype, int r, int* cluster, int* grid) {
         pick = i;
         break;
       }
+    // tuning override: WP_CLUSTER=1|2|4|8 forces the cluster size (when schedulable)
+    if (const char* env = std::getenv("WP_CLUSTER")) {
+      const int want = std::atoi(env);
+      for (int i = 0; i < 4; ++i)
+        if (sizes[i] == want && g[i] > 0) pick = i;
+    }
     h->plan_cluster[key] = sizes[pick];
     h->plan_grid[key] = std::max(g[pick], sizes[pick]);
   }

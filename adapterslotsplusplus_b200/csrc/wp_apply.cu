@@ -648,35 +648,35 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           }
           named_sync(kBarCompute, kComputeThreads);
           tr.mark(3);
-          // phase B: every compute thread takes (token, 8-column chunk) pairs
-          const int nch = wc >> 3;
-          for (int e = tid; e < n * nch; e += kComputeThreads) {
-            const int t = e / nch;
-            const int col = (e - t * nch) * 8;
-            const float* dr = Ds + t * C::DPITCH + col;
-            const float4 d0 = reinterpret_cast<const float4*>(dr)[0];
-            const float4 d1 = reinterpret_cast<const float4*>(dr)[1];
-            const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-            T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + a.y_off + oc + col;
-            if (a.y_tma) {
-              const int cib = (col & 63) >> 3;  // 16-byte chunk inside the 128-byte box row
-              const int4 yv =
-                  *reinterpret_cast<const int4*>(st + (col >> 6) * C::XBOX + t * 128 + ((cib ^ (t & 7)) << 4));
-              const uint32_t* yw = reinterpret_cast<const uint32_t*>(&yv);
-              int4 out;
-              uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
+          // phase B: warp w takes tokens w, w + 8, ...; lane l the 8-column chunk l
+          const int col = lane * 8;
+          if (col < wc) {
+            const int cib = lane & 7;  // 16-byte chunk inside the 128-byte box row
+            const uint8_t* yb = st + (lane >> 3) * C::XBOX;
+            for (int t = warp; t < n; t += kComputeWarps) {
+              const float* dr = Ds + t * C::DPITCH + col;
+              const float4 d0 = reinterpret_cast<const float4*>(dr)[0];
+              const float4 d1 = reinterpret_cast<const float4*>(dr)[1];
+              const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
+              T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + a.y_off + oc + col;
+              if (a.y_tma) {
+                const int4 yv = *reinterpret_cast<const int4*>(yb + t * 128 + ((cib ^ (t & 7)) << 4));
+                const uint32_t* yw = reinterpret_cast<const uint32_t*>(&yv);
+                int4 out;
+                uint32_t* ow = reinterpret_cast<uint32_t*>(&out);
 #pragma unroll
-              for (int p2 = 0; p2 < 4; ++p2) {
-                const float2 f = E::unpack2(yw[p2]);
-                ow[p2] = E::pack2(f.x + dv[2 * p2], f.y + dv[2 * p2 + 1]);
+                for (int p2 = 0; p2 < 4; ++p2) {
+                  const float2 f = E::unpack2(yw[p2]);
+                  ow[p2] = E::pack2(f.x + dv[2 * p2], f.y + dv[2 * p2 + 1]);
+                }
+                *reinterpret_cast<int4*>(yp) = out;
+              } else {
+                float yv[8];
+#pragma unroll
+                for (int x = 0; x < 8; ++x) yv[x] = E::to_f(yp[x]);
+#pragma unroll
+                for (int x = 0; x < 8; ++x) yp[x] = E::from_f(yv[x] + dv[x]);
               }
-              *reinterpret_cast<int4*>(yp) = out;
-            } else {
-              float yv[8];
-#pragma unroll
-              for (int x = 0; x < 8; ++x) yv[x] = E::to_f(yp[x]);
-#pragma unroll
-              for (int x = 0; x < 8; ++x) yp[x] = E::from_f(yv[x] + dv[x]);
             }
           }
           tr.mark(4);
