@@ -88,8 +88,9 @@ struct wp_handle {
   uint64_t generation = 0;
 
   // apply kernel plan per (dtype, rank): cluster size and persistent grid
-  int plan_cluster[8] = {0, 0, 0, 0, 0, 0, 0, 0};
-  int plan_grid[8] = {0, 0, 0, 0, 0, 0, 0, 0};
+  // launch plans per (variant, dtype, rank)
+  int plan_cluster[16] = {};
+  int plan_grid[16] = {};
   // optional per-CTA phase traces of the latest launch (0: fused/shrink, 1: expand-only)
   unsigned long long* d_trace[2] = {nullptr, nullptr};
   bool trace_on = false;
@@ -163,8 +164,8 @@ bool encode_map(CUtensorMap* m, int dtype, int rank, const void* base, const uin
                 CUtensorMapSwizzle swizzle = CU_TENSOR_MAP_SWIZZLE_128B) {
   auto fn = encode_fn();
   if (!fn) return false;
-  cuuint64_t gd[3], gs[2];
-  cuuint32_t bx[3], es[3] = {1, 1, 1};
+  cuuint64_t gd[4], gs[3];
+  cuuint32_t bx[4], es[4] = {1, 1, 1, 1};
   for (int i = 0; i < rank; ++i) {
     gd[i] = dims[i];
     bx[i] = box[i];
@@ -178,7 +179,20 @@ bool encode_map(CUtensorMap* m, int dtype, int rank, const void* base, const uin
 }
 
 // A stack [L, r, d] (row stride d, adapter stride `stride0` elements): box 64 x r x 1.
+// d (A, x) or o (y) allows the sliced view [cols / 64][64] of a row.
+bool sliced(int cols) { return cols % wp::kBoxCols == 0; }
+
+// A stack [L, r, d]: sliced view [L][d / 64][r][64] with box {64, r, 4, 1}
+// (4 slices of one stage, one instruction), else box {64, r, 1}.
 bool encode_a_map(CUtensorMap* m, int dtype, const void* base, int d, int r, int64_t L, int64_t stride0) {
+  if (sliced(d)) {
+    const uint64_t dims[4] = {static_cast<uint64_t>(wp::kBoxCols), static_cast<uint64_t>(r),
+                              static_cast<uint64_t>(d / wp::kBoxCols), static_cast<uint64_t>(L)};
+    const uint64_t strides[3] = {static_cast<uint64_t>(d) * 2, static_cast<uint64_t>(wp::kBoxCols) * 2,
+                                 static_cast<uint64_t>(stride0) * 2};
+    const uint32_t box[4] = {static_cast<uint32_t>(wp::kBoxCols), static_cast<uint32_t>(r), 4, 1};
+    return encode_map(m, dtype, 4, base, dims, strides, box);
+  }
   const uint64_t dims[3] = {static_cast<uint64_t>(d), static_cast<uint64_t>(r), static_cast<uint64_t>(L)};
   const uint64_t strides[2] = {static_cast<uint64_t>(d) * 2, static_cast<uint64_t>(stride0) * 2};
   const uint32_t box[3] = {static_cast<uint32_t>(wp::kBoxCols), static_cast<uint32_t>(r), 1};
@@ -190,14 +204,23 @@ bool encode_a_map(CUtensorMap* m, int dtype, const void* base, int d, int r, int
 bool encode_b_map(CUtensorMap* m, int dtype, const void* base, int o, int r, int64_t L, int64_t stride0) {
   const uint64_t dims[3] = {static_cast<uint64_t>(r), static_cast<uint64_t>(o), static_cast<uint64_t>(L)};
   const uint64_t strides[2] = {static_cast<uint64_t>(r) * 2, static_cast<uint64_t>(stride0) * 2};
-  const uint32_t box[3] = {static_cast<uint32_t>(r), 128, 1};
+  const uint32_t box[3] = {static_cast<uint32_t>(r), 256, 1};
   const CUtensorMapSwizzle sw =
       r == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : (r == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
   return encode_map(m, dtype, 3, base, dims, strides, box, sw);
 }
 
 // Activation rows [T, cols] with row stride ld elements: box 64 x box_rows.
+// Rows of x or y ([T, cols], leading dimension ld): sliced view
+// [cols / 64][T][64] with box {64, box_rows, 4}, else box {64, box_rows}.
 bool encode_rows_map(CUtensorMap* m, int dtype, const void* base, int cols, int T, int64_t ld, int box_rows) {
+  if (sliced(cols)) {
+    const uint64_t dims[3] = {static_cast<uint64_t>(wp::kBoxCols), static_cast<uint64_t>(T),
+                              static_cast<uint64_t>(cols / wp::kBoxCols)};
+    const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(wp::kBoxCols) * 2};
+    const uint32_t box[3] = {static_cast<uint32_t>(wp::kBoxCols), static_cast<uint32_t>(box_rows), 4};
+    return encode_map(m, dtype, 3, base, dims, strides, box);
+  }
   const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(T)};
   const uint64_t strides[1] = {static_cast<uint64_t>(ld) * 2};
   const uint32_t box[2] = {static_cast<uint32_t>(wp::kBoxCols), static_cast<uint32_t>(box_rows)};
@@ -686,13 +709,13 @@ namespace {
 // Cluster size and persistent grid of the apply kernel for (dtype, rank):
 // the largest cluster whose co-resident grid keeps at least 95% of the CTAs
 // that the best cluster size achieves (cached per handle).
-void apply_plan(wp_handle* h, int dtype, int r, int* cluster, int* grid) {
-  const int key = (dtype == WP_DTYPE_BF16 ? 4 : 0) + (r == 8 ? 0 : r == 16 ? 1 : r == 32 ? 2 : 3);
+void apply_plan(wp_handle* h, int dtype, int r, bool dec, int* cluster, int* grid) {
+  const int key = (dec ? 8 : 0) + (dtype == WP_DTYPE_BF16 ? 4 : 0) + (r == 8 ? 0 : r == 16 ? 1 : r == 32 ? 2 : 3);
   if (h->plan_grid[key] == 0) {
     const int sizes[4] = {8, 4, 2, 1};
     int g[4], best = 0;
     for (int i = 0; i < 4; ++i) {
-      g[i] = wp::apply_max_grid(dtype, r, sizes[i]);
+      g[i] = wp::apply_max_grid(dtype, r, sizes[i], dec);
       if (h->cfg.ctas_per_sm > 0) g[i] = std::min(g[i], h->num_sms * h->cfg.ctas_per_sm / sizes[i] * sizes[i]);
       best = std::max(best, g[i]);
     }
@@ -717,6 +740,16 @@ void apply_plan(wp_handle* h, int dtype, int r, int* cluster, int* grid) {
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
+// Kernel variant: the decode kernel (mma.sync) unless WP_KERNEL=tc selects
+// the tcgen05 kernel.
+bool use_decode_kernel() {
+  static const bool dec = [] {
+    const char* env = std::getenv("WP_KERNEL");
+    return !(env && std::strcmp(env, "tc") == 0);
+  }();
+  return dec;
+}
+
 // One apply launch. mode: wp::kModeShrink / kModeExpand / kModeFused.
 int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int* nseg, int T, int r, int dtype,
              const void* x, int64_t x_ld, int d, const void* wa, int64_t wa_stride, int64_t num_adapters, float scale,
@@ -734,6 +767,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   a.trace = h->trace_on ? h->d_trace[mode == wp::kModeExpand ? 1 : 0] : nullptr;
   if (mode & wp::kModeShrink) {
     a.d = d;
+    a.d_sliced = sliced(d) ? 1 : 0;
     for (int i = 0; i < 3; ++i)
       if (!encode_rows_map(&a.tmap_x[i], dtype, x, d, T, x_ld, 8 << i))
         return fail(h, WP_ERR_CUDA, "apply: cuTensorMapEncodeTiled(x) failed");
@@ -748,6 +782,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
     a.wb_base = wb;
     a.wb_stride = wb_stride;
     a.y_tma = al16(y) && (y_ld % 8 == 0) && (y_off % 8 == 0);
+    a.o_sliced = sliced(o) ? 1 : 0;
     if (!registry && r >= 16 && !encode_b_map(&a.tmap_b, dtype, wb, o, r, std::max<int64_t>(1, num_adapters), wb_stride))
       return fail(h, WP_ERR_CUDA, "apply: cuTensorMapEncodeTiled(wb_t_all) failed");
     for (int i = 0; a.y_tma && i < 3; ++i)
@@ -756,7 +791,8 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
         return fail(h, WP_ERR_CUDA, "apply: cuTensorMapEncodeTiled(y) failed");
   }
   int cluster = 1, grid = 1;
-  apply_plan(h, dtype, r, &cluster, &grid);
+  const bool dec = use_decode_kernel();
+  apply_plan(h, dtype, r, dec, &cluster, &grid);
   a.split_len = round_up((std::max(d, 1) + cluster - 1) / cluster, wp::kStageK);
   a.oslice = round_up((std::max(o, 1) + cluster - 1) / cluster, wp::kStageCols);
   const bool pdl = h->cfg.use_pdl != 0;
@@ -765,7 +801,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   // caller's promise (prefetch_weights) that the preceding kernel writes no
   // adapter weights, and a preceding kernel that is not the segmenter.
   a.prefetch_weights = !pdl || (h->cfg.prefetch_weights != 0 && !h->last_was_segmenter);
-  wp::LaunchCfg lc{grid, cluster, stream, pdl};
+  wp::LaunchCfg lc{grid, cluster, stream, pdl, dec};
   cudaError_t e = wp::launch_apply(dtype, r, a, lc);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "apply launch: %s", cudaGetErrorString(e));
   ++h->launches;
@@ -940,7 +976,7 @@ int wp_apply_plan(wp_handle* h, int32_t dtype, int32_t rank, int32_t* cluster, i
   if (!rank_ok(rank) || !dtype16(dtype)) return fail(h, WP_ERR_INVALID, "apply_plan: bad rank or dtype");
   DeviceGuard dg(h->device);
   int c = 0, g = 0;
-  apply_plan(h, dtype, rank, &c, &g);
+  apply_plan(h, dtype, rank, use_decode_kernel(), &c, &g);
   if (cluster) *cluster = c;
   if (grid) *grid = g;
   return WP_OK;

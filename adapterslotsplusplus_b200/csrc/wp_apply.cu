@@ -96,7 +96,12 @@ constexpr int kBarCompute = 1;  // named barrier of the compute warps
 constexpr int kDescCache = 64;  // segment descriptors cached per CTA
 constexpr unsigned long long kDrainNs = 10000000ull;  // 10 ms per stage when draining after an error
 
-template <int R>
+constexpr int kSmemMax = 232448;  // dynamic shared memory per CTA (227 KB)
+
+// DEC = true selects the decode variant: shrink and expand on warp-level
+// mma.sync in the compute warps (no tensor memory, no MMA warp); false selects
+// tcgen05 (shrink always, expand for ranks 16-64).
+template <int R, bool DEC>
 struct ApplyCfg {
   static constexpr int KC = kStageK;  // d elements per shrink stage (4 boxes)
   static constexpr int W = kStageCols;  // output columns per expand stage (4 boxes)
@@ -104,21 +109,32 @@ struct ApplyCfg {
   static constexpr int XBOX = 32 * 128;  // room for one 32-row x or y box
   static constexpr int STAGE = 4 * ABOX + 4 * XBOX;  // == 4 * XBOX + W * R * 2; multiple of 1024
   static_assert(STAGE == 4 * XBOX + W * R * 2, "shrink and expand stages have one size");
-  static constexpr int STAGES = R == 64 ? 2 : (R == 32 ? 5 : (R == 16 ? 7 : 8));
   static constexpr int PITCH = R + 4;  // floats per row of the P / H tiles
   static constexpr int OFF_FLAGS = 448;
   static constexpr int OFF_DESC = 512;
   static constexpr int OFF_P = OFF_DESC + kDescCache * 32;
   static constexpr int OFF_H = OFF_P + 32 * PITCH * 4;
   static constexpr int OFF_END = OFF_H + 32 * PITCH * 4;
-  static constexpr bool TC = R >= 16;  // expand on tcgen05 (K = r must be a multiple of 16)
+  static constexpr bool TC = !DEC && R >= 16;  // expand on tcgen05 (K = r must be a multiple of 16)
+  static constexpr bool BTMA = R >= 16;  // B as swizzled tensor boxes (rank 8: one linear bulk copy)
   static constexpr int HT = 32 * R * 2;  // one 16-bit H tile (hi or lo): 32 token rows, swizzled like B
   static constexpr int SWZ_BYTES = R * 2;  // B / H row bytes = swizzle span
   static constexpr uint32_t SWZ_MASK = R == 64 ? 0x70u : (R == 32 ? 0x30u : 0x10u);
   static constexpr uint32_t UMMA_LAYOUT = R == 64 ? 2u : (R == 32 ? 4u : 6u);
   static constexpr int DPITCH = 256 + 4;  // floats per row of the expand result tile Ds (bank-shifted rows)
   static constexpr int DS = TC ? 32 * DPITCH * 4 : 0;
-  static constexpr int SMEM = OFF_END + DS + 1024 + (TC ? 2 * HT : 0) + STAGES * STAGE;
+  // decode variant: shrink partials of 4 warps (32 tokens x PITCH floats each) for the cross-warp sum
+  static constexpr int PSLOT = 32 * PITCH;
+  static constexpr int PW = DEC ? 4 * PSLOT * 4 : 0;
+  // decode variant: receive slots of the cluster exchange, [2 segment parities][CLMAX ranks]
+  static constexpr int CLMAX = R == 64 ? 2 : 4;
+  static constexpr int RX = DEC ? 2 * CLMAX * PSLOT * 4 : 0;
+  static constexpr int FIXED = OFF_END + DS + PW + RX + 1024 + (TC ? 2 * HT : 0);
+  static constexpr int FIT = (kSmemMax - FIXED) / STAGE;
+  static constexpr int STAGES = DEC ? (FIT > 8 ? 8 : FIT) : (R == 64 ? 2 : (R == 32 ? 5 : (R == 16 ? 7 : 8)));
+  static constexpr int SMEM = FIXED + STAGES * STAGE;
+  static_assert(STAGES >= 2 && STAGES <= 8 && SMEM <= kSmemMax, "shared memory budget");
+  static_assert(32 * PITCH * 4 >= kComputeWarps * 128, "the P tile holds one scratch row per compute warp");
 };
 
 __device__ __forceinline__ DevSeg unpack_seg(int4 v0, int4 v1) {
@@ -154,6 +170,15 @@ __device__ __forceinline__ uint8_t* align1024(uint8_t* p) {
 
 // Optional phase trace (a.trace != nullptr), kept by thread 0 (compute) and by
 // the producer's lane 0 (its wait time only).
+__device__ __forceinline__ void trace_mark(unsigned long long* base, int k) {
+  if (base) base[blockIdx.x * kTraceSlots + 8 + k] = global_timer_ns();
+}
+// Mark k (6 or 7) of stage-unit u, written by the MMA or producer warp.
+__device__ __forceinline__ void trace_unit(unsigned long long* base, int u, int k) {
+  if (base && u >= 0 && u < kTraceUnits)
+    base[blockIdx.x * kTraceSlots + 8 + kTraceSegMarks + kTraceMarks * u + k] = global_timer_ns();
+}
+
 struct Trace {
   unsigned long long* rec = nullptr;
   unsigned long long t_start = 0, t_dep = 0, t_first = 0, waited = 0, units = 0;
@@ -169,7 +194,7 @@ struct Trace {
   __device__ unsigned long long before_wait() {
     if (!rec) return 0ull;
     const unsigned long long t = global_timer_ns();
-    if (units < kTraceUnits) rec[8 + kTraceMarks * units] = t;
+    if (units < kTraceUnits) rec[8 + kTraceSegMarks + kTraceMarks * units] = t;
     return t;
   }
   __device__ void after_wait(unsigned long long t0) {
@@ -177,12 +202,15 @@ struct Trace {
       const unsigned long long t = global_timer_ns();
       if (!t_first) t_first = t;
       waited += t - t0;
-      if (units < kTraceUnits) rec[8 + kTraceMarks * units + 1] = t;
+      if (units < kTraceUnits) rec[8 + kTraceSegMarks + kTraceMarks * units + 1] = t;
       ++units;
     }
   }
   __device__ void mark(int k) {  // k = 2..5: phase marks of the latest stage
-    if (rec && units >= 1 && units <= kTraceUnits) rec[8 + kTraceMarks * (units - 1) + k] = global_timer_ns();
+    if (rec && units >= 1 && units <= kTraceUnits) rec[8 + kTraceSegMarks + kTraceMarks * (units - 1) + k] = global_timer_ns();
+  }
+  __device__ void seg(int k, int sj) {  // marks of the first segment
+    if (rec && sj == 0) rec[8 + k] = global_timer_ns();
   }
   __device__ void finish() {
     if (rec) {
@@ -196,13 +224,11 @@ struct Trace {
   }
 };
 
-template <typename T, int R>
+template <typename T, int R, bool DEC>
 __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constant__ ApplyArgs a) {
-  using C = ApplyCfg<R>;
+  using C = ApplyCfg<R, DEC>;
   using E = Elem<T>;
   constexpr int S = C::STAGES;
-  constexpr int NTW = C::W / 8 / kComputeWarps;  // expand: n-tiles of 8 columns per warp
-  constexpr int KE = R >= 16 ? R / 16 : 1;  // expand: k-steps over the rank
   constexpr int PITCH = C::PITCH;
 
   extern __shared__ __align__(128) uint8_t smem[];
@@ -222,7 +248,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   uint64_t* acc_free = reinterpret_cast<uint64_t*>(smem + 304);  // [2] expand accumulator read (8 warps)
   uint32_t* s_tmem = reinterpret_cast<uint32_t*>(smem + 336);
   float* Ds = reinterpret_cast<float*>(smem + C::OFF_END);  // expand results of one stage (fp32)
-  uint8_t* ht_base = align1024(smem + C::OFF_END + C::DS);  // H hi / lo tiles (tcgen05 expand)
+  float* Pw = reinterpret_cast<float*>(smem + C::OFF_END + C::DS);  // decode: cross-warp shrink partials
+  float* Rx = reinterpret_cast<float*>(smem + C::OFF_END + C::DS + C::PW);  // decode: cluster receive slots
+  uint64_t* rx_full = reinterpret_cast<uint64_t*>(smem + 352);  // [2] all peers' partials landed (tx count)
+  uint64_t* rx_free = reinterpret_cast<uint64_t*>(smem + 368);  // [2] every peer has read my partial
+  uint64_t* ydone = reinterpret_cast<uint64_t*>(smem + 384);  // [S] decode: y box of the stage final (8 warps)
+  uint8_t* ht_base = align1024(smem + C::OFF_END + C::DS + C::PW + C::RX);  // H hi / lo tiles (tcgen05 expand)
   uint8_t* stage_base = ht_base + (C::TC ? 2 * C::HT : 0);
 
   const int tid = threadIdx.x;
@@ -239,7 +270,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
       mbar_init(&full[s], 1);
-      mbar_init(&empty[s], 1);
+      mbar_init(&empty[s], DEC ? kComputeWarps : 1);  // decode: every compute warp frees the stage
+      mbar_init(&ydone[s], kComputeWarps);
     }
     mbar_init(cbar, CL);
     mbar_init(sh_full, 1);
@@ -248,6 +280,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     for (int b = 0; b < 2; ++b) {
       mbar_init(&acc_full[b], 1);
       mbar_init(&acc_free[b], kComputeWarps);
+      mbar_init(&rx_full[b], 1);
+      mbar_init(&rx_free[b], CL > 1 ? CL - 1 : 1);
     }
     *s_bad = 0;
     *s_issued = 0;
@@ -260,11 +294,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
     if ((a.mode & kModeExpand) && a.y_tma)
       for (int i = 0; i < 3; ++i) prefetch_tmap(&a.tmap_y[i]);
-    if ((a.mode & kModeExpand) && C::TC && !a.registry) prefetch_tmap(&a.tmap_b);
+    if ((a.mode & kModeExpand) && C::BTMA && !a.registry) prefetch_tmap(&a.tmap_b);
   }
   // TMEM: shrink accumulator (columns 0-31) and two expand accumulators of two
   // 128 x 32 halves each (columns 64-127 and 128-191)
-  const bool use_tmem = (a.mode & kModeShrink) || (C::TC && (a.mode & kModeExpand));
+  const bool use_tmem = !DEC && ((a.mode & kModeShrink) || (C::TC && (a.mode & kModeExpand)));
   if (use_tmem && warp == 0) tmem_alloc(s_tmem, 256);
   if (use_tmem) tc_fence_before();
   __syncthreads();
@@ -278,6 +312,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const int oB0 = static_cast<int>(q) * a.oslice;
   const int nB = do_ex ? (max(0, min(a.oslice, a.o - oB0)) + C::W - 1) / C::W : 0;
   const int ups = nA + nB;  // stages per segment for this CTA
+  // decode variant: the y box of an expand stage goes back to global memory
+  // with one tensor store when its rows are exactly the segment's rows
+  auto y_by_tma = [&](int n) -> bool {
+    return DEC && a.y_tma && a.o_sliced && (n == 8 || n == 16 || n == 32);
+  };
 
   // ---- segment table of this cluster (all threads) -------------------------
   int nmine = 0;
@@ -302,6 +341,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     tr.dep();
     read_table();
   }
+  if (tid == 0) trace_mark(a.trace, 7);
   const int total = nmine * ups;
   const uint32_t tbase = use_tmem ? *s_tmem : 0u;
   const uint32_t t_sh = tbase;
@@ -316,7 +356,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         const int sub = u % ups;
         const int n = clamp_rows(s.token_count);
         const int bi = box_index(n);
-        const uint32_t box_bytes = (8u << bi) * 128u;
+        const uint32_t box_bytes = (8u << bi) * 128u;  // one 64-column slice of x or y
         uint8_t* st = stage_base + stage * C::STAGE;
         uint64_t* bar = &full[stage];
         if (sub < nA) {
@@ -325,25 +365,32 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
             mbar_arrive_expect_tx(bar, 4 * C::ABOX + 4 * box_bytes);
             const void* amap = a.registry ? s.a : static_cast<const void*>(&a.tmap_a);
             const int aid = a.registry ? 0 : s.adapter_id;
+            if (a.d_sliced) {
+              tma_load_4d(st, amap, 0, 0, k0 / kBoxCols, aid, bar);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j) tma_load_3d(st + j * C::ABOX, amap, k0 + j * kBoxCols, 0, aid, bar);
+              for (int j = 0; j < 4; ++j) tma_load_3d(st + j * C::ABOX, amap, k0 + j * kBoxCols, 0, aid, bar);
+            }
           }
           if (parts & 2) {
+            if (a.d_sliced) {
+              tma_load_3d(st + 4 * C::ABOX, &a.tmap_x[bi], 0, s.token_start, k0 / kBoxCols, bar);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              tma_load_2d(st + 4 * C::ABOX + j * C::XBOX, &a.tmap_x[bi], k0 + j * kBoxCols, s.token_start, bar);
+              for (int j = 0; j < 4; ++j)
+                tma_load_2d(st + 4 * C::ABOX + j * box_bytes, &a.tmap_x[bi], k0 + j * kBoxCols, s.token_start, bar);
+            }
           }
         } else {
           const int oc = oB0 + (sub - nA) * C::W;
           const int wc = min(C::W, a.o - oc);
           if (parts & 1) {
-            if constexpr (C::TC) {
-              // two 128-row boxes of B, rows past o zero-filled
-              mbar_arrive_expect_tx(bar, 2 * 128 * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
+            if constexpr (C::BTMA) {
+              // one 256-row box of B, rows past o zero-filled
+              mbar_arrive_expect_tx(bar, 256 * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
               const void* bmap = a.registry ? s.b : static_cast<const void*>(&a.tmap_b);
               const int bid = a.registry ? 0 : s.adapter_id;
               tma_load_3d(st + 4 * C::XBOX, bmap, 0, oc, bid, bar);
-              tma_load_3d(st + 4 * C::XBOX + 128 * R * 2, bmap, 0, oc + 128, bid, bar);
             } else {
               mbar_arrive_expect_tx(bar, wc * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
               const T* B = a.registry ? static_cast<const T*>(s.b)
@@ -353,17 +400,28 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
             }
           }
           if ((parts & 2) && a.y_tma) {
+            if (a.o_sliced) {
+              tma_load_3d(st, &a.tmap_y[bi], 0, s.token_start, oc / kBoxCols, bar);
+            } else {
 #pragma unroll
-            for (int j = 0; j < 4; ++j)
-              tma_load_2d(st + j * C::XBOX, &a.tmap_y[bi], oc + j * kBoxCols, s.token_start, bar);
+              for (int j = 0; j < 4; ++j)
+                tma_load_2d(st + j * box_bytes, &a.tmap_y[bi], oc + j * kBoxCols, s.token_start, bar);
+            }
           }
         }
       };
       const int first = min(S, total);
+      trace_mark(a.trace, 9);
       if (a.prefetch_weights) {
-        for (int u = 0; u < first; ++u) issue(u, u, 1);
+        for (int u = 0; u < first; ++u) {
+          issue(u, u, 1);
+          trace_unit(a.trace, u, 7);
+          if (u == 0) trace_mark(a.trace, 10);
+        }
+        trace_mark(a.trace, 8);
         pdl_wait_prior();
         pdl_launch_dependents();
+        trace_mark(a.trace, 6);
         for (int u = 0; u < first; ++u) issue(u, u, 2);
       } else {
         for (int u = 0; u < first; ++u) issue(u, u, 3);
@@ -374,6 +432,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         if (!mbar_wait_bounded(&empty[stage], ((u / S) - 1) & 1, a.err)) *s_bad = 1;
         if (*s_bad) break;
         issue(u, stage, 3);
+        trace_unit(a.trace, u, 7);
         *s_issued = u + 1;
       }
     } else if (a.prefetch_weights) {
@@ -389,16 +448,48 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       pdl_wait_prior();
       pdl_launch_dependents();
     }
-    if (lane != 0) return;
-    int u = 0;
-    uint32_t sh_uses = 0, ht_uses = 0, acc_uses[2] = {0u, 0u};
-    int ebuf = 0;
     auto wait_ok = [&](uint64_t* bar, uint32_t parity) -> bool {
       if (*s_bad) return false;
       const bool ok = mbar_wait_bounded(bar, parity, a.err);
       if (!ok) *s_bad = 1;
       return ok;
     };
+    if constexpr (DEC) {
+      // ===================== y store thread (decode) ========================
+      // For every expand stage whose y box is stored by TMA: wait until the
+      // compute warps have written it (ydone), store it, wait until the store
+      // has read shared memory, then free the stage for the producer.
+      if (lane != 0 || !do_ex) return;
+      uint32_t ypar = 0u;
+      int u = 0;
+      for (int sj = 0; sj < nmine; ++sj) {
+        const DevSeg s = desc(sj);
+        const int n = clamp_rows(s.token_count);
+        u += nA;
+        if (!y_by_tma(n)) {
+          u += nB;
+          continue;
+        }
+        for (int i = 0; i < nB; ++i, ++u) {
+          const int stage = u % S;
+          const bool ok = wait_ok(&ydone[stage], (ypar >> stage) & 1u);
+          ypar ^= 1u << stage;
+          if (ok) {
+            tma_store_3d(&a.tmap_y[box_index(n)], 0, s.token_start, (oB0 + i * C::W) / kBoxCols,
+                         stage_base + stage * C::STAGE);
+            bulk_commit();
+            bulk_wait_read();
+          }
+          mbar_arrive_n(&empty[stage], kComputeWarps);
+        }
+      }
+      bulk_wait_all();
+      return;
+    }
+    if (lane != 0) return;
+    int u = 0;
+    uint32_t sh_uses = 0, ht_uses = 0, acc_uses[2] = {0u, 0u};
+    int ebuf = 0;
     for (int sj = 0; sj < nmine; ++sj) {
       const DevSeg s = desc(sj);
       const int n = clamp_rows(s.token_count);
@@ -410,10 +501,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         const bool have = nA > 0 && n > 0;
         if (have && sh_uses > 0) wait_ok(sh_free, (sh_uses - 1) & 1);
         const uint32_t Nsh = static_cast<uint32_t>(max(8, (n + 7) & ~7));
+        const int xsp = (8 << box_index(n)) * 128;  // bytes of one x slice
         const uint32_t idesc = umma_idesc(kAbf, 64, Nsh);
         for (int i = 0; i < nA; ++i, ++u) {
           const int stage = u % S;
           const bool ok = wait_ok(&full[stage], (u / S) & 1);
+          if (sj == 0 && i == 0) trace_mark(a.trace, 4);
           if (ok && have) {
             tc_fence_after();
             const uint32_t st = smem_u32(stage_base + stage * C::STAGE);
@@ -425,13 +518,14 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
 #pragma unroll
               for (int ks = 0; ks < 4; ++ks)
                 umma_f16(t_sh, da + static_cast<uint64_t>((j * C::ABOX + ks * 32) >> 4),
-                         dx + static_cast<uint64_t>((j * C::XBOX + ks * 32) >> 4), idesc,
+                         dx + static_cast<uint64_t>((j * xsp + ks * 32) >> 4), idesc,
                          (i > 0 || j > 0 || ks > 0) ? 1u : 0u);
             umma_commit(&empty[stage]);  // the stage is free once these MMAs have read it
           } else {
             mbar_arrive(&empty[stage]);
           }
         }
+        if (sj == 0) trace_mark(a.trace, 5);
         if (have) {
           if (!*s_bad) umma_commit(sh_full);
           ++sh_uses;
@@ -471,6 +565,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
               for (int ks = 0; ks < R / 16; ++ks) umma_f16(acc, db + 2 * ks, dl + 2 * ks, idesc, 1u);
             }
             umma_commit(&acc_full[b]);
+            if (sj == 0) trace_unit(a.trace, i, 6);
           }
         } else {
           u += nB;
@@ -512,48 +607,242 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     return ok;
   };
 
+  // mma.sync paths: shared-memory offsets of this thread's ldmatrix rows,
+  // relative to a stage (the same for every stage).
+  constexpr int MT = R >= 16 ? R / 16 : 1;  // 16-row rank tiles of the shrink (rank 8: rows 8-15 unused)
+  constexpr int KS = R >= 16 ? R / 16 : 1;  // expand k-steps of 16 (rank 8: one m16n8k8 step)
+  uint32_t offA[2][MT], offX[2][2], offB[KS][2], offY[2][2];
+  if constexpr (DEC) {
+#pragma unroll
+    for (int ks = 0; ks < 2; ++ks) {
+#pragma unroll
+      for (int mt = 0; mt < MT; ++mt) {
+        const int row = mt * 16 + (lane & 15);
+        const int ch = (warp & 1) * 4 + 2 * ks + (lane >> 4);
+        offA[ks][mt] = (warp >> 1) * C::ABOX + row * 128 + (((ch ^ row) & 7) << 4);
+      }
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        const int row = p * 16 + (lane & 7) + ((lane >> 4) << 3);
+        const int ch = (warp & 1) * 4 + 2 * ks + ((lane >> 3) & 1);
+        offX[ks][p] = 4 * C::ABOX + row * 128 + (((ch ^ row) & 7) << 4);  // + slice (warp / 2)
+      }
+    }
+  }
+  if constexpr (!C::TC) {
+#pragma unroll
+    for (int ks = 0; ks < KS; ++ks)
+#pragma unroll
+      for (int p = 0; p < 2; ++p) {
+        // B rows (output columns) of tiles 2p, 2p+1 of this warp; 16-byte chunks 2ks, 2ks+1
+        const int row = warp * 32 + p * 16 + (lane & 7) + ((lane >> 4) << 3);
+        uint32_t lin = static_cast<uint32_t>(row * (2 * R) + (2 * ks + ((lane >> 3) & 1)) * 16);
+        if constexpr (C::BTMA) lin ^= (lin >> 3) & C::SWZ_MASK;
+        offB[ks][p] = 4 * C::XBOX + lin;
+      }
+#pragma unroll
+    for (int m = 0; m < 2; ++m)
+#pragma unroll
+      for (int jp = 0; jp < 2; ++jp) {
+        // y rows (tokens) m*16 + 0..15, columns of tiles 2jp, 2jp+1 of this warp
+        const int row = m * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
+        const int col = warp * 32 + (2 * jp + (lane >> 4)) * 8;
+        offY[m][jp] = row * 128 + (((((col & 63) >> 3) ^ row) & 7) << 4);  // + slice (warp / 2)
+      }
+  }
+
   for (int sj = 0; sj < nmine; ++sj) {
     const DevSeg s = desc(sj);
     const int n = clamp_rows(s.token_count);
     if (tid == 0 && n == 0 && a.err) atomicOr(a.err, kErrBadSegment);
+    // x / y slices are (8 << box_index(n)) rows of 128 bytes; this warp reads slice warp / 2
+    const uint32_t xsl = static_cast<uint32_t>((warp >> 1) * ((8 << box_index(n)) * 128));
     const float alpha = a.registry ? s.alpha : a.scale;
 
     if (do_sh) {
-      kc += nA;  // shrink stages are consumed by the MMA warp
-      // ---- 1. partial tile -> Ps[token][rank] (zeros when this CTA owns no slice of d)
-      const bool have = nA > 0 && n > 0;
-      if (have) {
-        wait_ok(sh_full, sh_ph);
-        sh_ph ^= 1u;
-        tc_fence_after();
-      }
-      // M = 64 accumulator layout: rank r sits in TMEM lane (r % 16) + 32 * (r / 16)
-      if (half == 0 && quarter * 16 < R) {
-        float v[32];
-        // warp-uniform: the tcgen05 loads are .sync.aligned
-        if (__shfl_sync(0xffffffffu, (have && !*s_bad) ? 1 : 0, 0)) {
-          const uint32_t ta = t_sh + (static_cast<uint32_t>(quarter * 32) << 16);
-          tmem_ld16(ta, *reinterpret_cast<float(*)[16]>(v));
-          tmem_ld16(ta + 16, *reinterpret_cast<float(*)[16]>(v + 16));
-        } else {
+      if constexpr (DEC) {
+        // ---- 1. shrink on mma.sync: D[rank, t] += A[rank, k] . x[t, k]^T.
+        // Warp w takes 32 columns of d of every stage (box w/2, half w%2) for
+        // all rank tiles and token tiles, so no two warps read the same bytes;
+        // the 8 partials are summed in a fixed order at the end of the segment.
+        const bool have = nA > 0 && n > 0;
+        const int np = (n + 15) >> 4;  // pairs of 8-token tiles
+        float acc[MT][4][4];
 #pragma unroll
-          for (int j = 0; j < 32; ++j) v[j] = 0.f;
-        }
-        const int r = quarter * 16 + lane;
-        if (lane < 16 && r < R) {
+        for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
-          for (int j = 0; j < 32; ++j) Ps[j * PITCH + r] = v[j];
+          for (int j = 0; j < 4; ++j)
+#pragma unroll
+            for (int e = 0; e < 4; ++e) acc[mt][j][e] = 0.f;
+        for (int i = 0; i < nA; ++i, ++kc) {
+          const int stage = kc % S;
+          if (wait_full(stage) && have) {
+            // all fragment loads first, then the MMAs (two warps per scheduler
+            // cannot hide a load-use chain per k-step)
+            const uint32_t sb = smem_u32(stage_base + stage * C::STAGE);
+            uint32_t af[2][MT][4], bx[2][2][4];
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+              for (int mt = 0; mt < MT; ++mt)
+                ldsm_x4(sb + offA[ks][mt], af[ks][mt][0], af[ks][mt][1], af[ks][mt][2], af[ks][mt][3]);
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+              for (int p = 0; p < 2; ++p)
+                if (p < np) ldsm_x4(sb + xsl + offX[ks][p], bx[ks][p][0], bx[ks][p][1], bx[ks][p][2], bx[ks][p][3]);
+#pragma unroll
+            for (int ks = 0; ks < 2; ++ks)
+#pragma unroll
+              for (int p = 0; p < 2; ++p)
+                if (p < np) {
+#pragma unroll
+                  for (int mt = 0; mt < MT; ++mt) {
+                    mma_k16<T>(acc[mt][2 * p], af[ks][mt], bx[ks][p][0], bx[ks][p][1]);
+                    mma_k16<T>(acc[mt][2 * p + 1], af[ks][mt], bx[ks][p][2], bx[ks][p][3]);
+                  }
+                }
+          }
+          __syncwarp();
+          tr.mark(5);
+          if (lane == 0) mbar_arrive(&empty[stage]);
+        }
+        tr.seg(0, sj);
+        // cross-warp sum: warps 4-7 park their partials, warps 0-3 add them and
+        // park the pair sums; the four slots are added below (fixed order)
+        auto park = [&](float* dst) {
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int r = mt * 16 + g + (e >> 1) * 8;
+                const int t = j * 8 + 2 * c + (e & 1);
+                if (r < R) dst[t * PITCH + r] = acc[mt][j][e];
+              }
+        };
+        if (warp >= 4) park(Pw + (warp - 4) * C::PSLOT);
+        named_sync(kBarCompute, kComputeThreads);
+        if (warp < 4) {
+          const float* src = Pw + warp * C::PSLOT;
+#pragma unroll
+          for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+#pragma unroll
+              for (int e = 0; e < 4; ++e) {
+                const int r = mt * 16 + g + (e >> 1) * 8;
+                const int t = j * 8 + 2 * c + (e & 1);
+                if (r < R) acc[mt][j][e] += src[t * PITCH + r];
+              }
+          park(Pw + warp * C::PSLOT);
+        }
+        named_sync(kBarCompute, kComputeThreads);
+        // ---- 2. cluster exchange (push): this CTA's partial rows go into its
+        // own receive slot and, by st.async, into the same slot of every peer,
+        // completing bytes on the peer's rx_full barrier; the slot of a segment
+        // parity is rewritten only after every peer has released it (rx_free).
+        const int par = sj & 1;
+        const uint32_t use = static_cast<uint32_t>(sj >> 1);  // uses of this parity so far
+        float* rx = Rx + par * C::CLMAX * C::PSLOT;
+        if (CL > 1 && use > 0 && !*s_bad && !mbar_wait_cluster_bounded(&rx_free[par], (use - 1) & 1, a.err)) *s_bad = 1;
+        constexpr int Q4 = R / 4;  // 16-byte chunks per partial row
+        const int nch = n * Q4;
+        if (!*s_bad) {
+          for (int e4 = tid; e4 < nch; e4 += kComputeThreads) {
+            const int off = (e4 / Q4) * PITCH + (e4 % Q4) * 4;
+            float4 v;
+            {
+              const float4 p0 = *reinterpret_cast<const float4*>(Pw + off);
+              const float4 p1 = *reinterpret_cast<const float4*>(Pw + C::PSLOT + off);
+              const float4 p2 = *reinterpret_cast<const float4*>(Pw + 2 * C::PSLOT + off);
+              const float4 p3 = *reinterpret_cast<const float4*>(Pw + 3 * C::PSLOT + off);
+              v.x = (p0.x + p1.x) + (p2.x + p3.x);
+              v.y = (p0.y + p1.y) + (p2.y + p3.y);
+              v.z = (p0.z + p1.z) + (p2.z + p3.z);
+              v.w = (p0.w + p1.w) + (p2.w + p3.w);
+            }
+            float* mine = rx + q * C::PSLOT + off;
+            *reinterpret_cast<float4*>(mine) = v;
+            for (uint32_t i = 1; i < CL; ++i) {
+              const uint32_t peer = (q + i) % CL;
+              st_async_v4(mapa(smem_u32(mine), peer), v, mapa(smem_u32(&rx_full[par]), peer));
+            }
+          }
+        }
+        if (tid == 0) mbar_arrive_expect_tx(&rx_full[par], (CL - 1) * static_cast<uint32_t>(nch) * 16u);
+        named_sync(kBarCompute, kComputeThreads);  // own slot written
+        tr.seg(3, sj);
+        if (!*s_bad && !mbar_wait_cluster_bounded(&rx_full[par], use & 1, a.err)) *s_bad = 1;
+        tr.seg(1, sj);
+        if (!*s_bad) {
+          for (int e4 = tid; e4 < nch; e4 += kComputeThreads) {
+            const int t = e4 / Q4;
+            const int off = t * PITCH + (e4 % Q4) * 4;
+            float4 sum = *reinterpret_cast<const float4*>(rx + off);
+            for (uint32_t i = 1; i < CL; ++i) {
+              const float4 v = *reinterpret_cast<const float4*>(rx + i * C::PSLOT + off);
+              sum.x += v.x;
+              sum.y += v.y;
+              sum.z += v.z;
+              sum.w += v.w;
+            }
+            sum.x *= alpha;
+            sum.y *= alpha;
+            sum.z *= alpha;
+            sum.w *= alpha;
+            if (do_ex) {
+              *reinterpret_cast<float4*>(Hs + off) = sum;
+            } else {
+              *reinterpret_cast<float4*>(a.h + static_cast<int64_t>(s.token_start + t) * R + (e4 % Q4) * 4) = sum;
+            }
+          }
+        }
+        named_sync(kBarCompute, kComputeThreads);  // slots read, H complete
+        if (tid == 0 && CL > 1)
+          for (uint32_t i = 1; i < CL; ++i) mbar_arrive_remote_relaxed(mapa(smem_u32(&rx_free[par]), (q + i) % CL));
+        tr.seg(2, sj);
+      } else {
+        kc += nA;  // shrink stages are consumed by the MMA warp
+        // ---- 1. partial tile -> Ps[token][rank] (zeros when this CTA owns no slice of d)
+        const bool have = nA > 0 && n > 0;
+        if (have) {
+          wait_ok(sh_full, sh_ph);
+          sh_ph ^= 1u;
+          tc_fence_after();
+        }
+        tr.seg(0, sj);
+        // M = 64 accumulator layout: rank r sits in TMEM lane (r % 16) + 32 * (r / 16)
+        if (half == 0 && quarter * 16 < R) {
+          float v[32];
+          // warp-uniform: the tcgen05 loads are .sync.aligned
+          if (__shfl_sync(0xffffffffu, (have && !*s_bad) ? 1 : 0, 0)) {
+            const uint32_t ta = t_sh + (static_cast<uint32_t>(quarter * 32) << 16);
+            tmem_ld16(ta, *reinterpret_cast<float(*)[16]>(v));
+            tmem_ld16(ta + 16, *reinterpret_cast<float(*)[16]>(v + 16));
+          } else {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) v[j] = 0.f;
+          }
+          const int r = quarter * 16 + lane;
+          if (lane < 16 && r < R) {
+#pragma unroll
+            for (int j = 0; j < 32; ++j) Ps[j * PITCH + r] = v[j];
+          }
+        }
+        if (have) {
+          tc_fence_before();
+          __syncwarp();
+          if (lane == 0) mbar_arrive(sh_free);  // the MMA warp may start the next shrink
         }
       }
-      if (have) {
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(sh_free);  // the MMA warp may start the next shrink
-      }
+      if constexpr (!DEC) {
       tr.mark(2);
       // ---- 2. reduce-scatter + all-gather of the partials over the cluster
       if (!cluster_barrier_bounded(cbar, cph, CL, kBarCompute, kComputeThreads, a.err)) *s_bad = 1;
       cph ^= 1u;
+      tr.seg(1, sj);
       if (!*s_bad && n > 0) {
         const int per = (n + static_cast<int>(CL) - 1) / static_cast<int>(CL);
         const int r0 = static_cast<int>(q) * per;
@@ -580,6 +869,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       }
       if (!cluster_barrier_bounded(cbar, cph, CL, kBarCompute, kComputeThreads, a.err)) *s_bad = 1;
       cph ^= 1u;
+      tr.seg(2, sj);
+      }
     } else if (do_ex) {
       // expand alone: H rows of the segment from global memory
       for (int e = tid; e < n * (R / 2); e += kComputeThreads) {
@@ -617,6 +908,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         __syncwarp();
         if (lane == 0) mbar_arrive(ht_full);
       }
+      tr.seg(3, sj);
       const int ol = half * 128 + quarter * 32 + lane;  // this lane's output column in the stage
       for (int i = 0; i < nB; ++i, ++kc) {
         const int stage = kc % S;
@@ -652,7 +944,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           const int col = lane * 8;
           if (col < wc) {
             const int cib = lane & 7;  // 16-byte chunk inside the 128-byte box row
-            const uint8_t* yb = st + (lane >> 3) * C::XBOX;
+            const uint8_t* yb = st + (lane >> 3) * ((8 << box_index(n)) * 128);
             for (int t = warp; t < n; t += kComputeWarps) {
               const float* dr = Ds + t * C::DPITCH + col;
               const float4 d0 = reinterpret_cast<const float4*>(dr)[0];
@@ -685,20 +977,30 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         if (tid == 0) mbar_arrive(&empty[stage]);
       }
     } else {
-      // ---- 3. expand (rank 8) over this CTA's slice of o with mma.sync -------
-      // H fragments (16-bit high part + residual) of both 16-row tiles.
-      uint32_t hi[2][KE][4], lo[2][KE][4];
+      // ---- 3. expand on mma.sync over this CTA's slice of o -----------------
+      // D[t, o] = H[t, :] . B[o, :]^T; warp w owns output columns 32w..32w+31
+      // of every stage (four 8-column tiles), all token tiles. B fragments
+      // come from the stage with ldmatrix. In the decode variant H enters
+      // rounded to T (the weights' type, as the stock expand does); the rank-8
+      // path of the tcgen05 kernel adds a 16-bit residual of H as well
+      // (~16 mantissa bits). Fragments are built once per segment.
+      uint32_t hi[2][KS][4], lo[2][KS][4];
 #pragma unroll
       for (int m = 0; m < 2; ++m) {
         const float* h0 = Hs + (m * 16 + g) * PITCH;
         const float* h1 = h0 + 8 * PITCH;
 #pragma unroll
-        for (int ks = 0; ks < KE; ++ks) {
+        for (int ks = 0; ks < KS; ++ks) {
           const int k0 = ks * 16 + 2 * c;
           float2 x[4];
           x[0] = *reinterpret_cast<const float2*>(h0 + k0);
           x[1] = *reinterpret_cast<const float2*>(h1 + k0);
-          x[2] = x[3] = make_float2(0.f, 0.f);
+          if constexpr (R >= 16) {
+            x[2] = *reinterpret_cast<const float2*>(h0 + k0 + 8);
+            x[3] = *reinterpret_cast<const float2*>(h1 + k0 + 8);
+          } else {
+            x[2] = x[3] = make_float2(0.f, 0.f);
+          }
 #pragma unroll
           for (int e = 0; e < 4; ++e) {
             hi[m][ks][e] = E::pack2(x[e].x, x[e].y);
@@ -708,81 +1010,189 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         }
       }
       const bool m1 = n > 16;
+      const bool tmy = y_by_tma(n);  // the store thread writes the y box back and frees the stage
       for (int i = 0; i < nB; ++i, ++kc) {
         const int stage = kc % S;
         if (wait_full(stage) && n > 0) {
           const uint8_t* st = stage_base + stage * C::STAGE;
-          const uint8_t* Bs = st + 4 * C::XBOX;
           const int oc = oB0 + i * C::W;
           const int wc = min(C::W, a.o - oc);
-          float acc[2][NTW][4];
+          const uint32_t sb = smem_u32(st);
+          // fragment loads first: y (when it sits in the stage) and B
+          const bool ysm = a.y_tma != 0;
+          // with 8-row slices (n <= 8) rows 8-15 of a y tile would alias the
+          // next slice: those lanes address a per-warp scratch row instead
+          // (the P tile is idle during the expand)
+          const bool spill = n <= 8 && (lane & 8);
+          const uint32_t scratch = smem_u32(Ps) + warp * 128 + (lane & 7) * 16;
+          uint32_t yf[2][2][4];
+          float acc[2][4][4];
+          if (ysm) {
 #pragma unroll
-          for (int m = 0; m < 2; ++m)
+            for (int m = 0; m < 2; ++m)
+              if (m == 0 || m1)
 #pragma unroll
-            for (int j = 0; j < NTW; ++j)
+                for (int jp = 0; jp < 2; ++jp)
+                  ldsm_x4(spill ? scratch : sb + xsl + offY[m][jp], yf[m][jp][0], yf[m][jp][1], yf[m][jp][2],
+                          yf[m][jp][3]);
+            // the accumulators start at y (fp32): D = y + H . B^T, rounded once
 #pragma unroll
-              for (int e = 0; e < 4; ++e) acc[m][j][e] = 0.f;
+            for (int m = 0; m < 2; ++m)
 #pragma unroll
-          for (int j = 0; j < NTW; ++j) {
-            const int nt = warp * NTW + j;
-            if (nt * 8 < wc) {
-              const uint32_t b0 = lds32(Bs + (nt * 8 + g) * (R * 2) + c * 4);
-              mma_k8<T>(acc[0][j], hi[0][0][0], hi[0][0][1], b0);
-              mma_k8<T>(acc[0][j], lo[0][0][0], lo[0][0][1], b0);
+              for (int jp = 0; jp < 2; ++jp)
+#pragma unroll
+                for (int k = 0; k < 4; ++k) {
+                  const float2 f = (m == 0 || m1) ? E::unpack2(yf[m][jp][k]) : make_float2(0.f, 0.f);
+                  acc[m][2 * jp + (k >> 1)][(k & 1) * 2] = f.x;
+                  acc[m][2 * jp + (k >> 1)][(k & 1) * 2 + 1] = f.y;
+                }
+          } else {
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+#pragma unroll
+              for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) acc[m][j][e] = 0.f;
+          }
+          if constexpr (R >= 16) {
+            constexpr int KB = KS > 2 ? 2 : KS;  // k-steps whose B fragments are loaded together
+#pragma unroll
+            for (int k0 = 0; k0 < KS; k0 += KB) {
+              uint32_t bfr[KB][2][4];
+#pragma unroll
+              for (int kk = 0; kk < KB; ++kk)
+#pragma unroll
+                for (int p = 0; p < 2; ++p)
+                  ldsm_x4(sb + offB[k0 + kk][p], bfr[kk][p][0], bfr[kk][p][1], bfr[kk][p][2], bfr[kk][p][3]);
+#pragma unroll
+              for (int kk = 0; kk < KB; ++kk)
+#pragma unroll
+                for (int p = 0; p < 2; ++p) {
+                  const int ks = k0 + kk;
+                  const uint32_t* b = bfr[kk][p];
+                  mma_k16<T>(acc[0][2 * p], hi[0][ks], b[0], b[1]);
+                  mma_k16<T>(acc[0][2 * p + 1], hi[0][ks], b[2], b[3]);
+                  if (m1) {
+                    mma_k16<T>(acc[1][2 * p], hi[1][ks], b[0], b[1]);
+                    mma_k16<T>(acc[1][2 * p + 1], hi[1][ks], b[2], b[3]);
+                  }
+                  if constexpr (!DEC) {  // decode: H is rounded to T once (no residual MMAs)
+                    mma_k16<T>(acc[0][2 * p], lo[0][ks], b[0], b[1]);
+                    mma_k16<T>(acc[0][2 * p + 1], lo[0][ks], b[2], b[3]);
+                    if (m1) {
+                      mma_k16<T>(acc[1][2 * p], lo[1][ks], b[0], b[1]);
+                      mma_k16<T>(acc[1][2 * p + 1], lo[1][ks], b[2], b[3]);
+                    }
+                  }
+                }
+            }
+          } else {
+            // rank 8: rows of 16 bytes (linear), matrix j = output tile j
+            uint32_t bf[4];
+            ldsm_x4(sb + 4 * C::XBOX + (warp * 32 + lane) * 16, bf[0], bf[1], bf[2], bf[3]);
+#pragma unroll
+            for (int j = 0; j < 4; ++j) {
+              mma_k8<T>(acc[0][j], hi[0][0][0], hi[0][0][1], bf[j]);
+              if constexpr (!DEC) mma_k8<T>(acc[0][j], lo[0][0][0], lo[0][0][1], bf[j]);
               if (m1) {
-                mma_k8<T>(acc[1][j], hi[1][0][0], hi[1][0][1], b0);
-                mma_k8<T>(acc[1][j], lo[1][0][0], lo[1][0][1], b0);
+                mma_k8<T>(acc[1][j], hi[1][0][0], hi[1][0][1], bf[j]);
+                if constexpr (!DEC) mma_k8<T>(acc[1][j], lo[1][0][0], lo[1][0][1], bf[j]);
               }
             }
           }
-          // y += acc, one rounding (all y reads first, then the stores)
-          float yv[2][NTW][2][2];
+          tr.mark(2);
+          if (ysm) {
+            // y + H . B^T rounded once, written back in place with stmatrix
+            // (the fragments are in the accumulator layout); then the box goes
+            // to global memory by one tensor store (store thread) or this
+            // warp's 16-byte row chunks are stored directly.
 #pragma unroll
-          for (int m = 0; m < 2; ++m)
+            for (int m = 0; m < 2; ++m)
+              if (m == 0 || m1)
 #pragma unroll
-            for (int j = 0; j < NTW; ++j)
+                for (int jp = 0; jp < 2; ++jp) {
 #pragma unroll
-              for (int hf = 0; hf < 2; ++hf) {
-                const int row = m * 16 + g + hf * 8;
-                const int col = (warp * NTW + j) * 8 + 2 * c;
-                float2 v2 = make_float2(0.f, 0.f);
-                if (row < n && col < wc) {
-                  if (a.y_tma) {
-                    v2 = E::unpack2(lds32(st + (col >> 6) * C::XBOX + sw128(row, col & 63)));
-                  } else {
-                    const T* yp = yg + static_cast<int64_t>(s.token_start + row) * a.y_ld + a.y_off + oc + col;
-                    v2 = make_float2(E::to_f(yp[0]), E::to_f(yp[1]));
+                  for (int k = 0; k < 4; ++k) {
+                    const float* av = &acc[m][2 * jp + (k >> 1)][(k & 1) * 2];
+                    yf[m][jp][k] = E::pack2(av[0], av[1]);
                   }
                 }
-                yv[m][j][hf][0] = v2.x;
-                yv[m][j][hf][1] = v2.y;
+#pragma unroll
+            for (int m = 0; m < 2; ++m)
+              if (m == 0 || m1)
+#pragma unroll
+                for (int jp = 0; jp < 2; ++jp)
+                  stsm_x4(spill ? scratch : sb + xsl + offY[m][jp], yf[m][jp][0], yf[m][jp][1], yf[m][jp][2],
+                          yf[m][jp][3]);
+            tr.mark(3);
+            if (tmy) {
+              fence_proxy_async_smem();  // the tensor store reads these writes
+            } else {
+            __syncwarp();
+            const int sub = lane & 3;
+            const int colw = warp * 32 + sub * 8;  // column of this lane's 16-byte chunk in the stage
+            const int chunk = (warp & 1) * 4 + sub;
+            const uint8_t* ybox = st + xsl;
+            T* ycol = yg + static_cast<int64_t>(s.token_start) * a.y_ld + a.y_off + oc + colw;
+            if (colw + 8 <= wc) {
+              int4 out[4];
+#pragma unroll
+              for (int it = 0; it < 4; ++it) {
+                const int row = (lane >> 2) + 8 * it;
+                if (row < n) out[it] = *reinterpret_cast<const int4*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
               }
 #pragma unroll
-          for (int m = 0; m < 2; ++m)
+              for (int it = 0; it < 4; ++it) {
+                const int row = (lane >> 2) + 8 * it;
+                if (row < n) *reinterpret_cast<int4*>(ycol + static_cast<int64_t>(row) * a.y_ld) = out[it];
+              }
+            } else if (colw < wc) {
+              for (int it = 0; it < 4; ++it) {
+                const int row = (lane >> 2) + 8 * it;
+                if (row < n) {
+                  const T* src = reinterpret_cast<const T*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
+                  for (int x = 0; x < wc - colw; ++x) ycol[static_cast<int64_t>(row) * a.y_ld + x] = src[x];
+                }
+              }
+            }
+            }
+          } else {
+            // y not 16-byte addressable: read and write it directly
 #pragma unroll
-            for (int j = 0; j < NTW; ++j)
+            for (int m = 0; m < 2; ++m)
 #pragma unroll
-              for (int hf = 0; hf < 2; ++hf) {
-                const int row = m * 16 + g + hf * 8;
-                const int col = (warp * NTW + j) * 8 + 2 * c;
-                if (row < n && col < wc) {
-                  T* yp = yg + static_cast<int64_t>(s.token_start + row) * a.y_ld + a.y_off + oc + col;
-                  const float v0 = yv[m][j][hf][0] + acc[m][j][hf * 2], v1 = yv[m][j][hf][1] + acc[m][j][hf * 2 + 1];
-                  if (a.y_tma) {
-                    *reinterpret_cast<uint32_t*>(yp) = E::pack2(v0, v1);
-                  } else {
+              for (int j = 0; j < 4; ++j)
+#pragma unroll
+                for (int hf = 0; hf < 2; ++hf) {
+                  const int row = m * 16 + g + hf * 8;
+                  const int col = warp * 32 + j * 8 + 2 * c;
+                  if (row < n && col < wc) {
+                    T* yp = yg + static_cast<int64_t>(s.token_start + row) * a.y_ld + a.y_off + oc + col;
+                    const float v0 = E::to_f(yp[0]) + acc[m][j][hf * 2];
                     yp[0] = E::from_f(v0);
-                    yp[1] = E::from_f(v1);
+                    if (col + 1 < wc) yp[1] = E::from_f(E::to_f(yp[1]) + acc[m][j][hf * 2 + 1]);
                   }
                 }
-              }
+          }
         }
-        named_sync(kBarCompute, kComputeThreads);
-        if (tid == 0) mbar_arrive(&empty[stage]);
+        tr.mark(4);
+        if constexpr (DEC) {
+          __syncwarp();
+          tr.mark(5);
+          if (lane == 0) mbar_arrive(tmy ? &ydone[stage] : &empty[stage]);
+        } else {
+          named_sync(kBarCompute, kComputeThreads);
+          if (tid == 0) mbar_arrive(&empty[stage]);
+        }
       }
     }
   }
 
+  if constexpr (DEC) {
+    // peers may still write this CTA's receive slots and barriers until they
+    // pass this barrier; the shared memory must outlive those accesses
+    if (CL > 1 && !cluster_barrier_bounded(cbar, cph, CL, kBarCompute, kComputeThreads, a.err)) *s_bad = 1;
+  }
   if (*s_bad) {
     // drain: copies may still be in flight into stages issued but not consumed
     named_sync(kBarCompute, kComputeThreads);
@@ -807,15 +1217,16 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
 
 namespace {
 
-template <typename T, int R>
+template <typename T, int R, bool DEC>
 struct ApplyKernel {
+  using C = ApplyCfg<R, DEC>;
   static bool prepare() {
     static std::atomic<uint64_t> done{0};
     int dev = 0;
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (done.load() & bit) return true;
-    if (cudaFuncSetAttribute(apply_kernel<T, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, ApplyCfg<R>::SMEM) !=
+    if (cudaFuncSetAttribute(apply_kernel<T, R, DEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
         cudaSuccess)
       return false;
     done.fetch_or(bit);
@@ -823,11 +1234,12 @@ struct ApplyKernel {
   }
 
   static cudaError_t launch(const ApplyArgs& a, const LaunchCfg& lc) {
+    if (DEC && lc.cluster > C::CLMAX) return cudaErrorInvalidValue;
     if (!prepare()) return cudaGetLastError();
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(lc.grid);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = ApplyCfg<R>::SMEM;
+    cfg.dynamicSmemBytes = C::SMEM;
     cfg.stream = lc.stream;
     cudaLaunchAttribute attr[2];
     attr[0].id = cudaLaunchAttributeClusterDimension;
@@ -838,15 +1250,16 @@ struct ApplyKernel {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = lc.pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, apply_kernel<T, R>, a);
+    return cudaLaunchKernelEx(&cfg, apply_kernel<T, R, DEC>, a);
   }
 
   static int max_grid(int cluster) {
+    if (DEC && cluster > C::CLMAX) return 0;  // receive slots exist for CLMAX ranks
     if (!prepare()) return 0;
     cudaLaunchConfig_t cfg = {};
     cfg.gridDim = dim3(cluster * 64);
     cfg.blockDim = dim3(kThreads);
-    cfg.dynamicSmemBytes = ApplyCfg<R>::SMEM;
+    cfg.dynamicSmemBytes = C::SMEM;
     cudaLaunchAttribute attr[1];
     attr[0].id = cudaLaunchAttributeClusterDimension;
     attr[0].val.clusterDim.x = cluster;
@@ -855,7 +1268,7 @@ struct ApplyKernel {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int nclusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&nclusters, apply_kernel<T, R>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&nclusters, apply_kernel<T, R, DEC>, &cfg) != cudaSuccess) {
       cudaGetLastError();
       return 0;
     }
@@ -866,21 +1279,21 @@ struct ApplyKernel {
 template <typename T>
 cudaError_t apply_by_rank(int rank, const ApplyArgs& a, const LaunchCfg& lc) {
   switch (rank) {
-    case 8: return ApplyKernel<T, 8>::launch(a, lc);
-    case 16: return ApplyKernel<T, 16>::launch(a, lc);
-    case 32: return ApplyKernel<T, 32>::launch(a, lc);
-    case 64: return ApplyKernel<T, 64>::launch(a, lc);
+    case 8: return lc.dec ? ApplyKernel<T, 8, true>::launch(a, lc) : ApplyKernel<T, 8, false>::launch(a, lc);
+    case 16: return lc.dec ? ApplyKernel<T, 16, true>::launch(a, lc) : ApplyKernel<T, 16, false>::launch(a, lc);
+    case 32: return lc.dec ? ApplyKernel<T, 32, true>::launch(a, lc) : ApplyKernel<T, 32, false>::launch(a, lc);
+    case 64: return lc.dec ? ApplyKernel<T, 64, true>::launch(a, lc) : ApplyKernel<T, 64, false>::launch(a, lc);
     default: return cudaErrorInvalidValue;
   }
 }
 
 template <typename T>
-int max_grid_by_rank(int rank, int cluster) {
+int max_grid_by_rank(int rank, int cluster, bool dec) {
   switch (rank) {
-    case 8: return ApplyKernel<T, 8>::max_grid(cluster);
-    case 16: return ApplyKernel<T, 16>::max_grid(cluster);
-    case 32: return ApplyKernel<T, 32>::max_grid(cluster);
-    case 64: return ApplyKernel<T, 64>::max_grid(cluster);
+    case 8: return dec ? ApplyKernel<T, 8, true>::max_grid(cluster) : ApplyKernel<T, 8, false>::max_grid(cluster);
+    case 16: return dec ? ApplyKernel<T, 16, true>::max_grid(cluster) : ApplyKernel<T, 16, false>::max_grid(cluster);
+    case 32: return dec ? ApplyKernel<T, 32, true>::max_grid(cluster) : ApplyKernel<T, 32, false>::max_grid(cluster);
+    case 64: return dec ? ApplyKernel<T, 64, true>::max_grid(cluster) : ApplyKernel<T, 64, false>::max_grid(cluster);
     default: return 0;
   }
 }
@@ -891,8 +1304,8 @@ cudaError_t launch_apply(int dtype, int rank, const ApplyArgs& a, const LaunchCf
   return dtype == 1 ? apply_by_rank<__nv_bfloat16>(rank, a, lc) : apply_by_rank<__half>(rank, a, lc);
 }
 
-int apply_max_grid(int dtype, int rank, int cluster) {
-  return dtype == 1 ? max_grid_by_rank<__nv_bfloat16>(rank, cluster) : max_grid_by_rank<__half>(rank, cluster);
+int apply_max_grid(int dtype, int rank, int cluster, bool dec) {
+  return dtype == 1 ? max_grid_by_rank<__nv_bfloat16>(rank, cluster, dec) : max_grid_by_rank<__half>(rank, cluster, dec);
 }
 
 }  // namespace wp

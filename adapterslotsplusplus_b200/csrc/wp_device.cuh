@@ -54,14 +54,31 @@ __device__ __forceinline__ bool mbar_try_wait(uint64_t* bar, uint32_t parity) {
   return ok != 0;
 }
 
-// Waits for phase `parity` of `bar` to complete, for at most kWaitTimeoutNs.
+// Suspend time hint of the blocking waits: the waiting thread sleeps in
+// hardware until the phase completes or this many nanoseconds pass, so a
+// waiting warp takes no issue slots from the warps doing the work.
+constexpr uint32_t kSuspendHintNs = 20000;
+
+__device__ __forceinline__ bool mbar_try_wait_sleep(uint64_t* bar, uint32_t parity) {
+  uint32_t ok;
+  asm volatile(
+      "{\n\t.reg .pred p;\n\t"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n\t"
+      "selp.u32 %0, 1, 0, p;\n\t}"
+      : "=r"(ok)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
+      : "memory");
+  return ok != 0;
+}
+
+// Waits for phase `parity` of `bar` to complete, for at most timeout_ns.
 // Returns false (and raises kErrWaitTimeout in *err) when the bound is hit.
 __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity, int* err,
                                                   unsigned long long timeout_ns = kWaitTimeoutNs) {
   if (mbar_try_wait(bar, parity)) return true;
   const unsigned long long t0 = global_timer_ns();
   while (true) {
-    if (mbar_try_wait(bar, parity)) return true;
+    if (mbar_try_wait_sleep(bar, parity)) return true;
     if (global_timer_ns() - t0 > timeout_ns) {
       if (err) atomicOr(err, kErrWaitTimeout);
       return false;
@@ -111,6 +128,23 @@ __device__ __forceinline__ void tma_load_2d(void* dst_smem, const void* tmap, in
       : "memory");
 }
 
+__device__ __forceinline__ void tma_load_4d(void* dst_smem, const void* tmap, int c0, int c1, int c2, int c3,
+                                            uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes [%0], [%1, {%2, %3, %4, %5}], "
+      "[%6];" ::"r"(smem_u32(dst_smem)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar))
+      : "memory");
+}
+
+// Tiled tensor store shared -> global (bulk-group completion).
+__device__ __forceinline__ void tma_store_3d(const void* tmap, int c0, int c1, int c2, const void* src_smem) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.global.shared::cta.tile.bulk_group [%0, {%1, %2, %3}], [%4];" ::"l"(tmap), "r"(c0),
+      "r"(c1), "r"(c2), "r"(smem_u32(src_smem))
+      : "memory");
+}
+
 __device__ __forceinline__ void tma_load_3d(void* dst_smem, const void* tmap, int c0, int c1, int c2,
                                             uint64_t* bar) {
   asm volatile(
@@ -140,6 +174,10 @@ __device__ __forceinline__ void named_sync(int id, int nthreads) {
 
 __device__ __forceinline__ void mbar_arrive(uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(smem_u32(bar)) : "memory");
+}
+// `count` arrivals at once.
+__device__ __forceinline__ void mbar_arrive_n(uint64_t* bar, uint32_t count) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0], %1;" ::"r"(smem_u32(bar)), "r"(count) : "memory");
 }
 
 // ---- thread-block clusters and distributed shared memory -----------------
@@ -190,16 +228,47 @@ __device__ __forceinline__ void mbar_arrive_remote(uint32_t cluster_addr) {
   asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
 }
 
+// Remote arrive without release semantics: for a caller whose earlier reads
+// are complete (their values were consumed before a CTA barrier) and whose
+// outstanding global stores need not be ordered before the arrive.
+__device__ __forceinline__ void mbar_arrive_remote_relaxed(uint32_t cluster_addr) {
+  asm volatile("mbarrier.arrive.relaxed.cluster.shared::cluster.b64 _, [%0];" ::"r"(cluster_addr) : "memory");
+}
+
 __device__ __forceinline__ bool mbar_try_wait_cluster(uint64_t* bar, uint32_t parity) {
   uint32_t ok;
   asm volatile(
       "{\n\t.reg .pred p;\n\t"
-      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2;\n\t"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n\t"
       "selp.u32 %0, 1, 0, p;\n\t}"
       : "=r"(ok)
-      : "r"(smem_u32(bar)), "r"(parity)
+      : "r"(smem_u32(bar)), "r"(parity), "r"(kSuspendHintNs)
       : "memory");
   return ok != 0;
+}
+
+// Bounded wait (acquire at cluster scope) for phase `parity` of a local
+// mbarrier that other CTAs of the cluster arrive on or complete bytes on.
+__device__ __forceinline__ bool mbar_wait_cluster_bounded(uint64_t* bar, uint32_t parity, int* err) {
+  if (mbar_try_wait_cluster(bar, parity)) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    if (mbar_try_wait_cluster(bar, parity)) return true;
+    if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+      if (err) atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
+// 16-byte store into another CTA's shared memory (cluster address) that
+// completes 16 bytes of transaction count on that CTA's mbarrier `rbar`
+// (cluster address) once the data is visible there.
+__device__ __forceinline__ void st_async_v4(uint32_t raddr, float4 v, uint32_t rbar) {
+  asm volatile(
+      "st.async.shared::cluster.mbarrier::complete_tx::bytes.v4.f32 [%0], {%1, %2, %3, %4}, [%5];" ::"r"(raddr),
+      "f"(v.x), "f"(v.y), "f"(v.z), "f"(v.w), "r"(rbar)
+      : "memory");
 }
 
 // Bounded cluster-wide barrier among the `nthreads` compute threads (named
@@ -404,7 +473,7 @@ __device__ __forceinline__ void mma_k16(float (&d)[4], const uint32_t (&a)[4], u
 
 template <>
 __device__ __forceinline__ void mma_k16<__half>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -414,7 +483,7 @@ __device__ __forceinline__ void mma_k16<__half>(float (&d)[4], const uint32_t (&
 template <>
 __device__ __forceinline__ void mma_k16<__nv_bfloat16>(float (&d)[4], const uint32_t (&a)[4], uint32_t b0,
                                                        uint32_t b1) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
       "{%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
@@ -426,7 +495,7 @@ __device__ __forceinline__ void mma_k8(float (&d)[4], uint32_t a0, uint32_t a1, 
 
 template <>
 __device__ __forceinline__ void mma_k8<__half>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k8.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(b0));
@@ -434,12 +503,30 @@ __device__ __forceinline__ void mma_k8<__half>(float (&d)[4], uint32_t a0, uint3
 
 template <>
 __device__ __forceinline__ void mma_k8<__nv_bfloat16>(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
-  asm volatile(
+  asm(
       "mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5}, {%6}, {%0,%1,%2,%3};"
       : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
       : "r"(a0), "r"(a1), "r"(b0));
 }
 
 __device__ __forceinline__ uint32_t lds32(const void* p) { return *reinterpret_cast<const uint32_t*>(p); }
+
+// Stores four 8x8 16-bit matrices to shared memory; addresses and fragment
+// ownership as for ldsm_x4.
+__device__ __forceinline__ void stsm_x4(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3)
+               : "memory");
+}
+
+// Four 8x8 16-bit matrices from shared memory: lanes 8i..8i+7 give the row
+// addresses (16 contiguous bytes each) of matrix i; r[i] receives this lane's
+// fragment of matrix i (row lane/4, elements 2*(lane%4) and +1).
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
 
 }  // namespace wp

@@ -44,10 +44,15 @@ enum : int { kModeShrink = 1, kModeExpand = 2, kModeFused = 3 };
 // aligned) come first; index i of tmap_x / tmap_y is the map whose box is
 // (8 << i) rows high (8, 16, 32), so a segment loads only the rows it needs.
 struct ApplyArgs {
-  CUtensorMap tmap_x[3];  // x [T, d]: boxes of 64 columns, 128B swizzle
-  CUtensorMap tmap_y[3];  // y columns [y_off, y_off + o) x T rows, 128B swizzle
-  CUtensorMap tmap_a;  // live mode: A stack [L, r, d], box 64 x r x 1
-  CUtensorMap tmap_b;  // live mode, r >= 16: B stack [L, o, r], box r x 128 x 1, swizzle = 2r bytes
+  // x / y / A maps are "sliced" when d (x, A) or o (y) is a multiple of 64:
+  // the row is viewed as [d / 64 slices][64 columns] and one box brings the 4
+  // slices of a stage ([4][rows][64] in shared memory, 128B swizzle) in a
+  // single instruction; otherwise they are plain maps loaded 64 columns at a
+  // time into the same layout.
+  CUtensorMap tmap_x[3];  // x [T, d], 8 << i rows per box
+  CUtensorMap tmap_y[3];  // y columns [y_off, y_off + o) x T rows, 8 << i rows per box
+  CUtensorMap tmap_a;  // live mode: A stack [L, r, d]
+  CUtensorMap tmap_b;  // live mode, r >= 16: B stack [L, o, r], box r x 256 x 1, swizzle = 2r bytes
   const DevSeg* segs;
   const int* num_segs;
   float* h;  // shrink-only: H [T, r] fp32 written; expand-only: read
@@ -64,6 +69,8 @@ struct ApplyArgs {
   int split_len;  // d elements per cluster rank (multiple of kStageK)
   int oslice;  // o columns per cluster rank (multiple of kStageCols)
   int y_tma;  // 1: tmap_y is valid; else y is read and written directly
+  int d_sliced;  // tmap_x and the A maps are sliced (d % 64 == 0)
+  int o_sliced;  // tmap_y is sliced (o % 64 == 0)
   int prefetch_weights;  // 1: table and weight loads may start before the dependency wait
   int* err;
   unsigned long long* trace;  // optional per-CTA phase timestamps (kTraceSlots per CTA), else null
@@ -71,19 +78,26 @@ struct ApplyArgs {
 
 // Per-CTA trace record (globaltimer ns): start, after the dependency wait,
 // first stage ready, end, stages consumed, ns consumers spent waiting for
-// stages, ns the producer spent waiting for free stages, 0; then, for the
-// first kTraceUnits stages, 6 timestamps each: before the stage wait, after
+// stages, ns the producer spent waiting for free stages, 0; eight marks of the
+// first segment (8: shrink accumulator ready, 9: after the first cluster
+// barrier, 10: after the second, 11: H tiles written, 12: first shrink stage
+// landed (MMA warp), 13: last shrink MMA issued, 14: producer past the
+// dependency wait, 15: table read, 16: producer before the dependency wait,
+// 17-19: unused); then, for the first kTraceUnits stages, 8 timestamps each: before the stage wait, after
 // it, then four phase marks (for an expand stage: MMA done, results in shared
-// memory, after the barrier, results stored).
+// memory, after the barrier, results stored; then the MMA warp's commit and
+// the producer's issue of that stage).
 constexpr int kTraceUnits = 16;
-constexpr int kTraceMarks = 6;
-constexpr int kTraceSlots = 8 + kTraceMarks * kTraceUnits;
+constexpr int kTraceMarks = 8;
+constexpr int kTraceSegMarks = 12;
+constexpr int kTraceSlots = 8 + kTraceSegMarks + kTraceMarks * kTraceUnits;
 
 struct LaunchCfg {
   int grid;
   int cluster;
   cudaStream_t stream;
   bool pdl;
+  bool dec;  // decode variant (mma.sync in the compute warps) instead of tcgen05
 };
 
 // dtype: 0 = f16, 1 = bf16 (WP_DTYPE_*). Launches the clustered apply kernel
@@ -91,7 +105,7 @@ struct LaunchCfg {
 cudaError_t launch_apply(int dtype, int rank, const ApplyArgs& a, const LaunchCfg& lc);
 // Largest co-resident persistent grid for the apply kernel of (dtype, rank)
 // with clusters of `cluster` CTAs (0 if that cluster size cannot be scheduled).
-int apply_max_grid(int dtype, int rank, int cluster);
+int apply_max_grid(int dtype, int rank, int cluster, bool dec);
 
 // idx_dtype: WP_DTYPE_I32 or WP_DTYPE_I64.
 cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs,
