@@ -94,6 +94,7 @@ constexpr int kMmaWarp = kComputeWarps + 1;  // tcgen05.mma issue
 constexpr int kThreads = kComputeThreads + 64;  // + the producer and MMA warps
 constexpr int kBarCompute = 1;  // named barrier of the compute warps
 constexpr int kDescCache = 64;  // segment descriptors cached per CTA
+constexpr int kSnakeMax = 128;  // tables up to this size are dealt by decreasing token count
 constexpr unsigned long long kDrainNs = 10000000ull;  // 10 ms per stage when draining after an error
 
 constexpr int kSmemMax = 232448;  // dynamic shared memory per CTA (227 KB)
@@ -135,6 +136,7 @@ struct ApplyCfg {
   static constexpr int SMEM = FIXED + STAGES * STAGE;
   static_assert(STAGES >= 2 && STAGES <= 8 && SMEM <= kSmemMax, "shared memory budget");
   static_assert(32 * PITCH * 4 >= kComputeWarps * 128, "the P tile holds one scratch row per compute warp");
+  static_assert(32 * PITCH * 4 >= 2 * kSnakeMax * 4, "the H tile holds the table-ordering scratch");
 };
 
 __device__ __forceinline__ DevSeg unpack_seg(int4 v0, int4 v1) {
@@ -320,12 +322,42 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
 
   // ---- segment table of this cluster (all threads) -------------------------
   int nmine = 0;
+  // Segments per cluster. Small tables (decode) are dealt in "snake" order of
+  // decreasing token count (round r gives cluster c the segment at sorted
+  // position r*G + c, or r*G + G-1-c on odd rounds), which pairs the largest
+  // segments with the smallest on the same cluster; larger tables go round
+  // robin (cluster c takes c, c + G, ...).
   auto read_table = [&]() {
     const int nseg = __ldcg(a.num_segs);
-    nmine = nseg > cid ? (nseg - cid + G - 1) / G : 0;
-    const int cached = min(nmine, kDescCache);
-    for (int j = tid; j < 2 * cached; j += kThreads)
-      sdesc[j] = __ldcg(reinterpret_cast<const int4*>(a.segs + cid + (j >> 1) * G) + (j & 1));
+    if (G > 1 && nseg > G && nseg <= kSnakeMax) {
+      int* cnt = reinterpret_cast<int*>(Hs);  // scratch: the H tile is idle until the first exchange
+      int* order = cnt + kSnakeMax;
+      for (int t = tid; t < nseg; t += kThreads) cnt[t] = __ldcg(&a.segs[t].token_count);
+      __syncthreads();
+      for (int t = tid; t < nseg; t += kThreads) {
+        const int ct = cnt[t];
+        int p = 0;
+        for (int j = 0; j < nseg; ++j) p += (cnt[j] > ct || (cnt[j] == ct && j < t)) ? 1 : 0;
+        order[p] = t;
+      }
+      __syncthreads();
+      const int rounds = (nseg + G - 1) / G;
+      nmine = 0;
+      for (int r = 0; r < rounds; ++r) {
+        const int p = r * G + ((r & 1) ? G - 1 - cid : cid);
+        if (p < nseg) nmine = r + 1;  // positions grow with r, so the items are rounds 0..nmine-1
+      }
+      for (int j = tid; j < 2 * nmine; j += kThreads) {
+        const int r = j >> 1;
+        const int p = r * G + ((r & 1) ? G - 1 - cid : cid);
+        sdesc[j] = __ldcg(reinterpret_cast<const int4*>(a.segs + order[p]) + (j & 1));
+      }
+    } else {
+      nmine = nseg > cid ? (nseg - cid + G - 1) / G : 0;
+      const int cached = min(nmine, kDescCache);
+      for (int j = tid; j < 2 * cached; j += kThreads)
+        sdesc[j] = __ldcg(reinterpret_cast<const int4*>(a.segs + cid + (j >> 1) * G) + (j & 1));
+    }
     __syncthreads();
   };
   auto desc = [&](int j) -> DevSeg {
@@ -611,7 +643,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   // relative to a stage (the same for every stage).
   constexpr int MT = R >= 16 ? R / 16 : 1;  // 16-row rank tiles of the shrink (rank 8: rows 8-15 unused)
   constexpr int KS = R >= 16 ? R / 16 : 1;  // expand k-steps of 16 (rank 8: one m16n8k8 step)
-  uint32_t offA[2][MT], offX[2][2], offB[KS][2], offY[2][2];
+  uint32_t offA[2][MT], offX[2][2], offB[KS][2], offY[4];
   if constexpr (DEC) {
 #pragma unroll
     for (int ks = 0; ks < 2; ++ks) {
@@ -630,25 +662,23 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
   }
   if constexpr (!C::TC) {
+    // expand, transposed: A operand = B rows (output columns) 16 per tile
 #pragma unroll
     for (int ks = 0; ks < KS; ++ks)
 #pragma unroll
-      for (int p = 0; p < 2; ++p) {
-        // B rows (output columns) of tiles 2p, 2p+1 of this warp; 16-byte chunks 2ks, 2ks+1
-        const int row = warp * 32 + p * 16 + (lane & 7) + ((lane >> 4) << 3);
-        uint32_t lin = static_cast<uint32_t>(row * (2 * R) + (2 * ks + ((lane >> 3) & 1)) * 16);
+      for (int m = 0; m < 2; ++m) {
+        const int row = warp * 32 + m * 16 + (lane & 15);
+        uint32_t lin = static_cast<uint32_t>(row * (2 * R) + (2 * ks + (lane >> 4)) * 16);
         if constexpr (C::BTMA) lin ^= (lin >> 3) & C::SWZ_MASK;
-        offB[ks][p] = 4 * C::XBOX + lin;
+        offB[ks][m] = 4 * C::XBOX + lin;
       }
+    // y (token rows t, this warp's 32 columns as four 8-column matrices)
 #pragma unroll
-    for (int m = 0; m < 2; ++m)
-#pragma unroll
-      for (int jp = 0; jp < 2; ++jp) {
-        // y rows (tokens) m*16 + 0..15, columns of tiles 2jp, 2jp+1 of this warp
-        const int row = m * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int col = warp * 32 + (2 * jp + (lane >> 4)) * 8;
-        offY[m][jp] = row * 128 + (((((col & 63) >> 3) ^ row) & 7) << 4);  // + slice (warp / 2)
-      }
+    for (int nt = 0; nt < 4; ++nt) {
+      const int t = nt * 8 + (lane & 7);
+      const int chunk = (warp & 1) * 4 + (lane >> 3);
+      offY[nt] = t * 128 + (((chunk ^ t) & 7) << 4);  // + slice (warp / 2)
+    }
   }
 
   for (int sj = 0; sj < nmine; ++sj) {
@@ -667,6 +697,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         // the 8 partials are summed in a fixed order at the end of the segment.
         const bool have = nA > 0 && n > 0;
         const int np = (n + 15) >> 4;  // pairs of 8-token tiles
+        const int nts = (n + 7) >> 3;  // 8-token tiles
         float acc[MT][4][4];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
@@ -699,7 +730,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
 #pragma unroll
                   for (int mt = 0; mt < MT; ++mt) {
                     mma_k16<T>(acc[mt][2 * p], af[ks][mt], bx[ks][p][0], bx[ks][p][1]);
-                    mma_k16<T>(acc[mt][2 * p + 1], af[ks][mt], bx[ks][p][2], bx[ks][p][3]);
+                    if (2 * p + 1 < nts) mma_k16<T>(acc[mt][2 * p + 1], af[ks][mt], bx[ks][p][2], bx[ks][p][3]);
                   }
                 }
           }
@@ -978,38 +1009,36 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       }
     } else {
       // ---- 3. expand on mma.sync over this CTA's slice of o -----------------
-      // D[t, o] = H[t, :] . B[o, :]^T; warp w owns output columns 32w..32w+31
-      // of every stage (four 8-column tiles), all token tiles. B fragments
-      // come from the stage with ldmatrix. In the decode variant H enters
-      // rounded to T (the weights' type, as the stock expand does); the rank-8
-      // path of the tcgen05 kernel adds a 16-bit residual of H as well
-      // (~16 mantissa bits). Fragments are built once per segment.
-      uint32_t hi[2][KS][4], lo[2][KS][4];
+      // Transposed: D^T[o, t] = B[o, :] . H[t, :]^T with M = 16 output columns
+      // per tile (A operand: B rows from the stage, ldmatrix) and N = 8 tokens
+      // per tile (B operand: H rows), so a segment of n tokens costs
+      // ceil(n / 8) token tiles. Warp w owns output columns 32w..32w+31 of
+      // every stage. y comes in and goes back through ldmatrix / stmatrix
+      // .trans, which turn the [token][column] box into the accumulator
+      // layout and back. In the decode variant H enters rounded to T (the
+      // weights' type, as the stock expand does); the rank-8 path of the
+      // tcgen05 kernel adds a 16-bit residual of H (~16 mantissa bits).
+      uint32_t hb[4][KS][2], hl[4][KS][2];
 #pragma unroll
-      for (int m = 0; m < 2; ++m) {
-        const float* h0 = Hs + (m * 16 + g) * PITCH;
-        const float* h1 = h0 + 8 * PITCH;
+      for (int nt = 0; nt < 4; ++nt) {
+        const float* hrow = Hs + (nt * 8 + g) * PITCH;
 #pragma unroll
         for (int ks = 0; ks < KS; ++ks) {
           const int k0 = ks * 16 + 2 * c;
-          float2 x[4];
-          x[0] = *reinterpret_cast<const float2*>(h0 + k0);
-          x[1] = *reinterpret_cast<const float2*>(h1 + k0);
-          if constexpr (R >= 16) {
-            x[2] = *reinterpret_cast<const float2*>(h0 + k0 + 8);
-            x[3] = *reinterpret_cast<const float2*>(h1 + k0 + 8);
-          } else {
-            x[2] = x[3] = make_float2(0.f, 0.f);
-          }
+          float2 x[2];
+          x[0] = *reinterpret_cast<const float2*>(hrow + k0);
+          x[1] = R >= 16 ? *reinterpret_cast<const float2*>(hrow + k0 + 8) : make_float2(0.f, 0.f);
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
-            hi[m][ks][e] = E::pack2(x[e].x, x[e].y);
-            const float2 r = E::unpack2(hi[m][ks][e]);
-            lo[m][ks][e] = E::pack2(x[e].x - r.x, x[e].y - r.y);
+          for (int e = 0; e < 2; ++e) {
+            hb[nt][ks][e] = E::pack2(x[e].x, x[e].y);
+            if constexpr (!DEC) {
+              const float2 r = E::unpack2(hb[nt][ks][e]);
+              hl[nt][ks][e] = E::pack2(x[e].x - r.x, x[e].y - r.y);
+            }
           }
         }
       }
-      const bool m1 = n > 16;
+      const int ntn = (n + 7) >> 3;  // token tiles of the segment
       const bool tmy = y_by_tma(n);  // the store thread writes the y box back and frees the stage
       for (int i = 0; i < nB; ++i, ++kc) {
         const int stage = kc % S;
@@ -1018,164 +1047,129 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           const int oc = oB0 + i * C::W;
           const int wc = min(C::W, a.o - oc);
           const uint32_t sb = smem_u32(st);
-          // fragment loads first: y (when it sits in the stage) and B
           const bool ysm = a.y_tma != 0;
-          // with 8-row slices (n <= 8) rows 8-15 of a y tile would alias the
-          // next slice: those lanes address a per-warp scratch row instead
-          // (the P tile is idle during the expand)
-          const bool spill = n <= 8 && (lane & 8);
-          const uint32_t scratch = smem_u32(Ps) + warp * 128 + (lane & 7) * 16;
-          uint32_t yf[2][2][4];
+          // y tiles (when y sits in the stage): yf[nt][ob] = y[t in tile nt][8 columns ob]
+          uint32_t yf[4][4];
           float acc[2][4][4];
           if (ysm) {
 #pragma unroll
-            for (int m = 0; m < 2; ++m)
-              if (m == 0 || m1)
-#pragma unroll
-                for (int jp = 0; jp < 2; ++jp)
-                  ldsm_x4(spill ? scratch : sb + xsl + offY[m][jp], yf[m][jp][0], yf[m][jp][1], yf[m][jp][2],
-                          yf[m][jp][3]);
-            // the accumulators start at y (fp32): D = y + H . B^T, rounded once
-#pragma unroll
-            for (int m = 0; m < 2; ++m)
-#pragma unroll
-              for (int jp = 0; jp < 2; ++jp)
-#pragma unroll
-                for (int k = 0; k < 4; ++k) {
-                  const float2 f = (m == 0 || m1) ? E::unpack2(yf[m][jp][k]) : make_float2(0.f, 0.f);
-                  acc[m][2 * jp + (k >> 1)][(k & 1) * 2] = f.x;
-                  acc[m][2 * jp + (k >> 1)][(k & 1) * 2 + 1] = f.y;
-                }
-          } else {
-#pragma unroll
-            for (int m = 0; m < 2; ++m)
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) acc[m][j][e] = 0.f;
+            for (int nt = 0; nt < 4; ++nt)
+              if (nt < ntn) ldsm_x4_t(sb + xsl + offY[nt], yf[nt][0], yf[nt][1], yf[nt][2], yf[nt][3]);
           }
+          // the accumulators start at y (fp32): D = y + H . B^T, rounded once
+#pragma unroll
+          for (int m = 0; m < 2; ++m)
+#pragma unroll
+            for (int nt = 0; nt < 4; ++nt) {
+              float2 f0 = make_float2(0.f, 0.f), f1 = make_float2(0.f, 0.f);
+              if (ysm && nt < ntn) {
+                f0 = E::unpack2(yf[nt][2 * m]);
+                f1 = E::unpack2(yf[nt][2 * m + 1]);
+              }
+              acc[m][nt][0] = f0.x;
+              acc[m][nt][1] = f0.y;
+              acc[m][nt][2] = f1.x;
+              acc[m][nt][3] = f1.y;
+            }
+          tr.mark(2);
           if constexpr (R >= 16) {
             constexpr int KB = KS > 2 ? 2 : KS;  // k-steps whose B fragments are loaded together
 #pragma unroll
             for (int k0 = 0; k0 < KS; k0 += KB) {
-              uint32_t bfr[KB][2][4];
+              uint32_t bA[KB][2][4];
 #pragma unroll
               for (int kk = 0; kk < KB; ++kk)
 #pragma unroll
-                for (int p = 0; p < 2; ++p)
-                  ldsm_x4(sb + offB[k0 + kk][p], bfr[kk][p][0], bfr[kk][p][1], bfr[kk][p][2], bfr[kk][p][3]);
+                for (int m = 0; m < 2; ++m)
+                  ldsm_x4(sb + offB[k0 + kk][m], bA[kk][m][0], bA[kk][m][1], bA[kk][m][2], bA[kk][m][3]);
 #pragma unroll
               for (int kk = 0; kk < KB; ++kk)
 #pragma unroll
-                for (int p = 0; p < 2; ++p) {
-                  const int ks = k0 + kk;
-                  const uint32_t* b = bfr[kk][p];
-                  mma_k16<T>(acc[0][2 * p], hi[0][ks], b[0], b[1]);
-                  mma_k16<T>(acc[0][2 * p + 1], hi[0][ks], b[2], b[3]);
-                  if (m1) {
-                    mma_k16<T>(acc[1][2 * p], hi[1][ks], b[0], b[1]);
-                    mma_k16<T>(acc[1][2 * p + 1], hi[1][ks], b[2], b[3]);
-                  }
-                  if constexpr (!DEC) {  // decode: H is rounded to T once (no residual MMAs)
-                    mma_k16<T>(acc[0][2 * p], lo[0][ks], b[0], b[1]);
-                    mma_k16<T>(acc[0][2 * p + 1], lo[0][ks], b[2], b[3]);
-                    if (m1) {
-                      mma_k16<T>(acc[1][2 * p], lo[1][ks], b[0], b[1]);
-                      mma_k16<T>(acc[1][2 * p + 1], lo[1][ks], b[2], b[3]);
+                for (int nt = 0; nt < 4; ++nt)
+                  if (nt < ntn) {
+                    const int ks = k0 + kk;
+#pragma unroll
+                    for (int m = 0; m < 2; ++m) {
+                      mma_k16<T>(acc[m][nt], bA[kk][m], hb[nt][ks][0], hb[nt][ks][1]);
+                      if constexpr (!DEC) mma_k16<T>(acc[m][nt], bA[kk][m], hl[nt][ks][0], hl[nt][ks][1]);
                     }
                   }
-                }
             }
           } else {
-            // rank 8: rows of 16 bytes (linear), matrix j = output tile j
+            // rank 8: B rows of 16 bytes (linear); matrices 2m, 2m + 1 = rows 16m..16m+15
             uint32_t bf[4];
             ldsm_x4(sb + 4 * C::XBOX + (warp * 32 + lane) * 16, bf[0], bf[1], bf[2], bf[3]);
 #pragma unroll
-            for (int j = 0; j < 4; ++j) {
-              mma_k8<T>(acc[0][j], hi[0][0][0], hi[0][0][1], bf[j]);
-              if constexpr (!DEC) mma_k8<T>(acc[0][j], lo[0][0][0], lo[0][0][1], bf[j]);
-              if (m1) {
-                mma_k8<T>(acc[1][j], hi[1][0][0], hi[1][0][1], bf[j]);
-                if constexpr (!DEC) mma_k8<T>(acc[1][j], lo[1][0][0], lo[1][0][1], bf[j]);
-              }
-            }
-          }
-          tr.mark(2);
-          if (ysm) {
-            // y + H . B^T rounded once, written back in place with stmatrix
-            // (the fragments are in the accumulator layout); then the box goes
-            // to global memory by one tensor store (store thread) or this
-            // warp's 16-byte row chunks are stored directly.
+            for (int nt = 0; nt < 4; ++nt)
+              if (nt < ntn) {
 #pragma unroll
-            for (int m = 0; m < 2; ++m)
-              if (m == 0 || m1)
-#pragma unroll
-                for (int jp = 0; jp < 2; ++jp) {
-#pragma unroll
-                  for (int k = 0; k < 4; ++k) {
-                    const float* av = &acc[m][2 * jp + (k >> 1)][(k & 1) * 2];
-                    yf[m][jp][k] = E::pack2(av[0], av[1]);
-                  }
+                for (int m = 0; m < 2; ++m) {
+                  mma_k8<T>(acc[m][nt], bf[2 * m], bf[2 * m + 1], hb[nt][0][0]);
+                  if constexpr (!DEC) mma_k8<T>(acc[m][nt], bf[2 * m], bf[2 * m + 1], hl[nt][0][0]);
                 }
+              }
+          }
+          tr.mark(3);
+          if (ysm) {
+            // back into the y box in place; then the box goes to global memory
+            // by one tensor store (store thread) or this warp's 16-byte row
+            // chunks are stored directly.
 #pragma unroll
-            for (int m = 0; m < 2; ++m)
-              if (m == 0 || m1)
-#pragma unroll
-                for (int jp = 0; jp < 2; ++jp)
-                  stsm_x4(spill ? scratch : sb + xsl + offY[m][jp], yf[m][jp][0], yf[m][jp][1], yf[m][jp][2],
-                          yf[m][jp][3]);
-            tr.mark(3);
+            for (int nt = 0; nt < 4; ++nt)
+              if (nt < ntn) {
+                stsm_x4_t(sb + xsl + offY[nt], E::pack2(acc[0][nt][0], acc[0][nt][1]),
+                          E::pack2(acc[0][nt][2], acc[0][nt][3]), E::pack2(acc[1][nt][0], acc[1][nt][1]),
+                          E::pack2(acc[1][nt][2], acc[1][nt][3]));
+              }
+            tr.mark(4);
             if (tmy) {
               fence_proxy_async_smem();  // the tensor store reads these writes
             } else {
-            __syncwarp();
-            const int sub = lane & 3;
-            const int colw = warp * 32 + sub * 8;  // column of this lane's 16-byte chunk in the stage
-            const int chunk = (warp & 1) * 4 + sub;
-            const uint8_t* ybox = st + xsl;
-            T* ycol = yg + static_cast<int64_t>(s.token_start) * a.y_ld + a.y_off + oc + colw;
-            if (colw + 8 <= wc) {
-              int4 out[4];
+              __syncwarp();
+              const int sub = lane & 3;
+              const int colw = warp * 32 + sub * 8;  // column of this lane's 16-byte chunk in the stage
+              const int chunk = (warp & 1) * 4 + sub;
+              const uint8_t* ybox = st + xsl;
+              T* ycol = yg + static_cast<int64_t>(s.token_start) * a.y_ld + a.y_off + oc + colw;
+              if (colw + 8 <= wc) {
+                int4 out[4];
 #pragma unroll
-              for (int it = 0; it < 4; ++it) {
-                const int row = (lane >> 2) + 8 * it;
-                if (row < n) out[it] = *reinterpret_cast<const int4*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
-              }
+                for (int it = 0; it < 4; ++it) {
+                  const int row = (lane >> 2) + 8 * it;
+                  if (row < n) out[it] = *reinterpret_cast<const int4*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
+                }
 #pragma unroll
-              for (int it = 0; it < 4; ++it) {
-                const int row = (lane >> 2) + 8 * it;
-                if (row < n) *reinterpret_cast<int4*>(ycol + static_cast<int64_t>(row) * a.y_ld) = out[it];
-              }
-            } else if (colw < wc) {
-              for (int it = 0; it < 4; ++it) {
-                const int row = (lane >> 2) + 8 * it;
-                if (row < n) {
-                  const T* src = reinterpret_cast<const T*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
-                  for (int x = 0; x < wc - colw; ++x) ycol[static_cast<int64_t>(row) * a.y_ld + x] = src[x];
+                for (int it = 0; it < 4; ++it) {
+                  const int row = (lane >> 2) + 8 * it;
+                  if (row < n) *reinterpret_cast<int4*>(ycol + static_cast<int64_t>(row) * a.y_ld) = out[it];
+                }
+              } else if (colw < wc) {
+                for (int it = 0; it < 4; ++it) {
+                  const int row = (lane >> 2) + 8 * it;
+                  if (row < n) {
+                    const T* src = reinterpret_cast<const T*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
+                    for (int x = 0; x < wc - colw; ++x) ycol[static_cast<int64_t>(row) * a.y_ld + x] = src[x];
+                  }
                 }
               }
-            }
             }
           } else {
             // y not 16-byte addressable: read and write it directly
 #pragma unroll
             for (int m = 0; m < 2; ++m)
 #pragma unroll
-              for (int j = 0; j < 4; ++j)
+              for (int nt = 0; nt < 4; ++nt)
 #pragma unroll
-                for (int hf = 0; hf < 2; ++hf) {
-                  const int row = m * 16 + g + hf * 8;
-                  const int col = warp * 32 + j * 8 + 2 * c;
-                  if (row < n && col < wc) {
-                    T* yp = yg + static_cast<int64_t>(s.token_start + row) * a.y_ld + a.y_off + oc + col;
-                    const float v0 = E::to_f(yp[0]) + acc[m][j][hf * 2];
-                    yp[0] = E::from_f(v0);
-                    if (col + 1 < wc) yp[1] = E::from_f(E::to_f(yp[1]) + acc[m][j][hf * 2 + 1]);
+                for (int e = 0; e < 4; ++e) {
+                  const int t = nt * 8 + 2 * c + (e & 1);
+                  const int col = warp * 32 + m * 16 + g + (e >> 1) * 8;
+                  if (t < n && col < wc) {
+                    T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + a.y_off + oc + col;
+                    *yp = E::from_f(E::to_f(*yp) + acc[m][nt][e]);
                   }
                 }
           }
         }
-        tr.mark(4);
         if constexpr (DEC) {
           __syncwarp();
           tr.mark(5);

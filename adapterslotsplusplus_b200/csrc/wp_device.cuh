@@ -519,6 +519,20 @@ __device__ __forceinline__ void stsm_x4(uint32_t addr, uint32_t r0, uint32_t r1,
                : "memory");
 }
 
+// Transposing forms: lane (g, c) receives / provides elements [2c][g] and
+// [2c + 1][g] of each stored 8x8 matrix (rows given by the lane addresses).
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr)
+               : "memory");
+}
+__device__ __forceinline__ void stsm_x4_t(uint32_t addr, uint32_t r0, uint32_t r1, uint32_t r2, uint32_t r3) {
+  asm volatile("stmatrix.sync.aligned.m8n8.x4.trans.shared.b16 [%0], {%1, %2, %3, %4};" ::"r"(addr), "r"(r0), "r"(r1),
+               "r"(r2), "r"(r3)
+               : "memory");
+}
+
 // Four 8x8 16-bit matrices from shared memory: lanes 8i..8i+7 give the row
 // addresses (16 contiguous bytes each) of matrix i; r[i] receives this lane's
 // fragment of matrix i (row lane/4, elements 2*(lane%4) and +1).
