@@ -76,6 +76,16 @@ struct wp_handle {
   int reg_dtype = -1;
 
   int* d_err = nullptr;  // device error word (wp::kErr* bits)
+  // balanced decode (split) kernel: shrink partials, H, per-segment counters
+  float* d_part = nullptr;
+  size_t part_bytes = 0;
+  float* d_hsplit = nullptr;
+  size_t hsplit_bytes = 0;
+  int* d_rflag = nullptr;  // per shrink item publication flags (zero between launches)
+  size_t rflag_bytes = 0;
+  int* d_sync = nullptr;  // 3 x cap ints, zero between launches
+  int sync_cap = 0;
+  int split_grid[8] = {};
 
   // store + slots
   std::unordered_map<int32_t, Adapter> store;
@@ -332,6 +342,9 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
   if ((e = cudaHostAlloc(&h->h_reg_maps, sizeof(CUtensorMap) * cap, cudaHostAllocDefault)) != cudaSuccess)
     return bail("registry map upload buffer", e);
   if ((e = cudaMalloc(&h->d_err, sizeof(int) * 4)) != cudaSuccess) return bail("error word", e);
+  if ((e = cudaMalloc(&h->d_sync, sizeof(int) * 3 * cap)) != cudaSuccess) return bail("segment counters", e);
+  cudaMemset(h->d_sync, 0, sizeof(int) * 3 * cap);
+  h->sync_cap = cap;
   cudaMemset(h->d_live_num, 0, sizeof(int) * 4);
   cudaMemset(h->d_reg_num, 0, sizeof(int) * 4);
   cudaMemset(h->d_err, 0, sizeof(int) * 4);
@@ -372,6 +385,10 @@ int wp_destroy(wp_handle* h) {
   cudaFree(h->d_trace[0]);
   cudaFree(h->d_trace[1]);
   cudaFree(h->d_err);
+  cudaFree(h->d_part);
+  cudaFree(h->d_hsplit);
+  cudaFree(h->d_rflag);
+  cudaFree(h->d_sync);
   if (h->reg_uploaded) cudaEventDestroy(h->reg_uploaded);
   if (h->caller_ready) cudaEventDestroy(h->caller_ready);
   if (h->registry_done) cudaEventDestroy(h->registry_done);
@@ -740,14 +757,58 @@ void apply_plan(wp_handle* h, int dtype, int r, bool dec, int* cluster, int* gri
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
-// Kernel variant: the decode kernel (mma.sync) unless WP_KERNEL=tc selects
-// the tcgen05 kernel.
-bool use_decode_kernel() {
-  static const bool dec = [] {
+// Kernel choice: the clustered kernel in its decode (mma.sync) variant.
+// WP_KERNEL=split runs fused live-mode calls on the balanced decode kernel
+// (one CTA per SM, equal stage counts); WP_KERNEL=tc selects the tcgen05
+// variant of the clustered kernel. A tuning and comparison knob.
+int kernel_override() {  // 0: split for fused live calls, 1: clustered decode, 2: clustered tcgen05
+  static const int v = [] {
     const char* env = std::getenv("WP_KERNEL");
-    return !(env && std::strcmp(env, "tc") == 0);
+    if (env && std::strcmp(env, "tc") == 0) return 2;
+    if (env && std::strcmp(env, "split") == 0) return 0;
+    return 1;
   }();
-  return dec;
+  return v;
+}
+bool use_decode_kernel() { return kernel_override() != 2; }
+
+// Makes the split kernel's buffers hold T tokens of nchunk partials of rank r.
+// Outside stream capture they grow as needed; under capture (no allocation
+// allowed) a call that does not fit returns false and runs the clustered
+// kernel instead.
+bool split_buffers(wp_handle* h, int T, int nchunk, int r, cudaStream_t stream) {
+  const size_t part = static_cast<size_t>(T) * nchunk * r * 4;
+  const size_t hs = static_cast<size_t>(T) * r * 4;
+  const size_t rf = static_cast<size_t>(T) * nchunk * 4;
+  if (part <= h->part_bytes && hs <= h->hsplit_bytes && rf <= h->rflag_bytes) return true;
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
+  if (part > h->part_bytes) {
+    cudaStreamSynchronize(stream);
+    cudaFree(h->d_part);
+    h->d_part = nullptr;
+    h->part_bytes = 0;
+    if (cudaMalloc(&h->d_part, part) != cudaSuccess) return false;
+    h->part_bytes = part;
+  }
+  if (hs > h->hsplit_bytes) {
+    cudaStreamSynchronize(stream);
+    cudaFree(h->d_hsplit);
+    h->d_hsplit = nullptr;
+    h->hsplit_bytes = 0;
+    if (cudaMalloc(&h->d_hsplit, hs) != cudaSuccess) return false;
+    h->hsplit_bytes = hs;
+  }
+  if (rf > h->rflag_bytes) {
+    cudaStreamSynchronize(stream);
+    cudaFree(h->d_rflag);
+    h->d_rflag = nullptr;
+    h->rflag_bytes = 0;
+    if (cudaMalloc(&h->d_rflag, rf) != cudaSuccess) return false;
+    if (cudaMemsetAsync(h->d_rflag, 0, rf, stream) != cudaSuccess) return false;
+    h->rflag_bytes = rf;
+  }
+  return true;
 }
 
 // One apply launch. mode: wp::kModeShrink / kModeExpand / kModeFused.
@@ -790,17 +851,41 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
                            y_ld, 8 << i))
         return fail(h, WP_ERR_CUDA, "apply: cuTensorMapEncodeTiled(y) failed");
   }
-  int cluster = 1, grid = 1;
-  const bool dec = use_decode_kernel();
-  apply_plan(h, dtype, r, dec, &cluster, &grid);
-  a.split_len = round_up((std::max(d, 1) + cluster - 1) / cluster, wp::kStageK);
-  a.oslice = round_up((std::max(o, 1) + cluster - 1) / cluster, wp::kStageCols);
   const bool pdl = h->cfg.use_pdl != 0;
   // Without PDL the kernel starts after its predecessor completed, so the
   // table and weights can always be read first. With PDL that needs the
   // caller's promise (prefetch_weights) that the preceding kernel writes no
   // adapter weights, and a preceding kernel that is not the segmenter.
   a.prefetch_weights = !pdl || (h->cfg.prefetch_weights != 0 && !h->last_was_segmenter);
+  const int nchunk = (d + wp::kStageK - 1) / wp::kStageK;
+  const int64_t nchunk_max = std::max<int64_t>(nchunk, (o + wp::kStageCols - 1) / wp::kStageCols);
+  // the split kernel's item arithmetic is 32-bit (items x grid < 2^31) and its
+  // run masks cover 2048 chunks
+  const bool split_fits = static_cast<int64_t>(T) * nchunk_max * h->num_sms < (int64_t{1} << 31) && nchunk_max <= 2048;
+  if (mode == wp::kModeFused && !registry && kernel_override() == 0 && T <= h->sync_cap && split_fits) {
+    const int key = (dtype == WP_DTYPE_BF16 ? 4 : 0) + (r == 8 ? 0 : r == 16 ? 1 : r == 32 ? 2 : 3);
+    if (h->split_grid[key] == 0) h->split_grid[key] = wp::apply_split_max_grid(dtype, r);
+    if (h->split_grid[key] > 0 && split_buffers(h, T, nchunk, r, stream)) {
+      a.part = h->d_part;
+      a.hsplit = h->d_hsplit;
+      a.sync = h->d_sync;
+      a.rflag = h->d_rflag;
+      a.pmax = nchunk;
+      a.sync_cap = h->sync_cap;
+      a.scale = scale;
+      wp::LaunchCfg lc{h->split_grid[key], 1, stream, pdl, true};
+      cudaError_t e = wp::launch_apply_split(dtype, r, a, lc);
+      if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "apply launch (split): %s", cudaGetErrorString(e));
+      ++h->launches;
+      h->last_was_segmenter = false;
+      return WP_OK;
+    }
+  }
+  int cluster = 1, grid = 1;
+  const bool dec = use_decode_kernel();
+  apply_plan(h, dtype, r, dec, &cluster, &grid);
+  a.split_len = round_up((std::max(d, 1) + cluster - 1) / cluster, wp::kStageK);
+  a.oslice = round_up((std::max(o, 1) + cluster - 1) / cluster, wp::kStageCols);
   wp::LaunchCfg lc{grid, cluster, stream, pdl, dec};
   cudaError_t e = wp::launch_apply(dtype, r, a, lc);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "apply launch: %s", cudaGetErrorString(e));

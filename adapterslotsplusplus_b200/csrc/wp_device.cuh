@@ -137,6 +137,30 @@ __device__ __forceinline__ void tma_load_4d(void* dst_smem, const void* tmap, in
       : "memory");
 }
 
+// L2 policy for data streamed once (adapter weights): evict first, so the
+// segment table, activations and H stay resident.
+__device__ __forceinline__ uint64_t l2_evict_first_policy() {
+  uint64_t p;
+  asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;" : "=l"(p));
+  return p;
+}
+__device__ __forceinline__ void tma_load_3d_ef(void* dst_smem, const void* tmap, int c0, int c1, int c2, uint64_t* bar,
+                                               uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3, %4}], [%5], %6;" ::"r"(smem_u32(dst_smem)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+__device__ __forceinline__ void tma_load_4d_ef(void* dst_smem, const void* tmap, int c0, int c1, int c2, int c3,
+                                               uint64_t* bar, uint64_t policy) {
+  asm volatile(
+      "cp.async.bulk.tensor.4d.shared::cluster.global.tile.mbarrier::complete_tx::bytes.L2::cache_hint [%0], [%1, {%2, "
+      "%3, %4, %5}], [%6], %7;" ::"r"(smem_u32(dst_smem)),
+      "l"(tmap), "r"(c0), "r"(c1), "r"(c2), "r"(c3), "r"(smem_u32(bar)), "l"(policy)
+      : "memory");
+}
+
 // Tiled tensor store shared -> global (bulk-group completion).
 __device__ __forceinline__ void tma_store_3d(const void* tmap, int c0, int c1, int c2, const void* src_smem) {
   asm volatile(

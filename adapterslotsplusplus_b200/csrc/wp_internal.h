@@ -74,6 +74,13 @@ struct ApplyArgs {
   int prefetch_weights;  // 1: table and weight loads may start before the dependency wait
   int* err;
   unsigned long long* trace;  // optional per-CTA phase timestamps (kTraceSlots per CTA), else null
+  // split (balanced decode) kernel only
+  float* part;  // shrink partials [T, pmax, r] fp32
+  float* hsplit;  // H [T, r] fp32 (alpha applied)
+  int* sync;  // per-segment counters: H readers done [cap]; zero between launches
+  int* rflag;  // per shrink item: 1 once the run starting at that item published its partial; zero between launches
+  int pmax;  // partial slots per token (>= d / 256 rounded up)
+  int sync_cap;  // segments the counters cover
 };
 
 // Per-CTA trace record (globaltimer ns): start, after the dependency wait,
@@ -103,6 +110,10 @@ struct LaunchCfg {
 // dtype: 0 = f16, 1 = bf16 (WP_DTYPE_*). Launches the clustered apply kernel
 // on `lc.grid` CTAs in clusters of `lc.cluster`. Returns a cudaError_t.
 cudaError_t launch_apply(int dtype, int rank, const ApplyArgs& a, const LaunchCfg& lc);
+// Balanced decode kernel (no clusters): grid = one CTA per SM.
+cudaError_t launch_apply_split(int dtype, int rank, const ApplyArgs& a, const LaunchCfg& lc);
+int apply_split_max_grid(int dtype, int rank);
+
 // Largest co-resident persistent grid for the apply kernel of (dtype, rank)
 // with clusters of `cluster` CTAs (0 if that cluster size cannot be scheduled).
 int apply_max_grid(int dtype, int rank, int cluster, bool dec);
