@@ -43,6 +43,7 @@ class WpConfig(ctypes.Structure):
         ("ctas_per_sm", ctypes.c_int32),
         ("use_pdl", ctypes.c_int32),
         ("prefetch_weights", ctypes.c_int32),
+        ("kernel", ctypes.c_int32),
     ]
 
 

@@ -27,3 +27,7 @@ class WarpPipeConfig:
     prefetch_weights: bool = False
     # cap on persistent CTAs per SM of the apply kernel (0 = as many as fit)
     ctas_per_sm: int = 0
+    # apply kernel of fused live-mode calls: "auto", "cluster" (clustered,
+    # mma.sync), "split" (balanced: one CTA per SM, equal one-stage items),
+    # "tc" (clustered, tcgen05)
+    kernel: str = "auto"

@@ -312,6 +312,7 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
   if (cfg.slot_bytes <= 0) cfg.slot_bytes = static_cast<int64_t>(2) * 64 * 16384 * 2;
   cfg.slot_bytes = (cfg.slot_bytes + 255) / 256 * 256;
   if (cfg.ctas_per_sm < 0) cfg.ctas_per_sm = 0;
+  if (cfg.kernel < 0 || cfg.kernel > 3) return fail(nullptr, WP_ERR_INVALID, "wp_create: kernel must be 0..3");
 
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
@@ -757,20 +758,25 @@ void apply_plan(wp_handle* h, int dtype, int r, bool dec, int* cluster, int* gri
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
-// Kernel choice: the clustered kernel in its decode (mma.sync) variant.
-// WP_KERNEL=split runs fused live-mode calls on the balanced decode kernel
-// (one CTA per SM, equal stage counts); WP_KERNEL=tc selects the tcgen05
-// variant of the clustered kernel. A tuning and comparison knob.
-int kernel_override() {  // 0: split for fused live calls, 1: clustered decode, 2: clustered tcgen05
-  static const int v = [] {
-    const char* env = std::getenv("WP_KERNEL");
-    if (env && std::strcmp(env, "tc") == 0) return 2;
-    if (env && std::strcmp(env, "split") == 0) return 0;
+// Kernel choice (wp_config.kernel; 0 defers to WP_KERNEL, a tuning knob):
+// 1 = clustered decode (mma.sync), 2 = balanced decode ("split") for fused
+// live-mode calls, 3 = clustered tcgen05. Returns 0 for split, 1 for
+// clustered decode, 2 for clustered tcgen05.
+int kernel_choice(const wp_handle* h) {
+  static const int env = [] {
+    const char* e = std::getenv("WP_KERNEL");
+    if (e && std::strcmp(e, "tc") == 0) return 2;
+    if (e && std::strcmp(e, "split") == 0) return 0;
     return 1;
   }();
-  return v;
+  switch (h->cfg.kernel) {
+    case 1: return 1;
+    case 2: return 0;
+    case 3: return 2;
+    default: return env;
+  }
 }
-bool use_decode_kernel() { return kernel_override() != 2; }
+bool use_decode_kernel(const wp_handle* h) { return kernel_choice(h) != 2; }
 
 // Makes the split kernel's buffers hold T tokens of nchunk partials of rank r.
 // Outside stream capture they grow as needed; under capture (no allocation
@@ -862,7 +868,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   // the split kernel's item arithmetic is 32-bit (items x grid < 2^31) and its
   // run masks cover 2048 chunks
   const bool split_fits = static_cast<int64_t>(T) * nchunk_max * h->num_sms < (int64_t{1} << 31) && nchunk_max <= 2048;
-  if (mode == wp::kModeFused && !registry && kernel_override() == 0 && T <= h->sync_cap && split_fits) {
+  if (mode == wp::kModeFused && !registry && kernel_choice(h) == 0 && T <= h->sync_cap && split_fits) {
     const int key = (dtype == WP_DTYPE_BF16 ? 4 : 0) + (r == 8 ? 0 : r == 16 ? 1 : r == 32 ? 2 : 3);
     if (h->split_grid[key] == 0) h->split_grid[key] = wp::apply_split_max_grid(dtype, r);
     if (h->split_grid[key] > 0 && split_buffers(h, T, nchunk, r, stream)) {
@@ -882,7 +888,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
     }
   }
   int cluster = 1, grid = 1;
-  const bool dec = use_decode_kernel();
+  const bool dec = use_decode_kernel(h);
   apply_plan(h, dtype, r, dec, &cluster, &grid);
   a.split_len = round_up((std::max(d, 1) + cluster - 1) / cluster, wp::kStageK);
   a.oslice = round_up((std::max(o, 1) + cluster - 1) / cluster, wp::kStageCols);
@@ -1061,7 +1067,7 @@ int wp_apply_plan(wp_handle* h, int32_t dtype, int32_t rank, int32_t* cluster, i
   if (!rank_ok(rank) || !dtype16(dtype)) return fail(h, WP_ERR_INVALID, "apply_plan: bad rank or dtype");
   DeviceGuard dg(h->device);
   int c = 0, g = 0;
-  apply_plan(h, dtype, rank, use_decode_kernel(), &c, &g);
+  apply_plan(h, dtype, rank, use_decode_kernel(h), &c, &g);
   if (cluster) *cluster = c;
   if (grid) *grid = g;
   return WP_OK;

@@ -64,6 +64,11 @@ typedef struct wp_config {
                                 that the kernel right before an apply call never writes the
                                 adapter weights (true in serving: weights are static during
                                 a step). 0 = strict stream order. */
+  int32_t kernel;            /* apply kernel of fused live-mode calls: 0 = default (clustered
+                                decode variant, or the WP_KERNEL environment variable:
+                                "split", "dec", "tc"), 1 = clustered decode (mma.sync),
+                                2 = balanced decode ("split": one CTA per SM, equal
+                                one-stage items), 3 = clustered tcgen05 */
 } wp_config;
 
 /* One entry of the segment table, as read back by wp_read_seg_table.

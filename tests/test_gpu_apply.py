@@ -22,9 +22,10 @@ ROOT = Path(__file__).resolve().parent.parent
 REF_LIB = ROOT / "oracle" / "_ref" / "libwpref.so"
 
 
-@pytest.fixture(scope="module")
-def engine(cuda):
-    return WarpPipeEngine(WarpPipeConfig(max_tokens=8192))
+@pytest.fixture(scope="module", params=["cluster", "split"])
+def engine(cuda, request):
+    """Both decode kernels: the clustered one and the balanced (split) one."""
+    return WarpPipeEngine(WarpPipeConfig(max_tokens=8192, kernel=request.param))
 
 
 def assert_close(y, y_ref, dtype, what=""):
