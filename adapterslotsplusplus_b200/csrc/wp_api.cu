@@ -84,6 +84,12 @@ struct wp_handle {
   int* d_rflag = nullptr;  // per shrink item publication flags (zero between launches)
   size_t rflag_bytes = 0;
   int* d_sync = nullptr;  // 3 x cap ints, zero between launches
+  // segment count of the latest build_seg_bounds, copied to pinned memory
+  // without a sync; a hint for the automatic kernel choice
+  int* h_nseg = nullptr;
+  cudaEvent_t nseg_ready = nullptr;
+  bool nseg_pending = false;
+  int nseg_hint = -1;
   int sync_cap = 0;
   int split_grid[8] = {};
 
@@ -344,6 +350,9 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
     return bail("registry map upload buffer", e);
   if ((e = cudaMalloc(&h->d_err, sizeof(int) * 4)) != cudaSuccess) return bail("error word", e);
   if ((e = cudaMalloc(&h->d_sync, sizeof(int) * 3 * cap)) != cudaSuccess) return bail("segment counters", e);
+  if ((e = cudaHostAlloc(&h->h_nseg, sizeof(int) * 4, cudaHostAllocDefault)) != cudaSuccess)
+    return bail("segment count buffer", e);
+  cudaEventCreateWithFlags(&h->nseg_ready, cudaEventDisableTiming);
   cudaMemset(h->d_sync, 0, sizeof(int) * 3 * cap);
   h->sync_cap = cap;
   cudaMemset(h->d_live_num, 0, sizeof(int) * 4);
@@ -390,6 +399,8 @@ int wp_destroy(wp_handle* h) {
   cudaFree(h->d_hsplit);
   cudaFree(h->d_rflag);
   cudaFree(h->d_sync);
+  if (h->h_nseg) cudaFreeHost(h->h_nseg);
+  if (h->nseg_ready) cudaEventDestroy(h->nseg_ready);
   if (h->reg_uploaded) cudaEventDestroy(h->reg_uploaded);
   if (h->caller_ready) cudaEventDestroy(h->caller_ready);
   if (h->registry_done) cudaEventDestroy(h->registry_done);
@@ -693,6 +704,15 @@ int wp_build_seg_bounds(wp_handle* h, const void* idx, int32_t idx_dtype, int32_
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "build_seg_bounds launch: %s", cudaGetErrorString(e));
   ++h->launches;
   h->last_was_segmenter = true;
+  // the segment count travels to the host asynchronously (outside graph
+  // capture); later calls read it once it has landed
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone && h->h_nseg &&
+      cudaMemcpyAsync(h->h_nseg, h->d_live_num, sizeof(int), cudaMemcpyDeviceToHost, stream) == cudaSuccess &&
+      cudaEventRecord(h->nseg_ready, stream) == cudaSuccess) {
+    h->nseg_pending = true;
+    h->last_was_segmenter = false;  // the copy sits between the segmenter and the next kernel
+  }
   return WP_OK;
 }
 
@@ -758,16 +778,17 @@ void apply_plan(wp_handle* h, int dtype, int r, bool dec, int* cluster, int* gri
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
-// Kernel choice (wp_config.kernel; 0 defers to WP_KERNEL, a tuning knob):
-// 1 = clustered decode (mma.sync), 2 = balanced decode ("split") for fused
-// live-mode calls, 3 = clustered tcgen05. Returns 0 for split, 1 for
-// clustered decode, 2 for clustered tcgen05.
+// Kernel choice (wp_config.kernel; 0 = automatic, or WP_KERNEL when set, a
+// tuning knob): 1 = clustered decode (mma.sync), 2 = balanced decode
+// ("split") for fused live-mode calls, 3 = clustered tcgen05. Returns 0 for
+// split, 1 for clustered decode, 2 for clustered tcgen05, -1 for automatic.
 int kernel_choice(const wp_handle* h) {
   static const int env = [] {
     const char* e = std::getenv("WP_KERNEL");
     if (e && std::strcmp(e, "tc") == 0) return 2;
     if (e && std::strcmp(e, "split") == 0) return 0;
-    return 1;
+    if (e && (std::strcmp(e, "dec") == 0 || std::strcmp(e, "cluster") == 0)) return 1;
+    return -1;
   }();
   switch (h->cfg.kernel) {
     case 1: return 1;
@@ -775,6 +796,28 @@ int kernel_choice(const wp_handle* h) {
     case 3: return 2;
     default: return env;
   }
+}
+
+// Automatic choice for a fused live-mode call: the clustered kernel gives
+// every segment one cluster (a second one when clusters are left over), so
+// its time follows the busiest cluster; the balanced kernel spreads every
+// segment over the whole GPU at the price of a flag exchange through L2.
+// Measured on B200: balance wins when the segments leave at least half of
+// the clusters idle, or exceed the clusters by 30% (several segments per
+// cluster); in between, one segment per cluster wins. The segment count is
+// the latest segmenter's (read without a sync); before one has landed, the
+// bound min(T, A + ceil(T / 32)) for A adapters among T tokens stands in.
+bool auto_split(wp_handle* h, cudaStream_t stream, int T, int64_t num_adapters, int clusters) {
+  cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
+  if (h->nseg_pending && cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone &&
+      cudaEventQuery(h->nseg_ready) == cudaSuccess) {
+    h->nseg_hint = *h->h_nseg;
+    h->nseg_pending = false;
+  }
+  cudaGetLastError();  // a not-ready query is not an error
+  int64_t nseg = h->nseg_hint;
+  if (nseg < 0) nseg = std::min<int64_t>(T, std::max<int64_t>(num_adapters, 1) + (T + wp::kSegTokens - 1) / wp::kSegTokens);
+  return nseg * 2 <= clusters || nseg * 10 >= static_cast<int64_t>(clusters) * 13;
 }
 bool use_decode_kernel(const wp_handle* h) { return kernel_choice(h) != 2; }
 
@@ -868,7 +911,13 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   // the split kernel's item arithmetic is 32-bit (items x grid < 2^31) and its
   // run masks cover 2048 chunks
   const bool split_fits = static_cast<int64_t>(T) * nchunk_max * h->num_sms < (int64_t{1} << 31) && nchunk_max <= 2048;
-  if (mode == wp::kModeFused && !registry && kernel_choice(h) == 0 && T <= h->sync_cap && split_fits) {
+  bool want_split = kernel_choice(h) == 0;
+  if (kernel_choice(h) < 0 && mode == wp::kModeFused && !registry) {
+    int c0 = 1, g0 = 1;
+    apply_plan(h, dtype, r, true, &c0, &g0);
+    want_split = auto_split(h, stream, T, num_adapters, g0 / std::max(c0, 1));
+  }
+  if (mode == wp::kModeFused && !registry && want_split && T <= h->sync_cap && split_fits) {
     const int key = (dtype == WP_DTYPE_BF16 ? 4 : 0) + (r == 8 ? 0 : r == 16 ? 1 : r == 32 ? 2 : 3);
     if (h->split_grid[key] == 0) h->split_grid[key] = wp::apply_split_max_grid(dtype, r);
     if (h->split_grid[key] > 0 && split_buffers(h, T, nchunk, r, stream)) {

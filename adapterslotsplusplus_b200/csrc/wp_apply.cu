@@ -225,9 +225,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const bool do_ex = (a.mode & kModeExpand) != 0;
   const int kA0 = static_cast<int>(q) * a.split_len;
   const int nA = do_sh ? (max(0, min(a.split_len, a.d - kA0)) + C::KC - 1) / C::KC : 0;
-  const int oB0 = static_cast<int>(q) * a.oslice;
-  const int nB = do_ex ? (max(0, min(a.oslice, a.o - oB0)) + C::W - 1) / C::W : 0;
-  const int ups = nA + nB;  // stages per segment for this CTA
+  // this CTA's expand columns (a helper cluster may take half of a segment's
+  // output columns; see read_table)
+  int oB0 = static_cast<int>(q) * a.oslice;
+  int nB = do_ex ? (max(0, min(a.oslice, a.o - oB0)) + C::W - 1) / C::W : 0;
+  int ups = nA + nB;  // stages per segment for this CTA
   // decode variant: the y box of an expand stage goes back to global memory
   // with one tensor store when its rows are exactly the segment's rows
   auto y_by_tma = [&](int n) -> bool {
@@ -241,11 +243,19 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   // position r*G + c, or r*G + G-1-c on odd rounds), which pairs the largest
   // segments with the smallest on the same cluster; larger tables go round
   // robin (cluster c takes c, c + G, ...).
+  // Segments per cluster, for small tables (decode) ordered by decreasing
+  // token count. Fewer segments than clusters: the largest segments get a
+  // helper cluster each, and the pair splits the segment's output columns
+  // (both clusters run the shrink; the second reads A mostly from L2).
+  // More segments than clusters: they are dealt in "snake" order (round r
+  // gives cluster c the segment at sorted position r*G + c, or r*G + G-1-c on
+  // odd rounds), pairing large segments with small ones. Larger tables go
+  // round robin (cluster c takes c, c + G, ...).
   auto read_table = [&]() {
     const int nseg = __ldcg(a.num_segs);
-    if (G > 1 && nseg > G && nseg <= kSnakeMax) {
-      int* cnt = reinterpret_cast<int*>(Hs);  // scratch: the H tile is idle until the first exchange
-      int* order = cnt + kSnakeMax;
+    int* cnt = reinterpret_cast<int*>(Hs);  // scratch: the H tile is idle until the first exchange
+    int* order = cnt + kSnakeMax;
+    auto sort_by_size = [&]() {
       for (int t = tid; t < nseg; t += kThreads) cnt[t] = __ldcg(&a.segs[t].token_count);
       __syncthreads();
       for (int t = tid; t < nseg; t += kThreads) {
@@ -255,6 +265,28 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         order[p] = t;
       }
       __syncthreads();
+    };
+    const int osplit = (((a.o + 1) / 2) + C::W - 1) / C::W * C::W;  // first column of a segment's second half
+    if (do_ex && G > 1 && nseg > 0 && nseg < G && nseg <= kSnakeMax && a.o - osplit >= static_cast<int>(CL) * C::W) {
+      sort_by_size();
+      const int helpers = min(nseg, G - nseg);
+      const int V = nseg + helpers;
+      nmine = cid < V ? 1 : 0;
+      if (nmine) {
+        const int pos = cid < 2 * helpers ? cid >> 1 : cid - helpers;
+        const int half = cid < 2 * helpers ? (cid & 1) : -1;
+        const int ob = half == 1 ? osplit : 0;
+        const int olen = half < 0 ? a.o : (half == 0 ? osplit : a.o - osplit);
+        const int osl = (olen + static_cast<int>(CL) - 1) / static_cast<int>(CL);
+        const int oslr = (osl + C::W - 1) / C::W * C::W;
+        oB0 = ob + static_cast<int>(q) * oslr;
+        nB = (max(0, min(oslr, ob + olen - oB0)) + C::W - 1) / C::W;
+        ups = nA + nB;
+        for (int j = tid; j < 2; j += kThreads)
+          sdesc[j] = __ldcg(reinterpret_cast<const int4*>(a.segs + order[pos]) + (j & 1));
+      }
+    } else if (G > 1 && nseg > G && nseg <= kSnakeMax) {
+      sort_by_size();
       const int rounds = (nseg + G - 1) / G;
       nmine = 0;
       for (int r = 0; r < rounds; ++r) {
