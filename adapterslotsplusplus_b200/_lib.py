@@ -64,6 +64,7 @@ SIGNATURES = {
     "wp_last_error": (ctypes.c_char_p, [_vp]),
     "wp_rank_supported": (_int, [_i32]),
     "wp_kernel_launch_count": (_i64, [_vp]),
+    "wp_last_apply_kernel": (ctypes.c_int32, [ctypes.c_void_p]),
     "wp_register_adapter": (_int, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _i32]),
     "wp_register_adapter_host": (_int, [_vp, _i32, _vp, _vp, _i32, _i32, _i32, _f32, _i32]),
     "wp_evict_adapter": (_int, [_vp, _i32]),

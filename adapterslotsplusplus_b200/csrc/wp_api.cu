@@ -90,6 +90,7 @@ struct wp_handle {
   cudaEvent_t nseg_ready = nullptr;
   bool nseg_pending = false;
   int nseg_hint = -1;
+  int last_kernel = -1;  // wp_last_apply_kernel
   int sync_cap = 0;
   int split_grid[8] = {};
 
@@ -307,6 +308,8 @@ int wp_set_global_error(int code, const char* msg) {
 int wp_rank_supported(int32_t rank) { return rank_ok(rank) ? 1 : 0; }
 
 int64_t wp_kernel_launch_count(const wp_handle* h) { return h ? h->launches : 0; }
+
+int32_t wp_last_apply_kernel(const wp_handle* h) { return h ? h->last_kernel : -1; }
 
 int wp_create(const wp_config* cfg_in, wp_handle** out) {
   if (!out) return fail(nullptr, WP_ERR_INVALID, "wp_create: out is NULL");
@@ -931,6 +934,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
       wp::LaunchCfg lc{h->split_grid[key], 1, stream, pdl, true};
       cudaError_t e = wp::launch_apply_split(dtype, r, a, lc);
       if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "apply launch (split): %s", cudaGetErrorString(e));
+      h->last_kernel = 0;
       ++h->launches;
       h->last_was_segmenter = false;
       return WP_OK;
@@ -944,6 +948,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   wp::LaunchCfg lc{grid, cluster, stream, pdl, dec};
   cudaError_t e = wp::launch_apply(dtype, r, a, lc);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "apply launch: %s", cudaGetErrorString(e));
+  h->last_kernel = dec ? 1 : 2;
   ++h->launches;
   h->last_was_segmenter = false;
   return WP_OK;

@@ -266,6 +266,12 @@ class WarpPipeEngine:
         self._check(self._lib.wp_apply_plan(self._h, _DTYPES[dtype], int(rank), ctypes.byref(c), ctypes.byref(g)))
         return c.value, g.value
 
+    def last_apply_kernel(self) -> str:
+        """Name of the kernel of the latest apply launch ("split_kernel" or
+        "apply_kernel"), or "" before the first one."""
+        k = int(self._lib.wp_last_apply_kernel(self._h))
+        return {0: "split_kernel", 1: "apply_kernel", 2: "apply_kernel"}.get(k, "")
+
     def kernel_launches(self) -> int:
         return int(self._lib.wp_kernel_launch_count(self._h))
 

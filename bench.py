@@ -44,10 +44,10 @@ RANK = 32
 TOKENS = 256
 RESIDENT = 64
 SEED = 1
-# (name, d_in, d_out, input activation)
-PROJS = [("q", HIDDEN, HIDDEN, "h"), ("k", HIDDEN, HIDDEN, "h"), ("v", HIDDEN, HIDDEN, "h"),
-         ("o", HIDDEN, HIDDEN, "attn"), ("gate", HIDDEN, INTER, "h"), ("up", HIDDEN, INTER, "h"),
-         ("down", INTER, HIDDEN, "inter")]
+# (name, d_in, d_out, input activation, tensor-parallel kind)
+PROJS = [("q", HIDDEN, HIDDEN, "h", "col"), ("k", HIDDEN, HIDDEN, "h", "col"), ("v", HIDDEN, HIDDEN, "h", "col"),
+         ("o", HIDDEN, HIDDEN, "attn", "row"), ("gate", HIDDEN, INTER, "h", "col"), ("up", HIDDEN, INTER, "h", "col"),
+         ("down", INTER, HIDDEN, "inter", "row")]
 WORKLOAD = "llama2-7b decode step: 32 layers x 7 LoRA projections, rank 32, bf16, 64 resident, 256 tokens, Zipf(1.1) seed 1"
 METRIC = "LoRA apply us/decode-step (HBM GB/s vs peak), 7B x 32 layers, r32, 64 resident, T=256"
 
@@ -61,12 +61,22 @@ def algorithmic_bytes(U: int, T: int, d: int, o: int, r: int, elt: int = 2) -> t
     return shrink, expand
 
 
-def step_bytes(U: int, T: int, r: int = RANK) -> tuple[int, int]:
+def step_bytes(U: int, T: int, r: int = RANK, world: int = 1) -> tuple[int, int]:
+    """Algorithmic bytes of one step on one rank of a tensor-parallel group of
+    `world` (world = 1: the whole model). Column-parallel projections split
+    B and y along out_features; row-parallel ones split x and A along d_in
+    and exchange the [T, r] fp32 partials (counted as read + write)."""
     s = e = 0
-    for _, d, o, _ in PROJS:
+    for _, d, o, _, kind in PROJS:
+        if world > 1 and kind == "col":
+            o = o // world
+        elif world > 1:
+            d = d // world
         bs, be = algorithmic_bytes(U, T, d, o, r)
         s += bs
         e += be
+        if world > 1 and kind == "row":
+            e += 2 * T * r * 4
     return s * LAYERS, e * LAYERS
 
 
@@ -143,27 +153,35 @@ def make_ids(resident: int, T: int = TOKENS, seed: int = SEED) -> np.ndarray:
 
 
 class Stack:
-    """Device-resident stacked LoRA weights + activations of the 7B stack."""
+    """Device-resident stacked LoRA weights + activations of the 7B stack, as
+    rank `rank` of a tensor-parallel group of `world` holds them."""
 
-    def __init__(self, device, resident, layers=LAYERS, T=TOKENS, dtype=torch.bfloat16, seed=0):
-        g = torch.Generator(device=device).manual_seed(seed)
+    def __init__(self, device, resident, layers=LAYERS, T=TOKENS, dtype=torch.bfloat16, seed=0, rank=0, world=1):
+        g = torch.Generator(device=device).manual_seed(seed + 1000 * rank)
         self.layers = []
         for _ in range(layers):
             L = {}
-            for name, d, o, _ in PROJS:
-                wa = torch.randn(resident, 1, RANK, d, device=device, dtype=dtype, generator=g) * 0.02
-                wb = torch.randn(resident, 1, o, RANK, device=device, dtype=dtype, generator=g) * 0.02
-                L[name] = (wa, wb, torch.zeros(T, o, device=device, dtype=dtype))
+            for name, d, o, _, kind in PROJS:
+                dl, ol = d, o
+                if world > 1 and kind == "col":
+                    ol = o // world
+                elif world > 1:
+                    dl = d // world
+                wa = torch.randn(resident, 1, RANK, dl, device=device, dtype=dtype, generator=g) * 0.02
+                wb = torch.randn(resident, 1, ol, RANK, device=device, dtype=dtype, generator=g) * 0.02
+                L[name] = (wa, wb, torch.zeros(T, ol, device=device, dtype=dtype))
+            dh = HIDDEN // world if world > 1 else HIDDEN
+            di = INTER // world if world > 1 else INTER
             L["x"] = {"h": torch.randn(T, HIDDEN, device=device, dtype=dtype, generator=g) * 0.1,
-                      "attn": torch.randn(T, HIDDEN, device=device, dtype=dtype, generator=g) * 0.1,
-                      "inter": torch.randn(T, INTER, device=device, dtype=dtype, generator=g) * 0.1}
+                      "attn": torch.randn(T, dh, device=device, dtype=dtype, generator=g) * 0.1,
+                      "inter": torch.randn(T, di, device=device, dtype=dtype, generator=g) * 0.1}
             self.layers.append(L)
 
     def calls(self):
         for L in self.layers:
-            for name, d, o, src in PROJS:
+            for name, d, o, src, kind in PROJS:
                 wa, wb, y = L[name]
-                yield y, L["x"][src], wa, wb
+                yield kind, y, L["x"][src], wa, wb
 
 
 def capture(fn, warm=2):
@@ -210,12 +228,25 @@ def run_ours(args, rank, world, local_rank):
     ids = make_ids(RESIDENT)
     U = int(np.unique(ids).size)
     idx_dev = torch.as_tensor(ids, device=device)
-    stack = Stack(device, RESIDENT)
+    stack = Stack(device, RESIDENT, rank=rank, world=world)
     calls = list(stack.calls())
+    tpa = None
+    if world > 1:
+        # tensor parallel over the N GPUs: column-parallel projections expand
+        # their own output columns, row-parallel ones all-reduce the shrink
+        # partials over NCCL (libwp_b200.so's own communicator)
+        from adapterslotsplusplus_b200.tp import TensorParallelApply
+
+        tpa = TensorParallelApply(eng)
 
     def full_step():
-        for y, x, wa, wb in calls:
-            eng.add_lora_packed(y, x, wa, wb, scale)
+        for kind, y, x, wa, wb in calls:
+            if tpa is None:
+                eng.add_lora_packed(y, x, wa, wb, scale)
+            elif kind == "col":
+                tpa.column_parallel(y, x, wa, wb, scale)
+            else:
+                tpa.row_parallel(y, x, wa, wb, scale)
 
     seg = lambda: eng.build_seg_bounds(idx_dev)  # noqa: E731
     seg()
@@ -242,7 +273,7 @@ def run_ours(args, rank, world, local_rank):
     # and a read back of one output row, all on the stream, every step.
     ids_host = torch.as_tensor(ids).pin_memory()
     out_host = torch.empty(HIDDEN, dtype=torch.bfloat16).pin_memory()
-    y_last = calls[-1][0]
+    y_last = calls[-1][1]
 
     def e2e_step():
         idx_dev.copy_(ids_host, non_blocking=True)
@@ -262,17 +293,19 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.synchronize()
     e2e_ms = max(st.elapsed_time(en), (time.perf_counter() - t0) * 1e3) / args.steps
 
-    shr_b, exp_b = step_bytes(U, TOKENS)
-    total_b = shr_b + exp_b
+    shr_b, exp_b = step_bytes(U, TOKENS, world=world)
+    total_b = (shr_b + exp_b) * world  # whole job: every rank's share of the step
     peaks = measured_peaks()
     hbm = peaks.get("hbm_gbs")
     peak_src = "measured" if hbm else "fallback"
     hbm = hbm or 6650.0
-    # dominant kernel: apply_kernel (one launch per call; the segmenter is one
-    # launch per step). Per launch: the mean over the 224 calls of the step.
-    dom = "apply_kernel"
-    per_launch_ms = ms_apply / (LAYERS * len(PROJS))
-    per_launch_b = total_b / (LAYERS * len(PROJS))
+    # dominant kernel: the apply kernel (one launch per call; the segmenter is
+    # one launch per step). Per launch: the mean over the calls of the step on
+    # one rank.
+    dom = eng.last_apply_kernel() or "apply_kernel"
+    launches_per_step = LAYERS * sum(1 if (world == 1 or k == "col") else 2 for *_, k in PROJS)
+    per_launch_ms = ms_apply / launches_per_step
+    per_launch_b = total_b / world / launches_per_step
     achieved = per_launch_b / (per_launch_ms * 1e-3) / 1e9
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
@@ -291,18 +324,18 @@ def run_ours(args, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
         "higher_is_better": False,
-        "scaling": "weak",
+        "scaling": "strong" if world > 1 else "weak",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded random weights and activations, Zipf(1.1) routing)",
         "config": {"workload": WORKLOAD, "layers": LAYERS, "projections": len(PROJS), "rank": RANK,
                    "resident_adapters": RESIDENT, "active_adapters": U, "tokens": TOKENS,
-                   "parallelism": f"replicas{world}" if world > 1 else "single",
+                   "parallelism": f"tp{world}" if world > 1 else "single",
                    "l2": "inputs exceed L2 (10.2 GB of adapter weights per step), no flush needed"},
         "step_gbs": round(total_b / (ms * 1e-3) / 1e9, 1),
         "step_frac_of_hbm": round(total_b / (ms * 1e-3) / 1e9 / hbm, 4),
         "step_bytes": total_b,
-        "kernels_ms_per_step": {"apply_kernel": round(ms_apply, 4), "segmenter_and_gaps": round(ms - ms_apply, 4)},
+        "kernels_ms_per_step": {dom: round(ms_apply, 4), "segmenter_and_gaps": round(ms - ms_apply, 4)},
         "apply_plan": {"cluster": plan[0], "ctas": plan[1]},
         "roofline": {"bound": "hbm", "kernel": dom, "achieved": round(achieved, 1), "peak": hbm,
                      "peak_source": peak_src, "unit": "GB/s", "frac": round(achieved / hbm, 4),
@@ -310,11 +343,13 @@ def run_ours(args, rank, world, local_rank):
                      "launch_us": round(per_launch_ms * 1e3, 3)},
         "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "us/step", "h2d_bytes_per_step": int(ids.nbytes),
                 "d2h_bytes_per_step": int(out_host.numel() * 2),
-                "path": "WarpPipeEngine.build_seg_bounds + graph of 224 add_lora_packed calls"},
-        "gpu_launches": args.steps * (1 + LAYERS * len(PROJS)),
+                "path": "WarpPipeEngine.build_seg_bounds + graph of the step's apply calls (tensor-parallel over NCCL when N > 1)"},
+        "gpu_launches": args.steps * (1 + launches_per_step),
         "clocks": clk.summary(),
     }
     del g_full, stack, calls
+    if tpa is not None:
+        tpa.close()
     torch.cuda.empty_cache()
     return eng, result
 
@@ -332,7 +367,7 @@ def sweep_resident(eng, device, counts, steps):
         calls = list(stack.calls())
 
         def step():
-            for y, x, wa, wb in calls:
+            for _, y, x, wa, wb in calls:
                 eng.add_lora_packed(y, x, wa, wb, scale)
 
         eng.build_seg_bounds(idx)
@@ -373,7 +408,7 @@ def cpu_reference_layers(n_layers: int, resident: int = RESIDENT, threads: int |
     weights = []
     for _ in range(n_layers):
         L = {}
-        for name, d, o, _ in PROJS:
+        for name, d, o, *_ in PROJS:
             L[name] = ((torch.randn(resident, RANK, d, generator=g) * 0.02).bfloat16(),
                        (torch.randn(resident, o, RANK, generator=g) * 0.02).bfloat16(),
                        (torch.randn(TOKENS, d, generator=g) * 0.1).bfloat16(),
@@ -382,7 +417,7 @@ def cpu_reference_layers(n_layers: int, resident: int = RESIDENT, threads: int |
     scale = 16.0 / RANK
 
     def one_layer(L):
-        for name, d, o, _ in PROJS:
+        for name, d, o, *_ in PROJS:
             wa, wb, x, y = L[name]
             yf = y.float()
             for aid, s, n in table:

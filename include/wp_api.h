@@ -98,6 +98,11 @@ const char* wp_last_error(const wp_handle* h);
  * 1 for r in {8,16,32,64}, else 0. */
 int wp_rank_supported(int32_t rank);
 
+/* Kernel of the latest apply launch: 0 = balanced decode ("split_kernel"),
+ * 1 = clustered decode ("apply_kernel", mma.sync variant), 2 = clustered
+ * tcgen05 ("apply_kernel"), -1 = none yet. For reports and profiling. */
+int32_t wp_last_apply_kernel(const wp_handle* h);
+
 /* Number of kernels this handle has launched so far (all entry points). */
 int64_t wp_kernel_launch_count(const wp_handle* h);
 
