@@ -12,6 +12,17 @@ implies against the measured peak. One JSON line on rank 0.
 
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-sweep]
 
+With N > 1 (launched under torch.distributed.run, one rank per GPU) the same
+step runs tensor-parallel over the N GPUs: column-parallel projections (q, k,
+v, gate, up) expand their own out_features slice, row-parallel ones (o, down)
+shrink their d_in slice and all-reduce the fp32 [T, r] partials over NCCL
+(strong scaling; the time is the max over ranks).
+
+  python bench.py --profile-case q|gate|down [--launches 12] [--kernel auto|cluster|split|tc]
+
+runs a few launches of one projection of the step and exits (a small case
+for profilers).
+
 --impl reference times the reference's CPU implementation of the path (its
 torch per-segment fp32 math, tests/correctness/reference_bgmv.py:4-18,
 restated in oracle/apply.py) on the host cores, on a bounded sample of the
@@ -457,6 +468,32 @@ def run_reference(args, rank, world):
     }
 
 
+def profile_case(args):
+    """A few launches of one projection of the workload, for profilers: the
+    decode-step call shape (T = 256, Zipf routing over 64 resident adapters,
+    rank 32) with 8 rotating weight sets (larger than L2 together)."""
+    from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
+
+    shapes = {"q": (HIDDEN, HIDDEN), "gate": (HIDDEN, INTER), "down": (INTER, HIDDEN)}
+    d, o = shapes[args.profile_case]
+    device = torch.device("cuda", 0)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True, kernel=args.kernel), device=device)
+    g = torch.Generator(device=device).manual_seed(0)
+    sets = [(torch.randn(RESIDENT, 1, RANK, d, device=device, dtype=torch.bfloat16, generator=g) * 0.02,
+             torch.randn(RESIDENT, 1, o, RANK, device=device, dtype=torch.bfloat16, generator=g) * 0.02)
+            for _ in range(8)]
+    x = torch.randn(TOKENS, d, device=device, dtype=torch.bfloat16, generator=g) * 0.1
+    y = torch.zeros(TOKENS, o, device=device, dtype=torch.bfloat16)
+    eng.build_seg_bounds(torch.as_tensor(make_ids(RESIDENT), device=device))
+    torch.cuda.synchronize()
+    for i in range(args.launches):
+        wa, wb = sets[i % len(sets)]
+        eng.add_lora_packed(y, x, wa, wb, 16.0 / RANK)
+    torch.cuda.synchronize()
+    print(json.dumps({"profile_case": args.profile_case, "launches": args.launches, "kernel": eng.last_apply_kernel(),
+                      "d": d, "o": o, "tokens": TOKENS, "rank": RANK}), flush=True)
+
+
 def main():
     ap = argparse.ArgumentParser()
     ap.add_argument("--gpus", type=int, default=1)
@@ -465,7 +502,15 @@ def main():
     ap.add_argument("--impl", choices=["ours", "reference"], default="ours")
     ap.add_argument("--no-sweep", action="store_true")
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the cpu_baseline sample")
+    ap.add_argument("--profile-case", choices=["q", "gate", "down"], default=None,
+                    help="run a few launches of one projection (for profilers) and exit")
+    ap.add_argument("--launches", type=int, default=12, help="launches of --profile-case")
+    ap.add_argument("--kernel", choices=["auto", "cluster", "split", "tc"], default="auto",
+                    help="apply kernel of --profile-case")
     args = ap.parse_args()
+    if args.profile_case:
+        profile_case(args)
+        return
     args.warmup = max(args.warmup, 3)
 
     world = int(os.environ.get("WORLD_SIZE", "1"))
