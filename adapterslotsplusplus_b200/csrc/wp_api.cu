@@ -91,6 +91,9 @@ struct wp_handle {
   bool nseg_pending = false;
   int nseg_hint = -1;
   int last_kernel = -1;  // wp_last_apply_kernel
+  // the segmenter's per-cluster assignment of the live table for plan_g clusters
+  wp::ClusterPlan* d_plan = nullptr;
+  int plan_g = 0;
   int sync_cap = 0;
   int split_grid[8] = {};
 
@@ -355,6 +358,8 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
   if ((e = cudaMalloc(&h->d_sync, sizeof(int) * 3 * cap)) != cudaSuccess) return bail("segment counters", e);
   if ((e = cudaHostAlloc(&h->h_nseg, sizeof(int) * 4, cudaHostAllocDefault)) != cudaSuccess)
     return bail("segment count buffer", e);
+  if ((e = cudaMalloc(&h->d_plan, sizeof(wp::ClusterPlan))) != cudaSuccess) return bail("cluster plan", e);
+  cudaMemset(h->d_plan, 0, sizeof(wp::ClusterPlan));
   cudaEventCreateWithFlags(&h->nseg_ready, cudaEventDisableTiming);
   cudaMemset(h->d_sync, 0, sizeof(int) * 3 * cap);
   h->sync_cap = cap;
@@ -402,6 +407,7 @@ int wp_destroy(wp_handle* h) {
   cudaFree(h->d_hsplit);
   cudaFree(h->d_rflag);
   cudaFree(h->d_sync);
+  cudaFree(h->d_plan);
   if (h->h_nseg) cudaFreeHost(h->h_nseg);
   if (h->nseg_ready) cudaEventDestroy(h->nseg_ready);
   if (h->reg_uploaded) cudaEventDestroy(h->reg_uploaded);
@@ -694,6 +700,12 @@ int wp_build_segments(wp_handle* h, const int32_t* ids, const int32_t* offs, int
   return WP_OK;
 }
 
+}  // extern "C"
+namespace {
+void apply_plan(wp_handle* h, int dtype, int r, bool dec, int* cluster, int* grid);
+}  // namespace
+extern "C" {
+
 int wp_build_seg_bounds(wp_handle* h, const void* idx, int32_t idx_dtype, int32_t T, void* stream_v) {
   if (!h) return fail(nullptr, WP_ERR_INVALID, "build_seg_bounds: NULL handle");
   if (idx_dtype != WP_DTYPE_I32 && idx_dtype != WP_DTYPE_I64)
@@ -703,7 +715,16 @@ int wp_build_seg_bounds(wp_handle* h, const void* idx, int32_t idx_dtype, int32_
   if (T > 0 && !idx) return fail(h, WP_ERR_INVALID, "build_seg_bounds: NULL indices");
   DeviceGuard dg(h->device);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
-  cudaError_t e = wp::launch_seg_bounds(idx, idx_dtype, T, h->d_live, h->d_live_num, h->d_run_starts, stream);
+  if (h->plan_g == 0) {
+    // the clustered decode plan of the common case (bf16, rank 32): every
+    // rank plans the same cluster count on B200, and a launch whose count
+    // differs ignores the assignment
+    int c = 1, g = 1;
+    apply_plan(h, WP_DTYPE_BF16, 32, true, &c, &g);
+    h->plan_g = g / std::max(c, 1);
+  }
+  cudaError_t e = wp::launch_seg_bounds(idx, idx_dtype, T, h->d_live, h->d_live_num, h->d_plan, h->plan_g,
+                                        h->d_run_starts, stream);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "build_seg_bounds launch: %s", cudaGetErrorString(e));
   ++h->launches;
   h->last_was_segmenter = true;
@@ -872,6 +893,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   wp::ApplyArgs a{};
   a.segs = segs;
   a.num_segs = nseg;
+  a.plan = (!registry && segs == h->d_live) ? h->d_plan : nullptr;
   a.h = H;
   a.mode = mode;
   a.registry = registry;

@@ -251,7 +251,46 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   // gives cluster c the segment at sorted position r*G + c, or r*G + G-1-c on
   // odd rounds), pairing large segments with small ones. Larger tables go
   // round robin (cluster c takes c, c + G, ...).
+  // The segmenter's plan (one load round: header, this cluster's count,
+  // half and descriptors together) replaces all of this when it was made for
+  // this launch's cluster count.
+  auto helper_range = [&](int half) {
+    const int osplit = (((a.o + 1) / 2) + C::W - 1) / C::W * C::W;
+    const int ob = half == 1 ? osplit : 0;
+    const int olen = half < 0 ? a.o : (half == 0 ? osplit : a.o - osplit);
+    const int osl = (olen + static_cast<int>(CL) - 1) / static_cast<int>(CL);
+    const int oslr = (osl + C::W - 1) / C::W * C::W;
+    oB0 = ob + static_cast<int>(q) * oslr;
+    nB = (max(0, min(oslr, ob + olen - oB0)) + C::W - 1) / C::W;
+    ups = nA + nB;
+  };
+  auto read_plan = [&]() -> bool {
+    int4* sh = reinterpret_cast<int4*>(Ps);  // scratch: header, count, half
+    if (tid == 0) sh[0] = __ldcg(&a.plan->hdr);
+    if (tid == 1) reinterpret_cast<int*>(sh + 1)[0] = __ldcg(&a.plan->count[min(cid, kPlanMaxClusters - 1)]);
+    if (tid == 2) reinterpret_cast<int*>(sh + 1)[1] = __ldcg(&a.plan->half[min(cid, kPlanMaxClusters - 1)]);
+    if (tid >= 32 && tid < 32 + 2 * kPlanRounds) {
+      const int j = tid - 32;
+      const int slot = min((j >> 1) * G + cid, kPlanRounds * kPlanMaxClusters - 1);
+      sdesc[j] = __ldcg(reinterpret_cast<const int4*>(&a.plan->seg[slot]) + (j & 1));
+    }
+    __syncthreads();
+    const int4 hdr = sh[0];
+    const int count = reinterpret_cast<const int*>(sh + 1)[0];
+    const int half = reinterpret_cast<const int*>(sh + 1)[1];
+    __syncthreads();
+    if (hdr.x == 0 || hdr.z != G || cid >= kPlanMaxClusters) return false;
+    if (hdr.x == 1) {
+      // helper halves need an expand and room for a split of the output columns
+      const int osplit = (((a.o + 1) / 2) + C::W - 1) / C::W * C::W;
+      if (!do_ex || a.o - osplit < static_cast<int>(CL) * C::W) return false;
+      if (count > 0) helper_range(half);
+    }
+    nmine = min(count, kPlanRounds);  // rounds r sit at slot r * G + cid, all loaded above
+    return true;
+  };
   auto read_table = [&]() {
+    if (a.plan && read_plan()) return;
     const int nseg = __ldcg(a.num_segs);
     int* cnt = reinterpret_cast<int*>(Hs);  // scratch: the H tile is idle until the first exchange
     int* order = cnt + kSnakeMax;
@@ -777,7 +816,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           }
         }
         named_sync(kBarCompute, kComputeThreads);  // slots read, H complete
-        if (tid == 0 && CL > 1)
+        // release the slots for the push two segments on (none after the last two)
+        if (tid == 0 && CL > 1 && sj + 2 < nmine)
           for (uint32_t i = 1; i < CL; ++i) mbar_arrive_remote_relaxed(mapa(smem_u32(&rx_free[par]), (q + i) % CL));
         tr.seg(2, sj);
       } else {
@@ -1129,9 +1169,13 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   }
 
   if constexpr (DEC) {
-    // peers may still write this CTA's receive slots and barriers until they
-    // pass this barrier; the shared memory must outlive those accesses
-    if (CL > 1 && !cluster_barrier_bounded(cbar, cph, CL, kBarCompute, kComputeThreads, a.err)) *s_bad = 1;
+    // Peers arrive on this CTA's barrier until they pass this one, so the
+    // shared memory must outlive it. Their other remote accesses (pushes into
+    // the receive slots, slot releases) were all observed before: every push
+    // was consumed, and the releases of the last two segments are not sent.
+    // No data crosses this barrier, so it needs no release fence (a fence
+    // would wait for this thread's outstanding y stores).
+    if (CL > 1 && !cluster_barrier_relaxed_bounded(cbar, cph, CL, kBarCompute, kComputeThreads, a.err)) *s_bad = 1;
   }
   if (*s_bad) {
     // drain: copies may still be in flight into stages issued but not consumed

@@ -324,6 +324,30 @@ __device__ __forceinline__ bool cluster_barrier_bounded(uint64_t* bar, uint32_t 
   return ok;
 }
 
+// Cluster barrier for the end of a kernel: the same bounded mbarrier protocol
+// without release semantics (no fence), for a point where the cluster only
+// needs every CTA to have arrived -- e.g. to keep shared memory alive until
+// peers stop arriving on it -- and no data written before it is read after.
+__device__ __forceinline__ bool cluster_barrier_relaxed_bounded(uint64_t* bar, uint32_t parity, uint32_t ncta,
+                                                                int bar_id, int nthreads, int* err) {
+  named_sync(bar_id, nthreads);
+  if (threadIdx.x == 0) {
+    const uint32_t local = smem_u32(bar);
+    for (uint32_t r = 0; r < ncta; ++r) mbar_arrive_remote_relaxed(mapa(local, r));
+  }
+  bool ok = mbar_try_wait_cluster(bar, parity);
+  if (!ok) {
+    const unsigned long long t0 = global_timer_ns();
+    while (!(ok = mbar_try_wait_cluster(bar, parity))) {
+      if (global_timer_ns() - t0 > kWaitTimeoutNs) {
+        if (err) atomicOr(err, kErrWaitTimeout);
+        break;
+      }
+    }
+  }
+  return ok;
+}
+
 // ---- 5th-generation tensor cores (tcgen05) and tensor memory -------------
 
 // Allocates `ncols` (power of two >= 32) TMEM columns for this CTA; one full

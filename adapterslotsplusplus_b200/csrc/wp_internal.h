@@ -37,6 +37,23 @@ constexpr int kBoxCols = 64;
 constexpr int kStageK = 256;
 constexpr int kStageCols = 256;
 
+// Per-cluster work assignment of the clustered apply kernel, computed once
+// per step by the segmenter for one cluster count G: segments ordered by
+// decreasing token count; mode 1 (fewer segments than clusters) gives the
+// largest segments a helper cluster that takes half of their output columns,
+// mode 2 (up to kPlanMaxSegs segments) deals them in snake order; mode 0:
+// no plan (the kernel deals round robin). Slot r * G + c holds round r of
+// cluster c.
+constexpr int kPlanRounds = 4;
+constexpr int kPlanMaxClusters = 160;
+constexpr int kPlanMaxSegs = 128;
+struct ClusterPlan {
+  int4 hdr;  // x: mode, y: segments, z: G, w: helper count (mode 1)
+  int count[kPlanMaxClusters];  // segments of cluster c
+  int half[kPlanMaxClusters];  // mode 1: -1 whole segment, 0 / 1 first / second half of the output columns
+  DevSeg seg[kPlanRounds * kPlanMaxClusters];
+};
+
 // Which halves of the apply one launch runs.
 enum : int { kModeShrink = 1, kModeExpand = 2, kModeFused = 3 };
 
@@ -80,6 +97,7 @@ struct ApplyArgs {
   int* sync;  // per-segment counters: H readers done [cap]; zero between launches
   int* rflag;  // per shrink item: 1 once the run starting at that item published its partial; zero between launches
   int pmax;  // partial slots per token (>= d / 256 rounded up)
+  const ClusterPlan* plan;  // clustered kernel: the segmenter's assignment for this table, or null
   int sync_cap;  // segments the counters cover
 };
 
@@ -119,7 +137,8 @@ int apply_split_max_grid(int dtype, int rank);
 int apply_max_grid(int dtype, int rank, int cluster, bool dec);
 
 // idx_dtype: WP_DTYPE_I32 or WP_DTYPE_I64.
-cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs,
+cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs, ClusterPlan* plan,
+                              int plan_g,
                               int* run_starts, cudaStream_t stream);
 
 }  // namespace wp

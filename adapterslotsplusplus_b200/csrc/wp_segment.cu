@@ -56,10 +56,62 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_buf, int* t
   return excl;
 }
 
+// Pass 3: the clustered apply kernel's per-cluster assignment for G
+// clusters (ClusterPlan). Segments are ranked by decreasing token count
+// (ties by position); fewer segments than clusters: position p of the
+// first `helpers` goes to clusters 2p and 2p + 1 (output-column halves),
+// the rest to one cluster each; more: round r gives cluster c the segment
+// at position r*G + c (r*G + G-1-c on odd rounds).
+__device__ void write_cluster_plan(const DevSeg* segs, int nseg, ClusterPlan* plan, int G) {
+  __shared__ int order[kPlanMaxSegs];
+  const int tid = threadIdx.x;
+  int mode = 0;
+  if (G > 1 && G <= kPlanMaxClusters && nseg > 0 && nseg <= kPlanMaxSegs && nseg != G &&
+      (nseg + G - 1) / G <= kPlanRounds)
+    mode = nseg < G ? 1 : 2;
+  const int helpers = mode == 1 ? min(nseg, G - nseg) : 0;
+  if (mode) {
+    if (tid < nseg) {
+      const int ct = segs[tid].token_count;
+      int p = 0;
+      for (int j = 0; j < nseg; ++j) {
+        const int cj = segs[j].token_count;
+        p += (cj > ct || (cj == ct && j < tid)) ? 1 : 0;
+      }
+      order[p] = tid;
+    }
+    __syncthreads();
+    for (int c = tid; c < G; c += kSegThreads) {
+      plan->half[c] = -1;
+      int n = 0;
+      if (mode == 1) {
+        const int V = nseg + helpers;
+        if (c < V) {
+          const int pos = c < 2 * helpers ? c >> 1 : c - helpers;
+          plan->half[c] = c < 2 * helpers ? (c & 1) : -1;
+          plan->seg[c] = segs[order[pos]];
+          n = 1;
+        }
+      } else {
+        for (int r = 0; r < kPlanRounds; ++r) {
+          const int p = r * G + ((r & 1) ? G - 1 - c : c);
+          if (p < nseg) {
+            plan->seg[r * G + c] = segs[order[p]];
+            n = r + 1;
+          }
+        }
+      }
+      plan->count[c] = n;
+    }
+  }
+  __syncthreads();
+  if (tid == 0) plan->hdr = make_int4(mode, nseg, G, helpers);
+}
+
 template <typename I>
 __global__ void __launch_bounds__(kSegThreads, 1)
     seg_bounds_kernel(const I* __restrict__ idx, int T, DevSeg* __restrict__ segs, int* __restrict__ num_segs,
-                      int* __restrict__ run_starts) {
+                      int* __restrict__ run_starts, ClusterPlan* __restrict__ plan, int plan_g) {
   __shared__ int warp_buf[33];
   const int tid = threadIdx.x;
 
@@ -107,16 +159,20 @@ __global__ void __launch_bounds__(kSegThreads, 1)
     nseg += total;
   }
   if (tid == 0) *num_segs = nseg;
+  if (plan) {
+    __syncthreads();  // the table (global memory, written by this block) is complete
+    write_cluster_plan(segs, nseg, plan, plan_g);
+  }
 }
 
-cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs,
-                              int* run_starts, cudaStream_t stream) {
+cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs, ClusterPlan* plan,
+                              int plan_g, int* run_starts, cudaStream_t stream) {
   if (idx_dtype == 4) {
     seg_bounds_kernel<int64_t><<<1, kSegThreads, 0, stream>>>(static_cast<const int64_t*>(idx), T, segs,
-                                                               num_segs, run_starts);
+                                                               num_segs, run_starts, plan, plan_g);
   } else {
     seg_bounds_kernel<int32_t><<<1, kSegThreads, 0, stream>>>(static_cast<const int32_t*>(idx), T, segs,
-                                                               num_segs, run_starts);
+                                                               num_segs, run_starts, plan, plan_g);
   }
   return cudaGetLastError();
 }

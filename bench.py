@@ -468,6 +468,40 @@ def run_reference(args, rank, world):
     }
 
 
+def prefill_mix(device, kernels=("cluster", "split", "tc"), iters=10):
+    """BASELINE config 2's prefill mix on one 4096 -> 4096 projection: 4096
+    tokens in 8 contiguous 512-token runs (8 adapters), rank 32, bf16. Per
+    kernel: device us per call (CUDA graph of one call, 8 rotating weight
+    sets) and the HBM GB/s of its algorithmic bytes."""
+    from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
+
+    T, n_ad = 4096, 8
+    ids = np.repeat(np.arange(n_ad), T // n_ad).astype(np.int64)
+    g = torch.Generator(device=device).manual_seed(3)
+    sets = [(torch.randn(n_ad, 1, RANK, HIDDEN, device=device, dtype=torch.bfloat16, generator=g) * 0.02,
+             torch.randn(n_ad, 1, HIDDEN, RANK, device=device, dtype=torch.bfloat16, generator=g) * 0.02)
+            for _ in range(8)]
+    x = torch.randn(T, HIDDEN, device=device, dtype=torch.bfloat16, generator=g) * 0.1
+    y = torch.zeros(T, HIDDEN, device=device, dtype=torch.bfloat16)
+    sb, eb = algorithmic_bytes(n_ad, T, HIDDEN, HIDDEN, RANK)
+    out = {}
+    for kern in kernels:
+        eng = WarpPipeEngine(WarpPipeConfig(max_tokens=T, prefetch_weights=True, kernel=kern), device=device)
+        eng.build_seg_bounds(torch.as_tensor(ids, device=device))
+
+        def step():
+            for wa, wb in sets:
+                eng.add_lora_packed(y, x, wa, wb, 16.0 / RANK)
+
+        gr = capture(step, warm=1)
+        ms = time_graph(gr, None, iters) / len(sets)
+        out[kern] = {"us_per_call": round(ms * 1e3, 2), "gbs": round((sb + eb) / (ms * 1e-3) / 1e9, 1),
+                     "kernel": eng.last_apply_kernel()}
+        del gr, eng
+    return {"tokens": T, "runs": f"{n_ad} x {T // n_ad}", "d": HIDDEN, "o": HIDDEN, "rank": RANK,
+            "algorithmic_mb": round((sb + eb) / 1e6, 1), "per_kernel": out}
+
+
 def profile_case(args):
     """A few launches of one projection of the workload, for profilers: the
     decode-step call shape (T = 256, Zipf routing over 64 resident adapters,
@@ -507,9 +541,13 @@ def main():
     ap.add_argument("--launches", type=int, default=12, help="launches of --profile-case")
     ap.add_argument("--kernel", choices=["auto", "cluster", "split", "tc"], default="auto",
                     help="apply kernel of --profile-case")
+    ap.add_argument("--prefill-mix", action="store_true", help="time config 2's prefill mix per kernel and exit")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args)
+        return
+    if args.prefill_mix:
+        print(json.dumps(prefill_mix(torch.device("cuda", 0))), flush=True)
         return
     args.warmup = max(args.warmup, 3)
 
