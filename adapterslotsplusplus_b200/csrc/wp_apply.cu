@@ -367,6 +367,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   if (warp == kProducerWarp) {
     // ======================= producer warp ===================================
     if (lane == 0) {
+      const uint64_t ef = l2_evict_first_policy();  // adapter weights stream through L2 once
       // parts: 1 = arm the stage's barrier and load the weights, 2 = load the activations
       auto issue = [&](int u, int stage, int parts) {
         const DevSeg s = desc(u / ups);
@@ -383,10 +384,10 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
             const void* amap = a.registry ? s.a : static_cast<const void*>(&a.tmap_a);
             const int aid = a.registry ? 0 : s.adapter_id;
             if (a.d_sliced) {
-              tma_load_4d(st, amap, 0, 0, k0 / kBoxCols, aid, bar);
+              tma_load_4d_ef(st, amap, 0, 0, k0 / kBoxCols, aid, bar, ef);
             } else {
 #pragma unroll
-              for (int j = 0; j < 4; ++j) tma_load_3d(st + j * C::ABOX, amap, k0 + j * kBoxCols, 0, aid, bar);
+              for (int j = 0; j < 4; ++j) tma_load_3d_ef(st + j * C::ABOX, amap, k0 + j * kBoxCols, 0, aid, bar, ef);
             }
           }
           if (parts & 2) {
@@ -407,7 +408,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
               mbar_arrive_expect_tx(bar, 256 * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
               const void* bmap = a.registry ? s.b : static_cast<const void*>(&a.tmap_b);
               const int bid = a.registry ? 0 : s.adapter_id;
-              tma_load_3d(st + 4 * C::XBOX, bmap, 0, oc, bid, bar);
+              tma_load_3d_ef(st + 4 * C::XBOX, bmap, 0, oc, bid, bar, ef);
             } else {
               mbar_arrive_expect_tx(bar, wc * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
               const T* B = a.registry ? static_cast<const T*>(s.b)
