@@ -77,6 +77,9 @@ SIGNATURES = {
     "wp_expand": (_int, [_vp, _vp, _vp, _i32, _i32, _i32, _i32, _vp]),
     "wp_add_lora": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _f32, _i32, _i32, _i32, _i32, _i64, _i64,
                            _i32, _i32, _vp]),
+    "wp_add_lora_slices": (_int, [_vp, _vp, _vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_i64),
+                                  ctypes.POINTER(_vp), ctypes.POINTER(_i64), ctypes.POINTER(_i32), _i32, _f32,
+                                  _i32, _i32, _i32, _i32, _i64, _i64, _i32, _vp]),
     "wp_add_lora_shrink": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _i32, _i32, _i32, _i64, _i32, _vp]),
     "wp_add_lora_expand": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32, _i32, _vp]),
     "wp_prefetch_adapter": (_i32, [_vp, _i32]),

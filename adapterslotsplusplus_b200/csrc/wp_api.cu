@@ -1110,6 +1110,96 @@ int wp_add_lora(wp_handle* h, void* y, const void* x, const void* wa_base, int64
                   static_cast<cudaStream_t>(stream_v));
 }
 
+// Several output slices that share x (vLLM's add_lora_packed_nslice: q/k/v,
+// gate/up) in ONE clustered launch: slice s adds x . A_s^T . B_s^T into
+// y[:, y_offsets[s] : y_offsets[s] + out_features]. Every slice has the same
+// rank, d_model and out_features; the kernel treats (slice, segment) pairs as
+// its work items, so the slices overlap instead of running back to back.
+int wp_add_lora_slices(wp_handle* h, void* y, const void* x, int32_t nslices, const void* const* wa_bases,
+                       const int64_t* wa_strides, const void* const* wb_bases, const int64_t* wb_strides,
+                       const int32_t* y_offsets, int32_t num_adapters, float scale, int32_t T, int32_t d_model,
+                       int32_t out_features, int32_t rank, int64_t x_ld, int64_t y_ld, int32_t dtype,
+                       void* stream_v) {
+  if (!h) return fail(nullptr, WP_ERR_INVALID, "add_lora_slices: NULL handle");
+  if (nslices < 1 || nslices > wp::kMaxSlices)
+    return fail(h, WP_ERR_INVALID, "add_lora_slices: %d slices outside [1, %d]", nslices, wp::kMaxSlices);
+  if (!wa_bases || !wa_strides || !wb_bases || !wb_strides || !y_offsets)
+    return fail(h, WP_ERR_INVALID, "add_lora_slices: NULL slice arrays");
+  int rc = check_live(h, T, rank, dtype);
+  for (int s = 0; !rc && s < nslices; ++s) {
+    rc = check_shrink_args(h, x, x_ld, d_model, wa_bases[s], wa_strides[s], num_adapters);
+    if (!rc) rc = check_expand_args(h, y, y_ld, y_offsets[s], out_features, wb_bases[s], wb_strides[s]);
+  }
+  if (rc) return rc;
+  DeviceGuard dg(h->device);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (nslices == 1 || kernel_choice(h) == 2)  // one slice, or the tcgen05 kernel: plain calls
+    for (int s = 0; s < nslices; ++s) {
+      rc = do_apply(h, wp::kModeFused, 0, h->d_live, h->d_live_num, T, rank, dtype, x, x_ld, d_model, wa_bases[s],
+                    wa_strides[s], num_adapters, scale, y, y_ld, y_offsets[s], out_features, wb_bases[s],
+                    wb_strides[s], nullptr, stream);
+      if (rc) return rc;
+    }
+  if (nslices == 1 || kernel_choice(h) == 2) return WP_OK;
+  if (T == 0) return WP_OK;
+  wp::ApplyArgs a{};
+  a.segs = h->d_live;
+  a.num_segs = h->d_live_num;
+  a.plan = nullptr;  // the precomputed plan covers one slice only
+  a.mode = wp::kModeFused;
+  a.scale = scale;
+  a.err = h->d_err;
+  a.trace = h->trace_on ? h->d_trace[0] : nullptr;
+  a.d = d_model;
+  a.d_sliced = sliced(d_model) ? 1 : 0;
+  a.nslices = nslices;
+  const int64_t L = std::max<int32_t>(1, num_adapters);
+  for (int i = 0; i < 3; ++i)
+    if (!encode_rows_map(&a.tmap_x[i], dtype, x, d_model, T, x_ld, 8 << i))
+      return fail(h, WP_ERR_CUDA, "add_lora_slices: cuTensorMapEncodeTiled(x) failed");
+  a.y = y;
+  a.y_ld = y_ld;
+  a.o = out_features;
+  a.o_sliced = sliced(out_features) ? 1 : 0;
+  a.y_tma = al16(y) && (y_ld % 8 == 0);
+  for (int s = 0; s < nslices; ++s) a.y_tma = a.y_tma && y_offsets[s] % 8 == 0;
+  for (int s = 0; s < nslices; ++s) {
+    CUtensorMap* am = s ? &a.tmap_a_x[s - 1] : &a.tmap_a;
+    CUtensorMap* bm = s ? &a.tmap_b_x[s - 1] : &a.tmap_b;
+    CUtensorMap* ym = s ? a.tmap_y_x[s - 1] : a.tmap_y;
+    if (!encode_a_map(am, dtype, wa_bases[s], d_model, rank, L, wa_strides[s]))
+      return fail(h, WP_ERR_CUDA, "add_lora_slices: cuTensorMapEncodeTiled(wa_t_all) failed");
+    if (rank >= 16 && !encode_b_map(bm, dtype, wb_bases[s], out_features, rank, L, wb_strides[s]))
+      return fail(h, WP_ERR_CUDA, "add_lora_slices: cuTensorMapEncodeTiled(wb_t_all) failed");
+    for (int i = 0; a.y_tma && i < 3; ++i)
+      if (!encode_rows_map(&ym[i], dtype, static_cast<const char*>(y) + static_cast<int64_t>(y_offsets[s]) * 2,
+                           out_features, T, y_ld, 8 << i))
+        return fail(h, WP_ERR_CUDA, "add_lora_slices: cuTensorMapEncodeTiled(y) failed");
+    if (s == 0) {
+      a.y_off = y_offsets[0];
+      a.wb_base = wb_bases[0];
+      a.wb_stride = wb_strides[0];
+    } else {
+      a.y_off_x[s - 1] = y_offsets[s];
+      a.wb_base_x[s - 1] = wb_bases[s];
+      a.wb_stride_x[s - 1] = wb_strides[s];
+    }
+  }
+  const bool pdl = h->cfg.use_pdl != 0;
+  a.prefetch_weights = !pdl || (h->cfg.prefetch_weights != 0 && !h->last_was_segmenter);
+  int cluster = 1, grid = 1;
+  apply_plan(h, dtype, rank, true, &cluster, &grid);
+  a.split_len = round_up((std::max<int>(d_model, 1) + cluster - 1) / cluster, wp::kStageK);
+  a.oslice = round_up((std::max<int>(out_features, 1) + cluster - 1) / cluster, wp::kStageCols);
+  wp::LaunchCfg lc{grid, cluster, stream, pdl, true};
+  cudaError_t e = wp::launch_apply(dtype, rank, a, lc);
+  if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "add_lora_slices launch: %s", cudaGetErrorString(e));
+  h->last_kernel = 1;
+  ++h->launches;
+  h->last_was_segmenter = false;
+  return WP_OK;
+}
+
 // ---- tracing -------------------------------------------------------------------
 
 int wp_trace_enable(wp_handle* h, int32_t enable) {

@@ -138,6 +138,7 @@ struct ApplyCfg {
   static_assert(STAGES >= 2 && STAGES <= 8 && SMEM <= kSmemMax, "shared memory budget");
   static_assert(32 * PITCH * 4 >= kComputeWarps * 128, "the P tile holds one scratch row per compute warp");
   static_assert(32 * PITCH * 4 >= 2 * kSnakeMax * 4, "the H tile holds the table-ordering scratch");
+  static_assert(!DEC || PW >= 4 * kSnakeMax * 4, "the partial slots hold the table-ordering scratch");
 };
 
 template <typename T, int R, bool DEC>
@@ -211,6 +212,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     if ((a.mode & kModeExpand) && a.y_tma)
       for (int i = 0; i < 3; ++i) prefetch_tmap(&a.tmap_y[i]);
     if ((a.mode & kModeExpand) && C::BTMA && !a.registry) prefetch_tmap(&a.tmap_b);
+    for (int sl = 1; sl < a.nslices && sl < kMaxSlices; ++sl) {
+      prefetch_tmap(&a.tmap_a_x[sl - 1]);
+      if (C::BTMA) prefetch_tmap(&a.tmap_b_x[sl - 1]);
+      if (a.y_tma)
+        for (int i = 0; i < 3; ++i) prefetch_tmap(&a.tmap_y_x[sl - 1][i]);
+    }
   }
   // TMEM: shrink accumulator (columns 0-31) and two expand accumulators of two
   // 128 x 32 halves each (columns 64-127 and 128-191)
@@ -289,13 +296,28 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     nmine = min(count, kPlanRounds);  // rounds r sit at slot r * G + cid, all loaded above
     return true;
   };
+  // Multi-slice calls: virtual segment v is segment v % nseg of slice
+  // v / nseg; its descriptor carries the slice in the (live-mode unused)
+  // alpha field.
+  const int S_sl = a.nslices > 1 ? a.nslices : 1;
+  int nseg_t = 0;  // segments of the table (not virtual)
+  auto put_desc = [&](int slot, int v) {
+    const int seg = v % nseg_t;
+    int4 x0 = __ldcg(reinterpret_cast<const int4*>(a.segs + seg));
+    const int4 x1 = __ldcg(reinterpret_cast<const int4*>(a.segs + seg) + 1);
+    if (S_sl > 1) x0.w = v / nseg_t;
+    sdesc[2 * slot] = x0;
+    sdesc[2 * slot + 1] = x1;
+  };
   auto read_table = [&]() {
-    if (a.plan && read_plan()) return;
-    const int nseg = __ldcg(a.num_segs);
-    int* cnt = reinterpret_cast<int*>(Hs);  // scratch: the H tile is idle until the first exchange
-    int* order = cnt + kSnakeMax;
+    if (S_sl == 1 && a.plan && read_plan()) return;
+    nseg_t = __ldcg(a.num_segs);
+    const int nseg = S_sl * nseg_t;  // virtual segments
+    constexpr int kSortMax = DEC ? 2 * kSnakeMax : kSnakeMax;  // scratch: decode: the partial slots; else the H tile
+    int* cnt = DEC ? reinterpret_cast<int*>(Pw) : reinterpret_cast<int*>(Hs);
+    int* order = cnt + kSortMax;
     auto sort_by_size = [&]() {
-      for (int t = tid; t < nseg; t += kThreads) cnt[t] = __ldcg(&a.segs[t].token_count);
+      for (int t = tid; t < nseg; t += kThreads) cnt[t] = __ldcg(&a.segs[t % nseg_t].token_count);
       __syncthreads();
       for (int t = tid; t < nseg; t += kThreads) {
         const int ct = cnt[t];
@@ -306,7 +328,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       __syncthreads();
     };
     const int osplit = (((a.o + 1) / 2) + C::W - 1) / C::W * C::W;  // first column of a segment's second half
-    if (do_ex && G > 1 && nseg > 0 && nseg < G && nseg <= kSnakeMax && a.o - osplit >= static_cast<int>(CL) * C::W) {
+    if (do_ex && G > 1 && nseg > 0 && nseg < G && nseg <= kSortMax && a.o - osplit >= static_cast<int>(CL) * C::W) {
       sort_by_size();
       const int helpers = min(nseg, G - nseg);
       const int V = nseg + helpers;
@@ -321,10 +343,9 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         oB0 = ob + static_cast<int>(q) * oslr;
         nB = (max(0, min(oslr, ob + olen - oB0)) + C::W - 1) / C::W;
         ups = nA + nB;
-        for (int j = tid; j < 2; j += kThreads)
-          sdesc[j] = __ldcg(reinterpret_cast<const int4*>(a.segs + order[pos]) + (j & 1));
+        if (tid == 0) put_desc(0, order[pos]);
       }
-    } else if (G > 1 && nseg > G && nseg <= kSnakeMax) {
+    } else if (G > 1 && nseg > G && nseg <= kSortMax) {
       sort_by_size();
       const int rounds = (nseg + G - 1) / G;
       nmine = 0;
@@ -332,22 +353,29 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         const int p = r * G + ((r & 1) ? G - 1 - cid : cid);
         if (p < nseg) nmine = r + 1;  // positions grow with r, so the items are rounds 0..nmine-1
       }
-      for (int j = tid; j < 2 * nmine; j += kThreads) {
-        const int r = j >> 1;
-        const int p = r * G + ((r & 1) ? G - 1 - cid : cid);
-        sdesc[j] = __ldcg(reinterpret_cast<const int4*>(a.segs + order[p]) + (j & 1));
-      }
+      for (int r = tid; r < min(nmine, kDescCache); r += kThreads)
+        put_desc(r, order[r * G + ((r & 1) ? G - 1 - cid : cid)]);
     } else {
       nmine = nseg > cid ? (nseg - cid + G - 1) / G : 0;
-      const int cached = min(nmine, kDescCache);
-      for (int j = tid; j < 2 * cached; j += kThreads)
-        sdesc[j] = __ldcg(reinterpret_cast<const int4*>(a.segs + cid + (j >> 1) * G) + (j & 1));
+      for (int r = tid; r < min(nmine, kDescCache); r += kThreads) put_desc(r, cid + r * G);
     }
     __syncthreads();
   };
   auto desc = [&](int j) -> DevSeg {
-    if (j >= kDescCache) return load_seg(a.segs, cid + j * G);
+    if (j >= kDescCache) {  // round robin beyond the cache (tables larger than the snake limit)
+      const int v = cid + j * G;
+      if (S_sl == 1) return load_seg(a.segs, v);
+      DevSeg d = load_seg(a.segs, v % nseg_t);
+      d.alpha = __int_as_float(v / nseg_t);
+      return d;
+    }
     return unpack_seg(sdesc[2 * j], sdesc[2 * j + 1]);  // shared-memory copy
+  };
+  // slice of a (live-mode) descriptor
+  auto slice_of = [&](const DevSeg& d) -> int { return S_sl > 1 ? __float_as_int(d.alpha) : 0; };
+  auto yoff_of = [&](const DevSeg& d) -> int {
+    const int sl = slice_of(d);
+    return sl ? a.y_off_x[sl - 1] : a.y_off;
   };
 
   if (a.prefetch_weights) {
@@ -381,7 +409,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           const int k0 = kA0 + sub * C::KC;
           if (parts & 1) {
             mbar_arrive_expect_tx(bar, 4 * C::ABOX + 4 * box_bytes);
-            const void* amap = a.registry ? s.a : static_cast<const void*>(&a.tmap_a);
+            const int sl = slice_of(s);
+            const void* amap = a.registry ? s.a : static_cast<const void*>(sl ? &a.tmap_a_x[sl - 1] : &a.tmap_a);
             const int aid = a.registry ? 0 : s.adapter_id;
             if (a.d_sliced) {
               tma_load_4d_ef(st, amap, 0, 0, k0 / kBoxCols, aid, bar, ef);
@@ -406,24 +435,28 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
             if constexpr (C::BTMA) {
               // one 256-row box of B, rows past o zero-filled
               mbar_arrive_expect_tx(bar, 256 * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
-              const void* bmap = a.registry ? s.b : static_cast<const void*>(&a.tmap_b);
+              const int sl = slice_of(s);
+              const void* bmap = a.registry ? s.b : static_cast<const void*>(sl ? &a.tmap_b_x[sl - 1] : &a.tmap_b);
               const int bid = a.registry ? 0 : s.adapter_id;
               tma_load_3d_ef(st + 4 * C::XBOX, bmap, 0, oc, bid, bar, ef);
             } else {
               mbar_arrive_expect_tx(bar, wc * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
+              const int sl = slice_of(s);
               const T* B = a.registry ? static_cast<const T*>(s.b)
-                                      : static_cast<const T*>(a.wb_base) +
-                                            static_cast<int64_t>(s.adapter_id) * a.wb_stride;
+                                      : static_cast<const T*>(sl ? a.wb_base_x[sl - 1] : a.wb_base) +
+                                            static_cast<int64_t>(s.adapter_id) * (sl ? a.wb_stride_x[sl - 1] : a.wb_stride);
               bulk_g2s(st + 4 * C::XBOX, B + static_cast<int64_t>(oc) * R, wc * R * 2, bar);
             }
           }
           if ((parts & 2) && a.y_tma) {
             if (a.o_sliced) {
-              tma_load_3d(st, &a.tmap_y[bi], 0, s.token_start, oc / kBoxCols, bar);
+              tma_load_3d(st, slice_of(s) ? &a.tmap_y_x[slice_of(s) - 1][bi] : &a.tmap_y[bi], 0, s.token_start,
+                          oc / kBoxCols, bar);
             } else {
 #pragma unroll
               for (int j = 0; j < 4; ++j)
-                tma_load_2d(st + j * box_bytes, &a.tmap_y[bi], oc + j * kBoxCols, s.token_start, bar);
+                tma_load_2d(st + j * box_bytes, slice_of(s) ? &a.tmap_y_x[slice_of(s) - 1][bi] : &a.tmap_y[bi],
+                            oc + j * kBoxCols, s.token_start, bar);
             }
           }
         }
@@ -493,7 +526,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           const bool ok = wait_ok(&ydone[stage], (ypar >> stage) & 1u);
           ypar ^= 1u << stage;
           if (ok) {
-            tma_store_3d(&a.tmap_y[box_index(n)], 0, s.token_start, (oB0 + i * C::W) / kBoxCols,
+            tma_store_3d(slice_of(s) ? &a.tmap_y_x[slice_of(s) - 1][box_index(n)] : &a.tmap_y[box_index(n)], 0,
+                         s.token_start, (oB0 + i * C::W) / kBoxCols,
                          stage_base + stage * C::STAGE);
             bulk_commit();
             bulk_wait_read();
@@ -968,7 +1002,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
               const float4 d0 = reinterpret_cast<const float4*>(dr)[0];
               const float4 d1 = reinterpret_cast<const float4*>(dr)[1];
               const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
-              T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + a.y_off + oc + col;
+              T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + yoff_of(s) + oc + col;
               if (a.y_tma) {
                 const int4 yv = *reinterpret_cast<const int4*>(yb + t * 128 + ((cib ^ (t & 7)) << 4));
                 const uint32_t* yw = reinterpret_cast<const uint32_t*>(&yv);
@@ -1117,7 +1151,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
               const int colw = warp * 32 + sub * 8;  // column of this lane's 16-byte chunk in the stage
               const int chunk = (warp & 1) * 4 + sub;
               const uint8_t* ybox = st + xsl;
-              T* ycol = yg + static_cast<int64_t>(s.token_start) * a.y_ld + a.y_off + oc + colw;
+              T* ycol = yg + static_cast<int64_t>(s.token_start) * a.y_ld + yoff_of(s) + oc + colw;
               if (colw + 8 <= wc) {
                 int4 out[4];
 #pragma unroll
@@ -1151,7 +1185,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
                   const int t = nt * 8 + 2 * c + (e & 1);
                   const int col = warp * 32 + m * 16 + g + (e >> 1) * 8;
                   if (t < n && col < wc) {
-                    T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + a.y_off + oc + col;
+                    T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + yoff_of(s) + oc + col;
                     *yp = E::from_f(E::to_f(*yp) + acc[m][nt][e]);
                   }
                 }

@@ -54,6 +54,9 @@ struct ClusterPlan {
   DevSeg seg[kPlanRounds * kPlanMaxClusters];
 };
 
+// Slices of one multi-slice call (q, k, v of a fused qkv projection).
+constexpr int kMaxSlices = 3;
+
 // Which halves of the apply one launch runs.
 enum : int { kModeShrink = 1, kModeExpand = 2, kModeFused = 3 };
 
@@ -70,6 +73,11 @@ struct ApplyArgs {
   CUtensorMap tmap_y[3];  // y columns [y_off, y_off + o) x T rows, 8 << i rows per box
   CUtensorMap tmap_a;  // live mode: A stack [L, r, d]
   CUtensorMap tmap_b;  // live mode, r >= 16: B stack [L, o, r], box r x 256 x 1, swizzle = 2r bytes
+  // multi-slice calls (nslices > 1, clustered kernel, live mode): slices 1
+  // and 2 share x and the table; their A / B stacks and y column ranges
+  CUtensorMap tmap_a_x[kMaxSlices - 1];
+  CUtensorMap tmap_b_x[kMaxSlices - 1];
+  CUtensorMap tmap_y_x[kMaxSlices - 1][3];
   const DevSeg* segs;
   const int* num_segs;
   float* h;  // shrink-only: H [T, r] fp32 written; expand-only: read
@@ -97,6 +105,10 @@ struct ApplyArgs {
   int* sync;  // per-segment counters: H readers done [cap]; zero between launches
   int* rflag;  // per shrink item: 1 once the run starting at that item published its partial; zero between launches
   int pmax;  // partial slots per token (>= d / 256 rounded up)
+  int nslices;  // 1, or up to kMaxSlices slices sharing x (virtual segment v = slice * segments + segment)
+  int y_off_x[kMaxSlices - 1];  // y column offset of slices 1, 2
+  const void* wb_base_x[kMaxSlices - 1];  // rank-8 bulk B of slices 1, 2
+  int64_t wb_stride_x[kMaxSlices - 1];
   const ClusterPlan* plan;  // clustered kernel: the segmenter's assignment for this table, or null
   int sync_cap;  // segments the counters cover
 };

@@ -208,6 +208,51 @@ class WarpPipeEngine:
             int(x2d.stride(0)), int(y2d.stride(0)), off, dt, _stream_ptr(x.device)))
         return True
 
+    def add_lora_packed_nslice(self, y, x, lora_a_stacked, lora_b_stacked, scale, output_slices) -> bool:
+        """vLLM's PunicaWrapper.add_lora_packed_nslice in one launch: slice s
+        (lora_a_stacked[s] [L, 1, rank, d], lora_b_stacked[s] [L, 1, o, rank])
+        adds into y[:, sum(output_slices[:s]) : ... + output_slices[s]]. The
+        slices must share rank and width; up to three slices go in one launch,
+        more are issued in groups of three."""
+        n = len(lora_a_stacked)
+        if n != len(lora_b_stacked) or n != len(output_slices) or n == 0:
+            raise RuntimeError("add_lora_packed_nslice: slice lists differ in length")
+        rank = int(lora_b_stacked[0].size(-1))
+        if not self.rank_supported(rank):
+            return False
+        widths = {int(w) for w in output_slices}
+        if len(widths) != 1 or any(int(b.size(-1)) != rank for b in lora_b_stacked):
+            raise RuntimeError("add_lora_packed_nslice: slices must share rank and width")
+        dt = _dtype_code(x, "add_lora_packed_nslice: x/y")
+        x2d = x.reshape(-1, x.size(-1))
+        y2d = y.view(-1, y.size(-1))
+        if x2d.stride(-1) != 1 or y2d.stride(-1) != 1:
+            raise RuntimeError("add_lora_packed_nslice: x/y must be contiguous")
+        for t in (*lora_a_stacked, *lora_b_stacked):
+            if t.dtype != x.dtype or not t.is_contiguous():
+                raise RuntimeError("add_lora_packed_nslice: stacks must be contiguous and of x's dtype")
+        T, d_model = int(x2d.size(0)), int(x2d.size(1))
+        o = widths.pop()
+        if sum(int(w) for w in output_slices) > int(y2d.size(1)):
+            raise RuntimeError("add_lora_packed_nslice: output_slices exceed y's width")
+        offs = [sum(int(w) for w in output_slices[:s]) for s in range(n)]
+        for g in range(0, n, 3):
+            k = min(3, n - g)
+            A, B = lora_a_stacked[g:g + k], lora_b_stacked[g:g + k]
+            if any(int(a.size(-1)) != d_model or int(a.size(-2)) != rank for a in A):
+                raise RuntimeError("add_lora_packed_nslice: lora_a must be [L, 1, rank, d_model]")
+            if any(int(b.size(-2)) != o for b in B):
+                raise RuntimeError("add_lora_packed_nslice: lora_b width must equal output_slices")
+            self._check(self._lib.wp_add_lora_slices(
+                self._h, y2d.data_ptr(), x2d.data_ptr(), k,
+                (ctypes.c_void_p * k)(*[a.data_ptr() for a in A]),
+                (ctypes.c_int64 * k)(*[int(a.stride(0)) for a in A]),
+                (ctypes.c_void_p * k)(*[b.data_ptr() for b in B]),
+                (ctypes.c_int64 * k)(*[int(b.stride(0)) for b in B]),
+                (ctypes.c_int32 * k)(*offs[g:g + k]), int(A[0].size(0)), float(scale), T, d_model, o, rank,
+                int(x2d.stride(0)), int(y2d.stride(0)), dt, _stream_ptr(x.device)))
+        return True
+
     def add_lora_strided(self, y_view, x, wa_t_all, wb_t_all, scale) -> bool:
         """add_lora onto a column view of a wider row-major y (e.g. a
         tensor-parallel output shard): the view's row stride is used as is."""

@@ -365,6 +365,41 @@ def run_ours(args, rank, world, local_rank):
     return eng, result
 
 
+def fused_slices(eng, device, steps):
+    """The same step with the projections that share an input fused the way
+    vLLM packs them (q/k/v and gate/up through add_lora_packed_nslice): 4
+    launches per layer instead of 7, identical bytes and results."""
+    stack = Stack(device, RESIDENT)
+    scale = 16.0 / RANK
+    yqkv = torch.zeros(TOKENS, 3 * HIDDEN, device=device, dtype=torch.bfloat16)
+    ygu = torch.zeros(TOKENS, 2 * INTER, device=device, dtype=torch.bfloat16)
+
+    def step():
+        for L in stack.layers:
+            xs = L["x"]
+            eng.add_lora_packed_nslice(yqkv, xs["h"], [L[n][0] for n in "qkv"], [L[n][1] for n in "qkv"], scale,
+                                       [HIDDEN] * 3)
+            wa, wb, y = L["o"]
+            eng.add_lora_packed(y, xs["attn"], wa, wb, scale)
+            eng.add_lora_packed_nslice(ygu, xs["h"], [L["gate"][0], L["up"][0]], [L["gate"][1], L["up"][1]],
+                                       scale, [INTER] * 2)
+            wa, wb, y = L["down"]
+            eng.add_lora_packed(y, xs["inter"], wa, wb, scale)
+
+    eng.build_seg_bounds(torch.as_tensor(make_ids(RESIDENT), device=device))
+    g = capture(step)
+    for _ in range(3):
+        g.replay()
+    ms = time_graph(g, None, steps)
+    U = int(np.unique(make_ids(RESIDENT)).size)
+    shr_b, exp_b = step_bytes(U, TOKENS)
+    del g, stack
+    torch.cuda.empty_cache()
+    return {"apply_us_per_step": round(ms * 1e3, 2), "launches_per_step": 4 * LAYERS,
+            "step_gbs": round((shr_b + exp_b) / (ms * 1e-3) / 1e9, 1),
+            "path": "add_lora_packed_nslice for q/k/v and gate/up, add_lora_packed for o and down"}
+
+
 def sweep_resident(eng, device, counts, steps):
     """Flatness: us/step and roofline-normalised time vs resident adapters."""
     out = []
@@ -569,6 +604,7 @@ def main():
         if not args.no_sweep:
             result["flatness"] = sweep_resident(eng, torch.device("cuda", local_rank), [1, 8, 64, 128, 512],
                                                 max(3, args.steps // 4))
+        result["fused_slices"] = fused_slices(eng, torch.device("cuda", local_rank), max(3, args.steps // 2))
         dt, threads = cpu_reference_layers(args.cpu_layers)
         result["cpu_baseline"] = {"value": round(dt * LAYERS * 1e6, 1), "unit": "us/step", "cores": threads,
                                   "kind": "port",

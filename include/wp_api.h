@@ -205,6 +205,20 @@ int wp_add_lora(wp_handle* h, void* y, const void* x, const void* wa_base, int64
                 int32_t out_features, int32_t rank, int64_t x_ld, int64_t y_ld, int32_t y_offset,
                 int32_t dtype, void* stream);
 
+/* Several output slices sharing x in one launch, the shape of vLLM's
+ * PunicaWrapper.add_lora_packed_nslice (q/k/v, gate/up), which the reference
+ * leaves to its FusedPunicaWrapper (lora_warp_pipe/punica_wrapper.py:8-30).
+ * Slice s (s < nslices <= 3) adds (scale * x . A_s,i^T) . B_s,i^T into
+ * y[:, y_offsets[s] : y_offsets[s] + out_features], with A_s,i = wa_bases[s]
+ * + i*wa_strides[s] and B_s,i = wb_bases[s] + i*wb_strides[s]. All slices
+ * share rank, d_model, out_features and num_adapters. Result per slice is
+ * identical to nslices wp_add_lora calls. */
+int wp_add_lora_slices(wp_handle* h, void* y, const void* x, int32_t nslices, const void* const* wa_bases,
+                       const int64_t* wa_strides, const void* const* wb_bases, const int64_t* wb_strides,
+                       const int32_t* y_offsets, int32_t num_adapters, float scale, int32_t T, int32_t d_model,
+                       int32_t out_features, int32_t rank, int64_t x_ld, int64_t y_ld, int32_t dtype,
+                       void* stream);
+
 /* Shrink half of wp_add_lora, exported for tensor-parallel row-parallel
  * layers: H [T, r] fp32 (device) receives scale * x . A^T for rows inside
  * live segments; other rows are left untouched. */

@@ -128,6 +128,39 @@ def test_sliced_output(engine, dtype):
     assert_close(y, ref, dtype, "unaligned slice")
 
 
+@pytest.mark.parametrize("nslices,rank,o,dtype", [(3, 32, 4096, torch.bfloat16), (2, 32, 11008, torch.bfloat16),
+                                                   (3, 16, 512, torch.float16), (2, 64, 1024, torch.bfloat16),
+                                                   (2, 8, 256, torch.float16), (5, 32, 256, torch.bfloat16)])
+@pytest.mark.parametrize("pattern", ["zipf", "prefill", "single"])
+def test_packed_nslice(engine, nslices, rank, o, dtype, pattern):
+    """add_lora_packed_nslice (one launch per three slices) equals one oracle
+    add_lora per slice, each into its own column range of y."""
+    d = 4096
+    if pattern == "zipf":
+        idx = zipf_ids(64, 256, seed=1).tolist()
+    elif pattern == "prefill":
+        idx = [0] * 300 + [-1] * 20 + [1] * 140 + [2] * 5
+    else:
+        idx = [3]
+    T, L = len(idx), 64
+    g = torch.Generator().manual_seed(nslices * 100 + rank)
+    wa = [(torch.randn(L, 1, rank, d, generator=g) * 0.02).to(dtype) for _ in range(nslices)]
+    wb = [(torch.randn(L, 1, o, rank, generator=g) * 0.02).to(dtype) for _ in range(nslices)]
+    x = (torch.randn(T, d, generator=g) * 0.1).to(dtype)
+    y = (torch.randn(T, nslices * o, generator=g) * 0.1).to(dtype)
+    scale = 0.5
+    ref = y.float().clone()
+    for s in range(nslices):
+        ref = oa.add_lora_grouped(ref, x, wa[s], wb[s], scale, torch.tensor(idx), y_offset=s * o)
+    yd = y.cuda()
+    assert engine.build_seg_bounds(torch.tensor(idx, dtype=torch.int64).cuda())
+    assert engine.add_lora_packed_nslice(yd, x.cuda(), [a.cuda() for a in wa], [b.cuda() for b in wb], scale,
+                                         [o] * nslices)
+    torch.cuda.synchronize()
+    for s in range(nslices):
+        assert_close(yd[:, s * o:(s + 1) * o], ref[:, s * o:(s + 1) * o], dtype, f"slice {s}")
+
+
 @pytest.mark.parametrize("d,o", [(1376, 4096), (4096, 1728), (640, 13824 // 8), (11008, 4096), (8, 8)])
 def test_shapes_beyond_reference_caps(engine, d, o):
     rng = np.random.default_rng(d + o)
