@@ -245,19 +245,16 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
 
   // ---- segment table of this cluster (all threads) -------------------------
   int nmine = 0;
-  // Segments per cluster. Small tables (decode) are dealt in "snake" order of
-  // decreasing token count (round r gives cluster c the segment at sorted
-  // position r*G + c, or r*G + G-1-c on odd rounds), which pairs the largest
-  // segments with the smallest on the same cluster; larger tables go round
-  // robin (cluster c takes c, c + G, ...).
   // Segments per cluster, for small tables (decode) ordered by decreasing
   // token count. Fewer segments than clusters: the largest segments get a
   // helper cluster each, and the pair splits the segment's output columns
-  // (both clusters run the shrink; the second reads A mostly from L2).
-  // More segments than clusters: they are dealt in "snake" order (round r
-  // gives cluster c the segment at sorted position r*G + c, or r*G + G-1-c on
-  // odd rounds), pairing large segments with small ones. Larger tables go
-  // round robin (cluster c takes c, c + G, ...).
+  // (both clusters run the shrink; the second reads A mostly from L2); the
+  // whole segments take the lowest clusters, which the hardware dispatches
+  // first (with programmatic dependent launch they also start first). More
+  // segments than clusters: "snake" dealing (round r gives cluster c the
+  // segment at sorted position r*G + c or r*G + G-1-c, alternating, with the
+  // last, partial round running forward), pairing large segments with small
+  // ones. Larger tables go round robin (cluster c takes c, c + G, ...).
   // The segmenter's plan (one load round: header, this cluster's count,
   // half and descriptors together) replaces all of this when it was made for
   // this launch's cluster count.
@@ -332,10 +329,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       sort_by_size();
       const int helpers = min(nseg, G - nseg);
       const int V = nseg + helpers;
+      const int solo = nseg - helpers;  // whole segments first (lowest clusters start first), then helper pairs
       nmine = cid < V ? 1 : 0;
       if (nmine) {
-        const int pos = cid < 2 * helpers ? cid >> 1 : cid - helpers;
-        const int half = cid < 2 * helpers ? (cid & 1) : -1;
+        const int pos = cid < solo ? helpers + cid : (cid - solo) >> 1;
+        const int half = cid < solo ? -1 : ((cid - solo) & 1);
         const int ob = half == 1 ? osplit : 0;
         const int olen = half < 0 ? a.o : (half == 0 ? osplit : a.o - osplit);
         const int osl = (olen + static_cast<int>(CL) - 1) / static_cast<int>(CL);
@@ -349,12 +347,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       sort_by_size();
       const int rounds = (nseg + G - 1) / G;
       nmine = 0;
-      for (int r = 0; r < rounds; ++r) {
-        const int p = r * G + ((r & 1) ? G - 1 - cid : cid);
-        if (p < nseg) nmine = r + 1;  // positions grow with r, so the items are rounds 0..nmine-1
-      }
-      for (int r = tid; r < min(nmine, kDescCache); r += kThreads)
-        put_desc(r, order[r * G + ((r & 1) ? G - 1 - cid : cid)]);
+      // snake dealing whose last (partial) round runs forward: the clusters
+      // holding one segment more are the lowest, which start first
+      auto pos_of = [&](int r) { return r * G + (((rounds - 1 - r) & 1) ? G - 1 - cid : cid); };
+      for (int r = 0; r < rounds; ++r)
+        if (pos_of(r) < nseg) nmine = r + 1;  // positions grow with r, so the items are rounds 0..nmine-1
+      for (int r = tid; r < min(nmine, kDescCache); r += kThreads) put_desc(r, order[pos_of(r)]);
     } else {
       nmine = nseg > cid ? (nseg - cid + G - 1) / G : 0;
       for (int r = tid; r < min(nmine, kDescCache); r += kThreads) put_desc(r, cid + r * G);

@@ -85,16 +85,24 @@ __device__ void write_cluster_plan(const DevSeg* segs, int nseg, ClusterPlan* pl
       plan->half[c] = -1;
       int n = 0;
       if (mode == 1) {
+        // the unhelped segments (whole output range, the most work) go to
+        // the lowest clusters, which the hardware dispatches first; the helper
+        // pairs of the largest segments follow
         const int V = nseg + helpers;
+        const int solo = nseg - helpers;
         if (c < V) {
-          const int pos = c < 2 * helpers ? c >> 1 : c - helpers;
-          plan->half[c] = c < 2 * helpers ? (c & 1) : -1;
+          const int j = c - solo;
+          const int pos = c < solo ? helpers + c : j >> 1;
+          plan->half[c] = c < solo ? -1 : (j & 1);
           plan->seg[c] = segs[order[pos]];
           n = 1;
         }
       } else {
+        // snake dealing whose last (partial) round runs forward, so the
+        // clusters holding one segment more are the lowest ones
+        const int rounds = (nseg + G - 1) / G;
         for (int r = 0; r < kPlanRounds; ++r) {
-          const int p = r * G + ((r & 1) ? G - 1 - c : c);
+          const int p = r * G + (((rounds - 1 - r) & 1) ? G - 1 - c : c);
           if (p < nseg) {
             plan->seg[r * G + c] = segs[order[p]];
             n = r + 1;
