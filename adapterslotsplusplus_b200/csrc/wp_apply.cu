@@ -100,6 +100,11 @@ constexpr unsigned long long kDrainNs = 10000000ull;  // 10 ms per stage when dr
 
 constexpr int kSmemMax = 232448;  // dynamic shared memory per CTA (227 KB)
 
+template <int N>
+struct IntC {
+  static constexpr int value = N;
+};
+
 // DEC = true selects the decode variant: shrink and expand on warp-level
 // mma.sync in the compute warps (no tensor memory, no MMA warp); false selects
 // tcgen05 (shrink always, expand for ranks 16-64).
@@ -714,8 +719,6 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         // all rank tiles and token tiles, so no two warps read the same bytes;
         // the 8 partials are summed in a fixed order at the end of the segment.
         const bool have = nA > 0 && n > 0;
-        const int np = (n + 15) >> 4;  // pairs of 8-token tiles
-        const int nts = (n + 7) >> 3;  // 8-token tiles
         float acc[MT][4][4];
 #pragma unroll
         for (int mt = 0; mt < MT; ++mt)
@@ -723,38 +726,50 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           for (int j = 0; j < 4; ++j)
 #pragma unroll
             for (int e = 0; e < 4; ++e) acc[mt][j][e] = 0.f;
-        for (int i = 0; i < nA; ++i, ++kc) {
-          const int stage = kc % S;
-          if (wait_full(stage) && have) {
-            // all fragment loads first, then the MMAs (two warps per scheduler
-            // cannot hide a load-use chain per k-step)
-            const uint32_t sb = smem_u32(stage_base + stage * C::STAGE);
-            uint32_t af[2][MT][4], bx[2][2][4];
-#pragma unroll
-            for (int ks = 0; ks < 2; ++ks)
-#pragma unroll
-              for (int mt = 0; mt < MT; ++mt)
-                ldsm_x4(sb + offA[ks][mt], af[ks][mt][0], af[ks][mt][1], af[ks][mt][2], af[ks][mt][3]);
-#pragma unroll
-            for (int ks = 0; ks < 2; ++ks)
-#pragma unroll
-              for (int p = 0; p < 2; ++p)
-                if (p < np) ldsm_x4(sb + xsl + offX[ks][p], bx[ks][p][0], bx[ks][p][1], bx[ks][p][2], bx[ks][p][3]);
-#pragma unroll
-            for (int ks = 0; ks < 2; ++ks)
-#pragma unroll
-              for (int p = 0; p < 2; ++p)
-                if (p < np) {
-#pragma unroll
-                  for (int mt = 0; mt < MT; ++mt) {
-                    mma_k16<T>(acc[mt][2 * p], af[ks][mt], bx[ks][p][0], bx[ks][p][1]);
-                    if (2 * p + 1 < nts) mma_k16<T>(acc[mt][2 * p + 1], af[ks][mt], bx[ks][p][2], bx[ks][p][3]);
+        // the unit body is compiled per token-tile count (1-4)
+        auto shrink_units = [&](auto ntc) {
+          constexpr int nts = decltype(ntc)::value;  // 8-token tiles
+          constexpr int np = (nts + 1) / 2;  // pairs of 8-token tiles
+          for (int i = 0; i < nA; ++i, ++kc) {
+            const int stage = kc % S;
+            if (wait_full(stage) && have) {
+              // all fragment loads first, then the MMAs (two warps per scheduler
+              // cannot hide a load-use chain per k-step)
+              const uint32_t sb = smem_u32(stage_base + stage * C::STAGE);
+              uint32_t af[2][MT][4], bx[2][2][4];
+  #pragma unroll
+              for (int ks = 0; ks < 2; ++ks)
+  #pragma unroll
+                for (int mt = 0; mt < MT; ++mt)
+                  ldsm_x4(sb + offA[ks][mt], af[ks][mt][0], af[ks][mt][1], af[ks][mt][2], af[ks][mt][3]);
+  #pragma unroll
+              for (int ks = 0; ks < 2; ++ks)
+  #pragma unroll
+                for (int p = 0; p < 2; ++p)
+                  if (p < np) ldsm_x4(sb + xsl + offX[ks][p], bx[ks][p][0], bx[ks][p][1], bx[ks][p][2], bx[ks][p][3]);
+  #pragma unroll
+              for (int ks = 0; ks < 2; ++ks)
+  #pragma unroll
+                for (int p = 0; p < 2; ++p)
+                  if (p < np) {
+  #pragma unroll
+                    for (int mt = 0; mt < MT; ++mt) {
+                      mma_k16<T>(acc[mt][2 * p], af[ks][mt], bx[ks][p][0], bx[ks][p][1]);
+                      if (2 * p + 1 < nts) mma_k16<T>(acc[mt][2 * p + 1], af[ks][mt], bx[ks][p][2], bx[ks][p][3]);
+                    }
                   }
-                }
+            }
+            __syncwarp();
+            tr.mark(5);
+            if (lane == 0) mbar_arrive(&empty[stage]);
           }
-          __syncwarp();
-          tr.mark(5);
-          if (lane == 0) mbar_arrive(&empty[stage]);
+        };
+        switch ((n + 7) >> 3) {
+          case 0:
+          case 1: shrink_units(IntC<1>{}); break;
+          case 2: shrink_units(IntC<2>{}); break;
+          case 3: shrink_units(IntC<3>{}); break;
+          default: shrink_units(IntC<4>{}); break;
         }
         tr.seg(0, sj);
         // cross-warp sum: warps 4-7 park their partials, warps 0-3 add them and
@@ -1057,146 +1072,157 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           }
         }
       }
-      const int ntn = (n + 7) >> 3;  // token tiles of the segment
       const bool tmy = y_by_tma(n);  // the store thread writes the y box back and frees the stage
-      for (int i = 0; i < nB; ++i, ++kc) {
-        const int stage = kc % S;
-        if (wait_full(stage) && n > 0) {
-          const uint8_t* st = stage_base + stage * C::STAGE;
-          const int oc = oB0 + i * C::W;
-          const int wc = min(C::W, a.o - oc);
-          const uint32_t sb = smem_u32(st);
-          const bool ysm = a.y_tma != 0;
-          // y tiles (when y sits in the stage): yf[nt][ob] = y[t in tile nt][8 columns ob]
-          uint32_t yf[4][4];
-          float acc[2][4][4];
-          if (ysm) {
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt)
-              if (nt < ntn) ldsm_x4_t(sb + xsl + offY[nt], yf[nt][0], yf[nt][1], yf[nt][2], yf[nt][3]);
-          }
-          // the accumulators start at y (fp32): D = y + H . B^T, rounded once
-#pragma unroll
-          for (int m = 0; m < 2; ++m)
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt) {
-              float2 f0 = make_float2(0.f, 0.f), f1 = make_float2(0.f, 0.f);
-              if (ysm && nt < ntn) {
-                f0 = E::unpack2(yf[nt][2 * m]);
-                f1 = E::unpack2(yf[nt][2 * m + 1]);
-              }
-              acc[m][nt][0] = f0.x;
-              acc[m][nt][1] = f0.y;
-              acc[m][nt][2] = f1.x;
-              acc[m][nt][3] = f1.y;
+      // the unit body is compiled per token-tile count (1-4): no runtime
+      // predication of the fragment loops
+      auto expand_units = [&](auto ntc) {
+        constexpr int ntn = decltype(ntc)::value;
+        for (int i = 0; i < nB; ++i, ++kc) {
+          const int stage = kc % S;
+          if (wait_full(stage) && n > 0) {
+            const uint8_t* st = stage_base + stage * C::STAGE;
+            const int oc = oB0 + i * C::W;
+            const int wc = min(C::W, a.o - oc);
+            const uint32_t sb = smem_u32(st);
+            const bool ysm = a.y_tma != 0;
+            // y tiles (when y sits in the stage): yf[nt][ob] = y[t in tile nt][8 columns ob]
+            uint32_t yf[4][4];
+            float acc[2][4][4];
+            if (ysm) {
+  #pragma unroll
+              for (int nt = 0; nt < 4; ++nt)
+                if (nt < ntn) ldsm_x4_t(sb + xsl + offY[nt], yf[nt][0], yf[nt][1], yf[nt][2], yf[nt][3]);
             }
-          tr.mark(2);
-          if constexpr (R >= 16) {
-            constexpr int KB = KS > 2 ? 2 : KS;  // k-steps whose B fragments are loaded together
-#pragma unroll
-            for (int k0 = 0; k0 < KS; k0 += KB) {
-              uint32_t bA[KB][2][4];
-#pragma unroll
-              for (int kk = 0; kk < KB; ++kk)
-#pragma unroll
-                for (int m = 0; m < 2; ++m)
-                  ldsm_x4(sb + offB[k0 + kk][m], bA[kk][m][0], bA[kk][m][1], bA[kk][m][2], bA[kk][m][3]);
-#pragma unroll
-              for (int kk = 0; kk < KB; ++kk)
-#pragma unroll
+            // the accumulators start at y (fp32): D = y + H . B^T, rounded once
+  #pragma unroll
+            for (int m = 0; m < 2; ++m)
+  #pragma unroll
+              for (int nt = 0; nt < 4; ++nt) {
+                float2 f0 = make_float2(0.f, 0.f), f1 = make_float2(0.f, 0.f);
+                if (ysm && nt < ntn) {
+                  f0 = E::unpack2(yf[nt][2 * m]);
+                  f1 = E::unpack2(yf[nt][2 * m + 1]);
+                }
+                acc[m][nt][0] = f0.x;
+                acc[m][nt][1] = f0.y;
+                acc[m][nt][2] = f1.x;
+                acc[m][nt][3] = f1.y;
+              }
+            tr.mark(2);
+            if constexpr (R >= 16) {
+              constexpr int KB = KS > 2 ? 2 : KS;  // k-steps whose B fragments are loaded together
+  #pragma unroll
+              for (int k0 = 0; k0 < KS; k0 += KB) {
+                uint32_t bA[KB][2][4];
+  #pragma unroll
+                for (int kk = 0; kk < KB; ++kk)
+  #pragma unroll
+                  for (int m = 0; m < 2; ++m)
+                    ldsm_x4(sb + offB[k0 + kk][m], bA[kk][m][0], bA[kk][m][1], bA[kk][m][2], bA[kk][m][3]);
+  #pragma unroll
+                for (int kk = 0; kk < KB; ++kk)
+  #pragma unroll
+                  for (int nt = 0; nt < 4; ++nt)
+                    if (nt < ntn) {
+                      const int ks = k0 + kk;
+  #pragma unroll
+                      for (int m = 0; m < 2; ++m) {
+                        mma_k16<T>(acc[m][nt], bA[kk][m], hb[nt][ks][0], hb[nt][ks][1]);
+                        if constexpr (!DEC) mma_k16<T>(acc[m][nt], bA[kk][m], hl[nt][ks][0], hl[nt][ks][1]);
+                      }
+                    }
+              }
+            } else {
+              // rank 8: B rows of 16 bytes (linear); matrices 2m, 2m + 1 = rows 16m..16m+15
+              uint32_t bf[4];
+              ldsm_x4(sb + 4 * C::XBOX + (warp * 32 + lane) * 16, bf[0], bf[1], bf[2], bf[3]);
+  #pragma unroll
+              for (int nt = 0; nt < 4; ++nt)
+                if (nt < ntn) {
+  #pragma unroll
+                  for (int m = 0; m < 2; ++m) {
+                    mma_k8<T>(acc[m][nt], bf[2 * m], bf[2 * m + 1], hb[nt][0][0]);
+                    if constexpr (!DEC) mma_k8<T>(acc[m][nt], bf[2 * m], bf[2 * m + 1], hl[nt][0][0]);
+                  }
+                }
+            }
+            tr.mark(3);
+            if (ysm) {
+              // back into the y box in place; then the box goes to global memory
+              // by one tensor store (store thread) or this warp's 16-byte row
+              // chunks are stored directly.
+  #pragma unroll
+              for (int nt = 0; nt < 4; ++nt)
+                if (nt < ntn) {
+                  stsm_x4_t(sb + xsl + offY[nt], E::pack2(acc[0][nt][0], acc[0][nt][1]),
+                            E::pack2(acc[0][nt][2], acc[0][nt][3]), E::pack2(acc[1][nt][0], acc[1][nt][1]),
+                            E::pack2(acc[1][nt][2], acc[1][nt][3]));
+                }
+              tr.mark(4);
+              if (tmy) {
+                fence_proxy_async_smem();  // the tensor store reads these writes
+              } else {
+                __syncwarp();
+                const int sub = lane & 3;
+                const int colw = warp * 32 + sub * 8;  // column of this lane's 16-byte chunk in the stage
+                const int chunk = (warp & 1) * 4 + sub;
+                const uint8_t* ybox = st + xsl;
+                T* ycol = yg + static_cast<int64_t>(s.token_start) * a.y_ld + yoff_of(s) + oc + colw;
+                if (colw + 8 <= wc) {
+                  int4 out[4];
+  #pragma unroll
+                  for (int it = 0; it < 4; ++it) {
+                    const int row = (lane >> 2) + 8 * it;
+                    if (row < n) out[it] = *reinterpret_cast<const int4*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
+                  }
+  #pragma unroll
+                  for (int it = 0; it < 4; ++it) {
+                    const int row = (lane >> 2) + 8 * it;
+                    if (row < n) *reinterpret_cast<int4*>(ycol + static_cast<int64_t>(row) * a.y_ld) = out[it];
+                  }
+                } else if (colw < wc) {
+                  for (int it = 0; it < 4; ++it) {
+                    const int row = (lane >> 2) + 8 * it;
+                    if (row < n) {
+                      const T* src = reinterpret_cast<const T*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
+                      for (int x = 0; x < wc - colw; ++x) ycol[static_cast<int64_t>(row) * a.y_ld + x] = src[x];
+                    }
+                  }
+                }
+              }
+            } else {
+              // y not 16-byte addressable: read and write it directly
+  #pragma unroll
+              for (int m = 0; m < 2; ++m)
+  #pragma unroll
                 for (int nt = 0; nt < 4; ++nt)
-                  if (nt < ntn) {
-                    const int ks = k0 + kk;
-#pragma unroll
-                    for (int m = 0; m < 2; ++m) {
-                      mma_k16<T>(acc[m][nt], bA[kk][m], hb[nt][ks][0], hb[nt][ks][1]);
-                      if constexpr (!DEC) mma_k16<T>(acc[m][nt], bA[kk][m], hl[nt][ks][0], hl[nt][ks][1]);
+  #pragma unroll
+                  for (int e = 0; e < 4; ++e) {
+                    const int t = nt * 8 + 2 * c + (e & 1);
+                    const int col = warp * 32 + m * 16 + g + (e >> 1) * 8;
+                    if (t < n && col < wc) {
+                      T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + yoff_of(s) + oc + col;
+                      *yp = E::from_f(E::to_f(*yp) + acc[m][nt][e]);
                     }
                   }
             }
-          } else {
-            // rank 8: B rows of 16 bytes (linear); matrices 2m, 2m + 1 = rows 16m..16m+15
-            uint32_t bf[4];
-            ldsm_x4(sb + 4 * C::XBOX + (warp * 32 + lane) * 16, bf[0], bf[1], bf[2], bf[3]);
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt)
-              if (nt < ntn) {
-#pragma unroll
-                for (int m = 0; m < 2; ++m) {
-                  mma_k8<T>(acc[m][nt], bf[2 * m], bf[2 * m + 1], hb[nt][0][0]);
-                  if constexpr (!DEC) mma_k8<T>(acc[m][nt], bf[2 * m], bf[2 * m + 1], hl[nt][0][0]);
-                }
-              }
           }
-          tr.mark(3);
-          if (ysm) {
-            // back into the y box in place; then the box goes to global memory
-            // by one tensor store (store thread) or this warp's 16-byte row
-            // chunks are stored directly.
-#pragma unroll
-            for (int nt = 0; nt < 4; ++nt)
-              if (nt < ntn) {
-                stsm_x4_t(sb + xsl + offY[nt], E::pack2(acc[0][nt][0], acc[0][nt][1]),
-                          E::pack2(acc[0][nt][2], acc[0][nt][3]), E::pack2(acc[1][nt][0], acc[1][nt][1]),
-                          E::pack2(acc[1][nt][2], acc[1][nt][3]));
-              }
-            tr.mark(4);
-            if (tmy) {
-              fence_proxy_async_smem();  // the tensor store reads these writes
-            } else {
-              __syncwarp();
-              const int sub = lane & 3;
-              const int colw = warp * 32 + sub * 8;  // column of this lane's 16-byte chunk in the stage
-              const int chunk = (warp & 1) * 4 + sub;
-              const uint8_t* ybox = st + xsl;
-              T* ycol = yg + static_cast<int64_t>(s.token_start) * a.y_ld + yoff_of(s) + oc + colw;
-              if (colw + 8 <= wc) {
-                int4 out[4];
-#pragma unroll
-                for (int it = 0; it < 4; ++it) {
-                  const int row = (lane >> 2) + 8 * it;
-                  if (row < n) out[it] = *reinterpret_cast<const int4*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
-                }
-#pragma unroll
-                for (int it = 0; it < 4; ++it) {
-                  const int row = (lane >> 2) + 8 * it;
-                  if (row < n) *reinterpret_cast<int4*>(ycol + static_cast<int64_t>(row) * a.y_ld) = out[it];
-                }
-              } else if (colw < wc) {
-                for (int it = 0; it < 4; ++it) {
-                  const int row = (lane >> 2) + 8 * it;
-                  if (row < n) {
-                    const T* src = reinterpret_cast<const T*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
-                    for (int x = 0; x < wc - colw; ++x) ycol[static_cast<int64_t>(row) * a.y_ld + x] = src[x];
-                  }
-                }
-              }
-            }
+          if constexpr (DEC) {
+            __syncwarp();
+            tr.mark(5);
+            if (lane == 0) mbar_arrive(tmy ? &ydone[stage] : &empty[stage]);
           } else {
-            // y not 16-byte addressable: read and write it directly
-#pragma unroll
-            for (int m = 0; m < 2; ++m)
-#pragma unroll
-              for (int nt = 0; nt < 4; ++nt)
-#pragma unroll
-                for (int e = 0; e < 4; ++e) {
-                  const int t = nt * 8 + 2 * c + (e & 1);
-                  const int col = warp * 32 + m * 16 + g + (e >> 1) * 8;
-                  if (t < n && col < wc) {
-                    T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + yoff_of(s) + oc + col;
-                    *yp = E::from_f(E::to_f(*yp) + acc[m][nt][e]);
-                  }
-                }
+            named_sync(kBarCompute, kComputeThreads);
+            if (tid == 0) mbar_arrive(&empty[stage]);
           }
         }
-        if constexpr (DEC) {
-          __syncwarp();
-          tr.mark(5);
-          if (lane == 0) mbar_arrive(tmy ? &ydone[stage] : &empty[stage]);
-        } else {
-          named_sync(kBarCompute, kComputeThreads);
-          if (tid == 0) mbar_arrive(&empty[stage]);
-        }
+      };
+      switch ((n + 7) >> 3) {
+        case 0:
+        case 1: expand_units(IntC<1>{}); break;
+        case 2: expand_units(IntC<2>{}); break;
+        case 3: expand_units(IntC<3>{}); break;
+        default: expand_units(IntC<4>{}); break;
       }
     }
   }
