@@ -1075,8 +1075,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       const bool tmy = y_by_tma(n);  // the store thread writes the y box back and frees the stage
       // the unit body is compiled per token-tile count (1-4): no runtime
       // predication of the fragment loops
+      // ntc = 1..4: y in the stage (tensor-map aligned), compiled per
+      // token-tile count; ntc = 0: y not 16-byte addressable (rare), one
+      // generic body that reads and writes y element by element
       auto expand_units = [&](auto ntc) {
-        constexpr int ntn = decltype(ntc)::value;
+        constexpr bool kGeneric = decltype(ntc)::value == 0;
+        const int ntn = kGeneric ? (n + 7) >> 3 : decltype(ntc)::value;
         for (int i = 0; i < nB; ++i, ++kc) {
           const int stage = kc % S;
           if (wait_full(stage) && n > 0) {
@@ -1084,7 +1088,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
             const int oc = oB0 + i * C::W;
             const int wc = min(C::W, a.o - oc);
             const uint32_t sb = smem_u32(st);
-            const bool ysm = a.y_tma != 0;
+            constexpr bool ysm = !kGeneric;
             // y tiles (when y sits in the stage): yf[nt][ob] = y[t in tile nt][8 columns ob]
             uint32_t yf[4][4];
             float acc[2][4][4];
@@ -1168,25 +1172,20 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
                 const int chunk = (warp & 1) * 4 + sub;
                 const uint8_t* ybox = st + xsl;
                 T* ycol = yg + static_cast<int64_t>(s.token_start) * a.y_ld + yoff_of(s) + oc + colw;
-                if (colw + 8 <= wc) {
+                // o and the stage columns are multiples of 8: a chunk lies
+                // wholly inside the output range or wholly outside it
+                if (colw < wc) {
                   int4 out[4];
   #pragma unroll
                   for (int it = 0; it < 4; ++it) {
                     const int row = (lane >> 2) + 8 * it;
-                    if (row < n) out[it] = *reinterpret_cast<const int4*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
+                    if (it < ntn && row < n)
+                      out[it] = *reinterpret_cast<const int4*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
                   }
   #pragma unroll
                   for (int it = 0; it < 4; ++it) {
                     const int row = (lane >> 2) + 8 * it;
-                    if (row < n) *reinterpret_cast<int4*>(ycol + static_cast<int64_t>(row) * a.y_ld) = out[it];
-                  }
-                } else if (colw < wc) {
-                  for (int it = 0; it < 4; ++it) {
-                    const int row = (lane >> 2) + 8 * it;
-                    if (row < n) {
-                      const T* src = reinterpret_cast<const T*>(ybox + row * 128 + (((chunk ^ row) & 7) << 4));
-                      for (int x = 0; x < wc - colw; ++x) ycol[static_cast<int64_t>(row) * a.y_ld + x] = src[x];
-                    }
+                    if (it < ntn && row < n) *reinterpret_cast<int4*>(ycol + static_cast<int64_t>(row) * a.y_ld) = out[it];
                   }
                 }
               }
@@ -1217,12 +1216,16 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           }
         }
       };
-      switch ((n + 7) >> 3) {
-        case 0:
-        case 1: expand_units(IntC<1>{}); break;
-        case 2: expand_units(IntC<2>{}); break;
-        case 3: expand_units(IntC<3>{}); break;
-        default: expand_units(IntC<4>{}); break;
+      if (!a.y_tma) {
+        expand_units(IntC<0>{});
+      } else {
+        switch ((n + 7) >> 3) {
+          case 0:
+          case 1: expand_units(IntC<1>{}); break;
+          case 2: expand_units(IntC<2>{}); break;
+          case 3: expand_units(IntC<3>{}); break;
+          default: expand_units(IntC<4>{}); break;
+        }
       }
     }
   }
