@@ -1075,12 +1075,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       const bool tmy = y_by_tma(n);  // the store thread writes the y box back and frees the stage
       // the unit body is compiled per token-tile count (1-4): no runtime
       // predication of the fragment loops
-      // ntc = 1..4: y in the stage (tensor-map aligned), compiled per
-      // token-tile count; ntc = 0: y not 16-byte addressable (rare), one
-      // generic body that reads and writes y element by element
       auto expand_units = [&](auto ntc) {
-        constexpr bool kGeneric = decltype(ntc)::value == 0;
-        const int ntn = kGeneric ? (n + 7) >> 3 : decltype(ntc)::value;
+        constexpr int ntn = decltype(ntc)::value;
         for (int i = 0; i < nB; ++i, ++kc) {
           const int stage = kc % S;
           if (wait_full(stage) && n > 0) {
@@ -1088,22 +1084,36 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
             const int oc = oB0 + i * C::W;
             const int wc = min(C::W, a.o - oc);
             const uint32_t sb = smem_u32(st);
-            constexpr bool ysm = !kGeneric;
-            // y tiles (when y sits in the stage): yf[nt][ob] = y[t in tile nt][8 columns ob]
+            // This warp's 32 columns of the y box: rows of 128 bytes, 16-byte
+            // chunk ch of row t at ((ch ^ t) & 7) * 16 (the tensor map's 128-byte
+            // swizzle). A y that the tensor maps cannot address (not 16-byte
+            // aligned) is copied in here by the warp itself, element by element.
+            uint8_t* ybox = const_cast<uint8_t*>(st) + xsl;
+            const int colw0 = warp * 32;  // first column of this warp in the stage
+            if (!a.y_tma) {
+              const T* ysrc = yg + static_cast<int64_t>(s.token_start) * a.y_ld + yoff_of(s) + oc + colw0;
+  #pragma unroll 1
+              for (int e = lane; e < n * 32; e += 32) {
+                const int t = e >> 5, col = e & 31;
+                const int ch = (warp & 1) * 4 + (col >> 3);
+                *reinterpret_cast<T*>(ybox + t * 128 + (((ch ^ t) & 7) << 4) + (col & 7) * 2) =
+                    colw0 + col < wc ? ysrc[static_cast<int64_t>(t) * a.y_ld + col] : E::from_f(0.f);
+              }
+              __syncwarp();
+            }
+            // y tiles: yf[nt][ob] = y[t in tile nt][8 columns ob]
             uint32_t yf[4][4];
             float acc[2][4][4];
-            if (ysm) {
   #pragma unroll
-              for (int nt = 0; nt < 4; ++nt)
-                if (nt < ntn) ldsm_x4_t(sb + xsl + offY[nt], yf[nt][0], yf[nt][1], yf[nt][2], yf[nt][3]);
-            }
+            for (int nt = 0; nt < 4; ++nt)
+              if (nt < ntn) ldsm_x4_t(sb + xsl + offY[nt], yf[nt][0], yf[nt][1], yf[nt][2], yf[nt][3]);
             // the accumulators start at y (fp32): D = y + H . B^T, rounded once
   #pragma unroll
             for (int m = 0; m < 2; ++m)
   #pragma unroll
               for (int nt = 0; nt < 4; ++nt) {
                 float2 f0 = make_float2(0.f, 0.f), f1 = make_float2(0.f, 0.f);
-                if (ysm && nt < ntn) {
+                if (nt < ntn) {
                   f0 = E::unpack2(yf[nt][2 * m]);
                   f1 = E::unpack2(yf[nt][2 * m + 1]);
                 }
@@ -1151,10 +1161,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
                 }
             }
             tr.mark(3);
-            if (ysm) {
+            {
               // back into the y box in place; then the box goes to global memory
               // by one tensor store (store thread) or this warp's 16-byte row
-              // chunks are stored directly.
+              // chunks are stored directly (element by element for a y that is
+              // not 16-byte addressable).
   #pragma unroll
               for (int nt = 0; nt < 4; ++nt)
                 if (nt < ntn) {
@@ -1165,12 +1176,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
               tr.mark(4);
               if (tmy) {
                 fence_proxy_async_smem();  // the tensor store reads these writes
-              } else {
+              } else if (a.y_tma) {
                 __syncwarp();
                 const int sub = lane & 3;
-                const int colw = warp * 32 + sub * 8;  // column of this lane's 16-byte chunk in the stage
+                const int colw = colw0 + sub * 8;  // column of this lane's 16-byte chunk in the stage
                 const int chunk = (warp & 1) * 4 + sub;
-                const uint8_t* ybox = st + xsl;
                 T* ycol = yg + static_cast<int64_t>(s.token_start) * a.y_ld + yoff_of(s) + oc + colw;
                 // o and the stage columns are multiples of 8: a chunk lies
                 // wholly inside the output range or wholly outside it
@@ -1188,22 +1198,18 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
                     if (it < ntn && row < n) *reinterpret_cast<int4*>(ycol + static_cast<int64_t>(row) * a.y_ld) = out[it];
                   }
                 }
+              } else {
+                __syncwarp();
+                T* ydst = yg + static_cast<int64_t>(s.token_start) * a.y_ld + yoff_of(s) + oc + colw0;
+  #pragma unroll 1
+                for (int e = lane; e < n * 32; e += 32) {
+                  const int t = e >> 5, col = e & 31;
+                  const int ch = (warp & 1) * 4 + (col >> 3);
+                  if (colw0 + col < wc)
+                    ydst[static_cast<int64_t>(t) * a.y_ld + col] =
+                        *reinterpret_cast<const T*>(ybox + t * 128 + (((ch ^ t) & 7) << 4) + (col & 7) * 2);
+                }
               }
-            } else {
-              // y not 16-byte addressable: read and write it directly
-  #pragma unroll
-              for (int m = 0; m < 2; ++m)
-  #pragma unroll
-                for (int nt = 0; nt < 4; ++nt)
-  #pragma unroll
-                  for (int e = 0; e < 4; ++e) {
-                    const int t = nt * 8 + 2 * c + (e & 1);
-                    const int col = warp * 32 + m * 16 + g + (e >> 1) * 8;
-                    if (t < n && col < wc) {
-                      T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + yoff_of(s) + oc + col;
-                      *yp = E::from_f(E::to_f(*yp) + acc[m][nt][e]);
-                    }
-                  }
             }
           }
           if constexpr (DEC) {
@@ -1216,16 +1222,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           }
         }
       };
-      if (!a.y_tma) {
-        expand_units(IntC<0>{});
-      } else {
-        switch ((n + 7) >> 3) {
-          case 0:
-          case 1: expand_units(IntC<1>{}); break;
-          case 2: expand_units(IntC<2>{}); break;
-          case 3: expand_units(IntC<3>{}); break;
-          default: expand_units(IntC<4>{}); break;
-        }
+      switch ((n + 7) >> 3) {
+        case 0:
+        case 1: expand_units(IntC<1>{}); break;
+        case 2: expand_units(IntC<2>{}); break;
+        case 3: expand_units(IntC<3>{}); break;
+        default: expand_units(IntC<4>{}); break;
       }
     }
   }
