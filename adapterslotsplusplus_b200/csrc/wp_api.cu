@@ -822,16 +822,20 @@ int kernel_choice(const wp_handle* h) {
   }
 }
 
-// Automatic choice for a fused live-mode call: the clustered kernel gives
-// every segment one cluster (a second one when clusters are left over), so
-// its time follows the busiest cluster; the balanced kernel spreads every
-// segment over the whole GPU at the price of a flag exchange through L2.
-// Measured on B200: balance wins when the segments leave at least half of
-// the clusters idle, or exceed the clusters by 30% (several segments per
-// cluster); in between, one segment per cluster wins. The segment count is
-// the latest segmenter's (read without a sync); before one has landed, the
-// bound min(T, A + ceil(T / 32)) for A adapters among T tokens stands in.
-bool auto_split(wp_handle* h, cudaStream_t stream, int T, int64_t num_adapters, int clusters) {
+// Automatic choice for a fused live-mode call, from a cost model of the two
+// decode kernels fitted to B200 measurements (rank 32, bf16, 256 tokens,
+// 1-512 resident adapters; us per launch inside a CUDA graph):
+//   clustered: ~4.4 + 0.5 x (pipeline stages of the busiest CTA), where a
+//     segment's CTA pair streams half of d each and a helper pair halves the
+//     output columns when clusters are left over;
+//   balanced ("split"): ~10 + 0.9 x (stages per CTA with every segment's
+//     stages spread over the whole grid) -- its flag exchange through L2
+//     costs a fixed ~5 us more.
+// The segment count is the latest segmenter's (read without a sync); before
+// one has landed, the bound min(T, A + ceil(T / 32)) for A adapters among T
+// tokens stands in.
+bool auto_split(wp_handle* h, cudaStream_t stream, int T, int64_t num_adapters, int clusters, int cluster, int d,
+                int o) {
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (h->nseg_pending && cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone &&
       cudaEventQuery(h->nseg_ready) == cudaSuccess) {
@@ -841,7 +845,24 @@ bool auto_split(wp_handle* h, cudaStream_t stream, int T, int64_t num_adapters, 
   cudaGetLastError();  // a not-ready query is not an error
   int64_t nseg = h->nseg_hint;
   if (nseg < 0) nseg = std::min<int64_t>(T, std::max<int64_t>(num_adapters, 1) + (T + wp::kSegTokens - 1) / wp::kSegTokens);
-  return nseg * 2 <= clusters || nseg * 10 >= static_cast<int64_t>(clusters) * 13;
+  if (nseg <= 0 || clusters <= 0) return false;
+  const int64_t cl = std::max(cluster, 1);
+  auto stages = [](int64_t cols) { return (cols + wp::kStageK - 1) / wp::kStageK; };
+  const int64_t nA = stages((d + cl - 1) / cl);
+  const int64_t nB = stages((o + cl - 1) / cl);
+  const int64_t half = (((o + 1) / 2) + wp::kStageCols - 1) / wp::kStageCols * wp::kStageCols;
+  const int64_t nB_half = stages((half + cl - 1) / cl);
+  int64_t busiest;
+  if (nseg <= clusters) {
+    const int64_t helpers = std::min<int64_t>(nseg, clusters - nseg);
+    busiest = nA + (helpers == nseg ? nB_half : nB);
+  } else {
+    busiest = (nseg + clusters - 1) / clusters * (nA + nB);
+  }
+  const double cost_cluster = 4.4 + 0.5 * static_cast<double>(busiest);
+  const double per_cta = static_cast<double>(nseg * (stages(d) + stages(o))) / static_cast<double>(h->num_sms);
+  const double cost_split = 10.0 + 0.9 * per_cta;
+  return cost_split < cost_cluster;
 }
 bool use_decode_kernel(const wp_handle* h) { return kernel_choice(h) != 2; }
 
@@ -940,7 +961,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   if (kernel_choice(h) < 0 && mode == wp::kModeFused && !registry) {
     int c0 = 1, g0 = 1;
     apply_plan(h, dtype, r, true, &c0, &g0);
-    want_split = auto_split(h, stream, T, num_adapters, g0 / std::max(c0, 1));
+    want_split = auto_split(h, stream, T, num_adapters, g0 / std::max(c0, 1), c0, d, o);
   }
   if (mode == wp::kModeFused && !registry && want_split && T <= h->sync_cap && split_fits) {
     const int key = (dtype == WP_DTYPE_BF16 ? 4 : 0) + (r == 8 ? 0 : r == 16 ? 1 : r == 32 ? 2 : 3);
