@@ -81,6 +81,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <type_traits>
 
 #include "wp_device.cuh"
 #include "wp_internal.h"
@@ -146,7 +147,7 @@ struct ApplyCfg {
   static_assert(!DEC || PW >= 4 * kSnakeMax * 4, "the partial slots hold the table-ordering scratch");
 };
 
-template <typename T, int R, bool DEC>
+template <typename T, int R, bool DEC, bool TR>
 __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constant__ ApplyArgs a) {
   using C = ApplyCfg<R, DEC>;
   using E = Elem<T>;
@@ -186,7 +187,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const uint32_t CL = cluster_nctarank();
   const int cid = static_cast<int>(cluster_id_x());
   const int G = static_cast<int>(cluster_count_x());
-  Trace tr;
+  std::conditional_t<TR, Trace, TraceOff> tr;
   tr.init(a.trace, tid == 0);
 
   if (tid == 0) {
@@ -389,7 +390,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     tr.dep();
     read_table();
   }
-  if (tid == 0) trace_mark(a.trace, 7);
+  if (tid == 0) trace_mark_t<TR>(a.trace, 7);
   const int total = nmine * ups;
   const uint32_t tbase = use_tmem ? *s_tmem : 0u;
   const uint32_t t_sh = tbase;
@@ -465,17 +466,17 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         }
       };
       const int first = min(S, total);
-      trace_mark(a.trace, 9);
+      trace_mark_t<TR>(a.trace, 9);
       if (a.prefetch_weights) {
         for (int u = 0; u < first; ++u) {
           issue(u, u, 1);
-          trace_unit(a.trace, u, 7);
-          if (u == 0) trace_mark(a.trace, 10);
+          trace_unit_t<TR>(a.trace, u, 7);
+          if (u == 0) trace_mark_t<TR>(a.trace, 10);
         }
-        trace_mark(a.trace, 8);
+        trace_mark_t<TR>(a.trace, 8);
         pdl_wait_prior();
         pdl_launch_dependents();
-        trace_mark(a.trace, 6);
+        trace_mark_t<TR>(a.trace, 6);
         for (int u = 0; u < first; ++u) issue(u, u, 2);
       } else {
         for (int u = 0; u < first; ++u) issue(u, u, 3);
@@ -486,7 +487,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         if (!mbar_wait_bounded(&empty[stage], ((u / S) - 1) & 1, a.err)) *s_bad = 1;
         if (*s_bad) break;
         issue(u, stage, 3);
-        trace_unit(a.trace, u, 7);
+        trace_unit_t<TR>(a.trace, u, 7);
         *s_issued = u + 1;
       }
     } else if (a.prefetch_weights) {
@@ -561,7 +562,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         for (int i = 0; i < nA; ++i, ++u) {
           const int stage = u % S;
           const bool ok = wait_ok(&full[stage], (u / S) & 1);
-          if (sj == 0 && i == 0) trace_mark(a.trace, 4);
+          if (sj == 0 && i == 0) trace_mark_t<TR>(a.trace, 4);
           if (ok && have) {
             tc_fence_after();
             const uint32_t st = smem_u32(stage_base + stage * C::STAGE);
@@ -580,7 +581,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
             mbar_arrive(&empty[stage]);
           }
         }
-        if (sj == 0) trace_mark(a.trace, 5);
+        if (sj == 0) trace_mark_t<TR>(a.trace, 5);
         if (have) {
           if (!*s_bad) umma_commit(sh_full);
           ++sh_uses;
@@ -620,7 +621,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
               for (int ks = 0; ks < R / 16; ++ks) umma_f16(acc, db + 2 * ks, dl + 2 * ks, idesc, 1u);
             }
             umma_commit(&acc_full[b]);
-            if (sj == 0) trace_unit(a.trace, i, 6);
+            if (sj == 0) trace_unit_t<TR>(a.trace, i, 6);
           }
         } else {
           u += nB;
@@ -1265,7 +1266,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
 
 namespace {
 
-template <typename T, int R, bool DEC>
+template <typename T, int R, bool DEC, bool TR>
 struct ApplyKernel {
   using C = ApplyCfg<R, DEC>;
   static bool prepare() {
@@ -1274,7 +1275,7 @@ struct ApplyKernel {
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (done.load() & bit) return true;
-    if (cudaFuncSetAttribute(apply_kernel<T, R, DEC>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+    if (cudaFuncSetAttribute(apply_kernel<T, R, DEC, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
         cudaSuccess)
       return false;
     done.fetch_or(bit);
@@ -1298,7 +1299,7 @@ struct ApplyKernel {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = lc.pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, apply_kernel<T, R, DEC>, a);
+    return cudaLaunchKernelEx(&cfg, apply_kernel<T, R, DEC, TR>, a);
   }
 
   static int max_grid(int cluster) {
@@ -1316,7 +1317,7 @@ struct ApplyKernel {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int nclusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&nclusters, apply_kernel<T, R, DEC>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&nclusters, apply_kernel<T, R, DEC, TR>, &cfg) != cudaSuccess) {
       cudaGetLastError();
       return 0;
     }
@@ -1324,13 +1325,19 @@ struct ApplyKernel {
   }
 };
 
+template <typename T, int R>
+cudaError_t apply_variant(const ApplyArgs& a, const LaunchCfg& lc) {
+  if (a.trace) return lc.dec ? ApplyKernel<T, R, true, true>::launch(a, lc) : ApplyKernel<T, R, false, true>::launch(a, lc);
+  return lc.dec ? ApplyKernel<T, R, true, false>::launch(a, lc) : ApplyKernel<T, R, false, false>::launch(a, lc);
+}
+
 template <typename T>
 cudaError_t apply_by_rank(int rank, const ApplyArgs& a, const LaunchCfg& lc) {
   switch (rank) {
-    case 8: return lc.dec ? ApplyKernel<T, 8, true>::launch(a, lc) : ApplyKernel<T, 8, false>::launch(a, lc);
-    case 16: return lc.dec ? ApplyKernel<T, 16, true>::launch(a, lc) : ApplyKernel<T, 16, false>::launch(a, lc);
-    case 32: return lc.dec ? ApplyKernel<T, 32, true>::launch(a, lc) : ApplyKernel<T, 32, false>::launch(a, lc);
-    case 64: return lc.dec ? ApplyKernel<T, 64, true>::launch(a, lc) : ApplyKernel<T, 64, false>::launch(a, lc);
+    case 8: return apply_variant<T, 8>(a, lc);
+    case 16: return apply_variant<T, 16>(a, lc);
+    case 32: return apply_variant<T, 32>(a, lc);
+    case 64: return apply_variant<T, 64>(a, lc);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -1338,10 +1345,10 @@ cudaError_t apply_by_rank(int rank, const ApplyArgs& a, const LaunchCfg& lc) {
 template <typename T>
 int max_grid_by_rank(int rank, int cluster, bool dec) {
   switch (rank) {
-    case 8: return dec ? ApplyKernel<T, 8, true>::max_grid(cluster) : ApplyKernel<T, 8, false>::max_grid(cluster);
-    case 16: return dec ? ApplyKernel<T, 16, true>::max_grid(cluster) : ApplyKernel<T, 16, false>::max_grid(cluster);
-    case 32: return dec ? ApplyKernel<T, 32, true>::max_grid(cluster) : ApplyKernel<T, 32, false>::max_grid(cluster);
-    case 64: return dec ? ApplyKernel<T, 64, true>::max_grid(cluster) : ApplyKernel<T, 64, false>::max_grid(cluster);
+    case 8: return dec ? ApplyKernel<T, 8, true, false>::max_grid(cluster) : ApplyKernel<T, 8, false, false>::max_grid(cluster);
+    case 16: return dec ? ApplyKernel<T, 16, true, false>::max_grid(cluster) : ApplyKernel<T, 16, false, false>::max_grid(cluster);
+    case 32: return dec ? ApplyKernel<T, 32, true, false>::max_grid(cluster) : ApplyKernel<T, 32, false, false>::max_grid(cluster);
+    case 64: return dec ? ApplyKernel<T, 64, true, false>::max_grid(cluster) : ApplyKernel<T, 64, false, false>::max_grid(cluster);
     default: return 0;
   }
 }

@@ -39,6 +39,7 @@
 #include <stdint.h>
 
 #include <atomic>
+#include <type_traits>
 
 #include "wp_device.cuh"
 #include "wp_internal.h"
@@ -126,7 +127,7 @@ __device__ __forceinline__ bool wait_flag(const int* p, int* err) {
   }
 }
 
-template <typename T, int R>
+template <typename T, int R, bool TR>
 __global__ void __launch_bounds__(kSThreads, 1) split_kernel(const __grid_constant__ ApplyArgs a) {
   using C = SplitCfg<R>;
   using E = Elem<T>;
@@ -153,7 +154,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_kernel(const __grid_consta
   const int lane = tid & 31;
   const int G = static_cast<int>(gridDim.x);
   const int k = static_cast<int>(blockIdx.x);
-  Trace tr;
+  std::conditional_t<TR, Trace, TraceOff> tr;
   tr.init(a.trace, tid == 0);
 
   if (tid == 0) {
@@ -784,7 +785,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_kernel(const __grid_consta
   tr.finish();
 }
 
-template <typename T, int R>
+template <typename T, int R, bool TR>
 struct SplitKernel {
   static bool prepare() {
     static std::atomic<uint64_t> done{0};
@@ -792,7 +793,7 @@ struct SplitKernel {
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (done.load() & bit) return true;
-    if (cudaFuncSetAttribute(split_kernel<T, R>, cudaFuncAttributeMaxDynamicSharedMemorySize, SplitCfg<R>::SMEM) !=
+    if (cudaFuncSetAttribute(split_kernel<T, R, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, SplitCfg<R>::SMEM) !=
         cudaSuccess)
       return false;
     done.fetch_or(bit);
@@ -810,12 +811,12 @@ struct SplitKernel {
     attr[0].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = lc.pdl ? 1 : 0;
-    return cudaLaunchKernelEx(&cfg, split_kernel<T, R>, a);
+    return cudaLaunchKernelEx(&cfg, split_kernel<T, R, TR>, a);
   }
   static int max_grid() {
     if (!prepare()) return 0;
     int per_sm = 0, dev = 0, sms = 0;
-    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, split_kernel<T, R>, kSThreads, SplitCfg<R>::SMEM) !=
+    if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&per_sm, split_kernel<T, R, TR>, kSThreads, SplitCfg<R>::SMEM) !=
         cudaSuccess) {
       cudaGetLastError();
       return 0;
@@ -829,10 +830,10 @@ struct SplitKernel {
 template <typename T>
 cudaError_t split_by_rank(int rank, const ApplyArgs& a, const LaunchCfg& lc) {
   switch (rank) {
-    case 8: return SplitKernel<T, 8>::launch(a, lc);
-    case 16: return SplitKernel<T, 16>::launch(a, lc);
-    case 32: return SplitKernel<T, 32>::launch(a, lc);
-    case 64: return SplitKernel<T, 64>::launch(a, lc);
+    case 8: return a.trace ? SplitKernel<T, 8, true>::launch(a, lc) : SplitKernel<T, 8, false>::launch(a, lc);
+    case 16: return a.trace ? SplitKernel<T, 16, true>::launch(a, lc) : SplitKernel<T, 16, false>::launch(a, lc);
+    case 32: return a.trace ? SplitKernel<T, 32, true>::launch(a, lc) : SplitKernel<T, 32, false>::launch(a, lc);
+    case 64: return a.trace ? SplitKernel<T, 64, true>::launch(a, lc) : SplitKernel<T, 64, false>::launch(a, lc);
     default: return cudaErrorInvalidValue;
   }
 }
@@ -840,10 +841,10 @@ cudaError_t split_by_rank(int rank, const ApplyArgs& a, const LaunchCfg& lc) {
 template <typename T>
 int split_grid_by_rank(int rank) {
   switch (rank) {
-    case 8: return SplitKernel<T, 8>::max_grid();
-    case 16: return SplitKernel<T, 16>::max_grid();
-    case 32: return SplitKernel<T, 32>::max_grid();
-    case 64: return SplitKernel<T, 64>::max_grid();
+    case 8: return SplitKernel<T, 8, false>::max_grid();
+    case 16: return SplitKernel<T, 16, false>::max_grid();
+    case 32: return SplitKernel<T, 32, false>::max_grid();
+    case 64: return SplitKernel<T, 64, false>::max_grid();
     default: return 0;
   }
 }

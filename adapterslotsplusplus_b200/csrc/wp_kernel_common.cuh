@@ -51,6 +51,28 @@ __device__ __forceinline__ void trace_unit(unsigned long long* base, int u, int 
     base[blockIdx.x * kTraceSlots + 8 + kTraceSegMarks + kTraceMarks * u + k] = global_timer_ns();
 }
 
+// Tracing is a compile-time variant of the kernels: the production
+// instantiations carry none of it (its code alone slowed a launch by ~12 %,
+// even when switched off at run time).
+template <bool TR>
+__device__ __forceinline__ void trace_mark_t(unsigned long long* base, int k) {
+  if constexpr (TR) trace_mark(base, k);
+}
+template <bool TR>
+__device__ __forceinline__ void trace_unit_t(unsigned long long* base, int u, int k) {
+  if constexpr (TR) trace_unit(base, u, k);
+}
+
+struct TraceOff {
+  __device__ void init(unsigned long long*, bool) {}
+  __device__ void dep() {}
+  __device__ unsigned long long before_wait() { return 0ull; }
+  __device__ void after_wait(unsigned long long) {}
+  __device__ void mark(int) {}
+  __device__ void seg(int, int) {}
+  __device__ void finish() {}
+};
+
 struct Trace {
   unsigned long long* rec = nullptr;
   unsigned long long t_start = 0, t_dep = 0, t_first = 0, waited = 0, units = 0;
