@@ -147,7 +147,7 @@ struct ApplyCfg {
   static_assert(!DEC || PW >= 4 * kSnakeMax * 4, "the partial slots hold the table-ordering scratch");
 };
 
-template <typename T, int R, bool DEC, bool TR>
+template <typename T, int R, bool DEC, bool TR, bool LF>
 __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constant__ ApplyArgs a) {
   using C = ApplyCfg<R, DEC>;
   using E = Elem<T>;
@@ -183,6 +183,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const bool producer = warp == kProducerWarp;
+  // LF: the live fused single-slice call with a tensor-map-aligned y (the
+  // serving hot path), compiled without the other modes' branches
+  const bool registry = !LF && a.registry != 0;
+  const bool y_tma = LF || a.y_tma != 0;
+  const int nslices = LF ? 1 : a.nslices;
   const uint32_t q = cluster_ctarank();
   const uint32_t CL = cluster_nctarank();
   const int cid = static_cast<int>(cluster_id_x());
@@ -213,15 +218,15 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   if (producer && lane == 0) {
     if (a.mode & kModeShrink) {
       for (int i = 0; i < 3; ++i) prefetch_tmap(&a.tmap_x[i]);
-      if (!a.registry) prefetch_tmap(&a.tmap_a);
+      if (!registry) prefetch_tmap(&a.tmap_a);
     }
-    if ((a.mode & kModeExpand) && a.y_tma)
+    if ((a.mode & kModeExpand) && y_tma)
       for (int i = 0; i < 3; ++i) prefetch_tmap(&a.tmap_y[i]);
-    if ((a.mode & kModeExpand) && C::BTMA && !a.registry) prefetch_tmap(&a.tmap_b);
-    for (int sl = 1; sl < a.nslices && sl < kMaxSlices; ++sl) {
+    if ((a.mode & kModeExpand) && C::BTMA && !registry) prefetch_tmap(&a.tmap_b);
+    for (int sl = 1; sl < nslices && sl < kMaxSlices; ++sl) {
       prefetch_tmap(&a.tmap_a_x[sl - 1]);
       if (C::BTMA) prefetch_tmap(&a.tmap_b_x[sl - 1]);
-      if (a.y_tma)
+      if (y_tma)
         for (int i = 0; i < 3; ++i) prefetch_tmap(&a.tmap_y_x[sl - 1][i]);
     }
   }
@@ -234,8 +239,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   if (use_tmem) tc_fence_after();
   cluster_sync_hw();  // every CTA's cluster barrier is initialised before anyone arrives on it
 
-  const bool do_sh = (a.mode & kModeShrink) != 0;
-  const bool do_ex = (a.mode & kModeExpand) != 0;
+  const bool do_sh = LF || (a.mode & kModeShrink) != 0;
+  const bool do_ex = LF || (a.mode & kModeExpand) != 0;
   const int kA0 = static_cast<int>(q) * a.split_len;
   const int nA = do_sh ? (max(0, min(a.split_len, a.d - kA0)) + C::KC - 1) / C::KC : 0;
   // this CTA's expand columns (a helper cluster may take half of a segment's
@@ -246,7 +251,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   // decode variant: the y box of an expand stage goes back to global memory
   // with one tensor store when its rows are exactly the segment's rows
   auto y_by_tma = [&](int n) -> bool {
-    return DEC && a.y_tma && a.o_sliced && (n == 8 || n == 16 || n == 32);
+    return DEC && y_tma && a.o_sliced && (n == 8 || n == 16 || n == 32);
   };
 
   // ---- segment table of this cluster (all threads) -------------------------
@@ -302,7 +307,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   // Multi-slice calls: virtual segment v is segment v % nseg of slice
   // v / nseg; its descriptor carries the slice in the (live-mode unused)
   // alpha field.
-  const int S_sl = a.nslices > 1 ? a.nslices : 1;
+  const int S_sl = nslices > 1 ? nslices : 1;
   int nseg_t = 0;  // segments of the table (not virtual)
   auto put_desc = [&](int slot, int v) {
     const int seg = v % nseg_t;
@@ -414,8 +419,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           if (parts & 1) {
             mbar_arrive_expect_tx(bar, 4 * C::ABOX + 4 * box_bytes);
             const int sl = slice_of(s);
-            const void* amap = a.registry ? s.a : static_cast<const void*>(sl ? &a.tmap_a_x[sl - 1] : &a.tmap_a);
-            const int aid = a.registry ? 0 : s.adapter_id;
+            const void* amap = registry ? s.a : static_cast<const void*>(sl ? &a.tmap_a_x[sl - 1] : &a.tmap_a);
+            const int aid = registry ? 0 : s.adapter_id;
             if (a.d_sliced) {
               tma_load_4d_ef(st, amap, 0, 0, k0 / kBoxCols, aid, bar, ef);
             } else {
@@ -438,21 +443,21 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           if (parts & 1) {
             if constexpr (C::BTMA) {
               // one 256-row box of B, rows past o zero-filled
-              mbar_arrive_expect_tx(bar, 256 * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
+              mbar_arrive_expect_tx(bar, 256 * R * 2 + (y_tma ? 4 * box_bytes : 0u));
               const int sl = slice_of(s);
-              const void* bmap = a.registry ? s.b : static_cast<const void*>(sl ? &a.tmap_b_x[sl - 1] : &a.tmap_b);
-              const int bid = a.registry ? 0 : s.adapter_id;
+              const void* bmap = registry ? s.b : static_cast<const void*>(sl ? &a.tmap_b_x[sl - 1] : &a.tmap_b);
+              const int bid = registry ? 0 : s.adapter_id;
               tma_load_3d_ef(st + 4 * C::XBOX, bmap, 0, oc, bid, bar, ef);
             } else {
-              mbar_arrive_expect_tx(bar, wc * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
+              mbar_arrive_expect_tx(bar, wc * R * 2 + (y_tma ? 4 * box_bytes : 0u));
               const int sl = slice_of(s);
-              const T* B = a.registry ? static_cast<const T*>(s.b)
+              const T* B = registry ? static_cast<const T*>(s.b)
                                       : static_cast<const T*>(sl ? a.wb_base_x[sl - 1] : a.wb_base) +
                                             static_cast<int64_t>(s.adapter_id) * (sl ? a.wb_stride_x[sl - 1] : a.wb_stride);
               bulk_g2s(st + 4 * C::XBOX, B + static_cast<int64_t>(oc) * R, wc * R * 2, bar);
             }
           }
-          if ((parts & 2) && a.y_tma) {
+          if ((parts & 2) && y_tma) {
             if (a.o_sliced) {
               tma_load_3d(st, slice_of(s) ? &a.tmap_y_x[slice_of(s) - 1][bi] : &a.tmap_y[bi], 0, s.token_start,
                           oc / kBoxCols, bar);
@@ -711,7 +716,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     if (tid == 0 && n == 0 && a.err) atomicOr(a.err, kErrBadSegment);
     // x / y slices are (8 << box_index(n)) rows of 128 bytes; this warp reads slice warp / 2
     const uint32_t xsl = static_cast<uint32_t>((warp >> 1) * ((8 << box_index(n)) * 128));
-    const float alpha = a.registry ? s.alpha : a.scale;
+    const float alpha = registry ? s.alpha : a.scale;
 
     if (do_sh) {
       if constexpr (DEC) {
@@ -1017,7 +1022,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
               const float4 d1 = reinterpret_cast<const float4*>(dr)[1];
               const float dv[8] = {d0.x, d0.y, d0.z, d0.w, d1.x, d1.y, d1.z, d1.w};
               T* yp = yg + static_cast<int64_t>(s.token_start + t) * a.y_ld + yoff_of(s) + oc + col;
-              if (a.y_tma) {
+              if (y_tma) {
                 const int4 yv = *reinterpret_cast<const int4*>(yb + t * 128 + ((cib ^ (t & 7)) << 4));
                 const uint32_t* yw = reinterpret_cast<const uint32_t*>(&yv);
                 int4 out;
@@ -1091,7 +1096,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
             // aligned) is copied in here by the warp itself, element by element.
             uint8_t* ybox = const_cast<uint8_t*>(st) + xsl;
             const int colw0 = warp * 32;  // first column of this warp in the stage
-            if (!a.y_tma) {
+            if (!y_tma) {
               const T* ysrc = yg + static_cast<int64_t>(s.token_start) * a.y_ld + yoff_of(s) + oc + colw0;
   #pragma unroll 1
               for (int e = lane; e < n * 32; e += 32) {
@@ -1177,7 +1182,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
               tr.mark(4);
               if (tmy) {
                 fence_proxy_async_smem();  // the tensor store reads these writes
-              } else if (a.y_tma) {
+              } else if (y_tma) {
                 __syncwarp();
                 const int sub = lane & 3;
                 const int colw = colw0 + sub * 8;  // column of this lane's 16-byte chunk in the stage
@@ -1266,7 +1271,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
 
 namespace {
 
-template <typename T, int R, bool DEC, bool TR>
+template <typename T, int R, bool DEC, bool TR, bool LF>
 struct ApplyKernel {
   using C = ApplyCfg<R, DEC>;
   static bool prepare() {
@@ -1275,7 +1280,7 @@ struct ApplyKernel {
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (done.load() & bit) return true;
-    if (cudaFuncSetAttribute(apply_kernel<T, R, DEC, TR>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+    if (cudaFuncSetAttribute(apply_kernel<T, R, DEC, TR, LF>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
         cudaSuccess)
       return false;
     done.fetch_or(bit);
@@ -1299,7 +1304,7 @@ struct ApplyKernel {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = lc.pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, apply_kernel<T, R, DEC, TR>, a);
+    return cudaLaunchKernelEx(&cfg, apply_kernel<T, R, DEC, TR, LF>, a);
   }
 
   static int max_grid(int cluster) {
@@ -1317,7 +1322,7 @@ struct ApplyKernel {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int nclusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&nclusters, apply_kernel<T, R, DEC, TR>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&nclusters, apply_kernel<T, R, DEC, TR, LF>, &cfg) != cudaSuccess) {
       cudaGetLastError();
       return 0;
     }
@@ -1327,8 +1332,11 @@ struct ApplyKernel {
 
 template <typename T, int R>
 cudaError_t apply_variant(const ApplyArgs& a, const LaunchCfg& lc) {
-  if (a.trace) return lc.dec ? ApplyKernel<T, R, true, true>::launch(a, lc) : ApplyKernel<T, R, false, true>::launch(a, lc);
-  return lc.dec ? ApplyKernel<T, R, true, false>::launch(a, lc) : ApplyKernel<T, R, false, false>::launch(a, lc);
+  if (a.trace)
+    return lc.dec ? ApplyKernel<T, R, true, true, false>::launch(a, lc) : ApplyKernel<T, R, false, true, false>::launch(a, lc);
+  const bool live_fused = a.mode == kModeFused && !a.registry && a.nslices <= 1 && a.y_tma;
+  if (lc.dec && live_fused) return ApplyKernel<T, R, true, false, true>::launch(a, lc);
+  return lc.dec ? ApplyKernel<T, R, true, false, false>::launch(a, lc) : ApplyKernel<T, R, false, false, false>::launch(a, lc);
 }
 
 template <typename T>
@@ -1345,10 +1353,10 @@ cudaError_t apply_by_rank(int rank, const ApplyArgs& a, const LaunchCfg& lc) {
 template <typename T>
 int max_grid_by_rank(int rank, int cluster, bool dec) {
   switch (rank) {
-    case 8: return dec ? ApplyKernel<T, 8, true, false>::max_grid(cluster) : ApplyKernel<T, 8, false, false>::max_grid(cluster);
-    case 16: return dec ? ApplyKernel<T, 16, true, false>::max_grid(cluster) : ApplyKernel<T, 16, false, false>::max_grid(cluster);
-    case 32: return dec ? ApplyKernel<T, 32, true, false>::max_grid(cluster) : ApplyKernel<T, 32, false, false>::max_grid(cluster);
-    case 64: return dec ? ApplyKernel<T, 64, true, false>::max_grid(cluster) : ApplyKernel<T, 64, false, false>::max_grid(cluster);
+    case 8: return dec ? ApplyKernel<T, 8, true, false, false>::max_grid(cluster) : ApplyKernel<T, 8, false, false, false>::max_grid(cluster);
+    case 16: return dec ? ApplyKernel<T, 16, true, false, false>::max_grid(cluster) : ApplyKernel<T, 16, false, false, false>::max_grid(cluster);
+    case 32: return dec ? ApplyKernel<T, 32, true, false, false>::max_grid(cluster) : ApplyKernel<T, 32, false, false, false>::max_grid(cluster);
+    case 64: return dec ? ApplyKernel<T, 64, true, false, false>::max_grid(cluster) : ApplyKernel<T, 64, false, false, false>::max_grid(cluster);
     default: return 0;
   }
 }
