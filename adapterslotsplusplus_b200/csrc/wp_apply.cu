@@ -160,6 +160,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   uint64_t* cbar = reinterpret_cast<uint64_t*>(smem + 256);
   volatile int* s_bad = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS);
   volatile int* s_issued = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS + 4);
+  volatile int* s_armed = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS + 8);  // stages armed by the producer
   int4* sdesc = reinterpret_cast<int4*>(smem + C::OFF_DESC);
   float* Ps = reinterpret_cast<float*>(smem + C::OFF_P);
   float* Hs = reinterpret_cast<float*>(smem + C::OFF_H);
@@ -213,6 +214,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
     *s_bad = 0;
     *s_issued = 0;
+    *s_armed = 0;
     fence_mbar_init();
   }
   if (producer && lane == 0) {
@@ -401,80 +403,86 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const uint32_t t_sh = tbase;
   constexpr uint32_t kAbf = E::is_bf16 ? 1u : 0u;
 
+  // TMA issue of stage-unit u into `stage`. parts: 1 = arm the stage's
+  // barrier (weights and activations) and load the weights, 2 = load the
+  // activations. ef: the L2 evict-first policy of the weight loads.
+  auto issue = [&](int u, int stage, int parts, uint64_t ef) {
+    const DevSeg s = desc(u / ups);
+    const int sub = u % ups;
+    const int n = clamp_rows(s.token_count);
+    const int bi = box_index(n);
+    const uint32_t box_bytes = (8u << bi) * 128u;  // one 64-column slice of x or y
+    uint8_t* st = stage_base + stage * C::STAGE;
+    uint64_t* bar = &full[stage];
+    if (sub < nA) {
+      const int k0 = kA0 + sub * C::KC;
+      if (parts & 1) {
+        mbar_arrive_expect_tx(bar, 4 * C::ABOX + 4 * box_bytes);
+        const int sl = slice_of(s);
+        const void* amap = registry ? s.a : static_cast<const void*>(sl ? &a.tmap_a_x[sl - 1] : &a.tmap_a);
+        const int aid = registry ? 0 : s.adapter_id;
+        if (a.d_sliced) {
+          tma_load_4d_ef(st, amap, 0, 0, k0 / kBoxCols, aid, bar, ef);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j) tma_load_3d_ef(st + j * C::ABOX, amap, k0 + j * kBoxCols, 0, aid, bar, ef);
+        }
+      }
+      if (parts & 2) {
+        if (a.d_sliced) {
+          tma_load_3d(st + 4 * C::ABOX, &a.tmap_x[bi], 0, s.token_start, k0 / kBoxCols, bar);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_2d(st + 4 * C::ABOX + j * box_bytes, &a.tmap_x[bi], k0 + j * kBoxCols, s.token_start, bar);
+        }
+      }
+    } else {
+      const int oc = oB0 + (sub - nA) * C::W;
+      const int wc = min(C::W, a.o - oc);
+      if (parts & 1) {
+        if constexpr (C::BTMA) {
+          // one 256-row box of B, rows past o zero-filled
+          mbar_arrive_expect_tx(bar, 256 * R * 2 + (y_tma ? 4 * box_bytes : 0u));
+          const int sl = slice_of(s);
+          const void* bmap = registry ? s.b : static_cast<const void*>(sl ? &a.tmap_b_x[sl - 1] : &a.tmap_b);
+          const int bid = registry ? 0 : s.adapter_id;
+          tma_load_3d_ef(st + 4 * C::XBOX, bmap, 0, oc, bid, bar, ef);
+        } else {
+          mbar_arrive_expect_tx(bar, wc * R * 2 + (y_tma ? 4 * box_bytes : 0u));
+          const int sl = slice_of(s);
+          const T* B = registry ? static_cast<const T*>(s.b)
+                                  : static_cast<const T*>(sl ? a.wb_base_x[sl - 1] : a.wb_base) +
+                                        static_cast<int64_t>(s.adapter_id) * (sl ? a.wb_stride_x[sl - 1] : a.wb_stride);
+          bulk_g2s(st + 4 * C::XBOX, B + static_cast<int64_t>(oc) * R, wc * R * 2, bar);
+        }
+      }
+      if ((parts & 2) && y_tma) {
+        if (a.o_sliced) {
+          tma_load_3d(st, slice_of(s) ? &a.tmap_y_x[slice_of(s) - 1][bi] : &a.tmap_y[bi], 0, s.token_start,
+                      oc / kBoxCols, bar);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_2d(st + j * box_bytes, slice_of(s) ? &a.tmap_y_x[slice_of(s) - 1][bi] : &a.tmap_y[bi],
+                        oc + j * kBoxCols, s.token_start, bar);
+        }
+      }
+    }
+  };
+  const int first = min(S, total);  // stages issued before any is consumed
   if (warp == kProducerWarp) {
     // ======================= producer warp ===================================
     if (lane == 0) {
       const uint64_t ef = l2_evict_first_policy();  // adapter weights stream through L2 once
-      // parts: 1 = arm the stage's barrier and load the weights, 2 = load the activations
-      auto issue = [&](int u, int stage, int parts) {
-        const DevSeg s = desc(u / ups);
-        const int sub = u % ups;
-        const int n = clamp_rows(s.token_count);
-        const int bi = box_index(n);
-        const uint32_t box_bytes = (8u << bi) * 128u;  // one 64-column slice of x or y
-        uint8_t* st = stage_base + stage * C::STAGE;
-        uint64_t* bar = &full[stage];
-        if (sub < nA) {
-          const int k0 = kA0 + sub * C::KC;
-          if (parts & 1) {
-            mbar_arrive_expect_tx(bar, 4 * C::ABOX + 4 * box_bytes);
-            const int sl = slice_of(s);
-            const void* amap = registry ? s.a : static_cast<const void*>(sl ? &a.tmap_a_x[sl - 1] : &a.tmap_a);
-            const int aid = registry ? 0 : s.adapter_id;
-            if (a.d_sliced) {
-              tma_load_4d_ef(st, amap, 0, 0, k0 / kBoxCols, aid, bar, ef);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 4; ++j) tma_load_3d_ef(st + j * C::ABOX, amap, k0 + j * kBoxCols, 0, aid, bar, ef);
-            }
-          }
-          if (parts & 2) {
-            if (a.d_sliced) {
-              tma_load_3d(st + 4 * C::ABOX, &a.tmap_x[bi], 0, s.token_start, k0 / kBoxCols, bar);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                tma_load_2d(st + 4 * C::ABOX + j * box_bytes, &a.tmap_x[bi], k0 + j * kBoxCols, s.token_start, bar);
-            }
-          }
-        } else {
-          const int oc = oB0 + (sub - nA) * C::W;
-          const int wc = min(C::W, a.o - oc);
-          if (parts & 1) {
-            if constexpr (C::BTMA) {
-              // one 256-row box of B, rows past o zero-filled
-              mbar_arrive_expect_tx(bar, 256 * R * 2 + (y_tma ? 4 * box_bytes : 0u));
-              const int sl = slice_of(s);
-              const void* bmap = registry ? s.b : static_cast<const void*>(sl ? &a.tmap_b_x[sl - 1] : &a.tmap_b);
-              const int bid = registry ? 0 : s.adapter_id;
-              tma_load_3d_ef(st + 4 * C::XBOX, bmap, 0, oc, bid, bar, ef);
-            } else {
-              mbar_arrive_expect_tx(bar, wc * R * 2 + (y_tma ? 4 * box_bytes : 0u));
-              const int sl = slice_of(s);
-              const T* B = registry ? static_cast<const T*>(s.b)
-                                      : static_cast<const T*>(sl ? a.wb_base_x[sl - 1] : a.wb_base) +
-                                            static_cast<int64_t>(s.adapter_id) * (sl ? a.wb_stride_x[sl - 1] : a.wb_stride);
-              bulk_g2s(st + 4 * C::XBOX, B + static_cast<int64_t>(oc) * R, wc * R * 2, bar);
-            }
-          }
-          if ((parts & 2) && y_tma) {
-            if (a.o_sliced) {
-              tma_load_3d(st, slice_of(s) ? &a.tmap_y_x[slice_of(s) - 1][bi] : &a.tmap_y[bi], 0, s.token_start,
-                          oc / kBoxCols, bar);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                tma_load_2d(st + j * box_bytes, slice_of(s) ? &a.tmap_y_x[slice_of(s) - 1][bi] : &a.tmap_y[bi],
-                            oc + j * kBoxCols, s.token_start, bar);
-            }
-          }
-        }
-      };
-      const int first = min(S, total);
       trace_mark_t<TR>(a.trace, 9);
       if (a.prefetch_weights) {
         for (int u = 0; u < first; ++u) {
-          issue(u, u, 1);
+          issue(u, u, 1, ef);
+          if constexpr (DEC) {
+            __threadfence_block();
+            *s_armed = u + 1;  // the store thread may load this stage's activations
+          }
           trace_unit_t<TR>(a.trace, u, 7);
           if (u == 0) trace_mark_t<TR>(a.trace, 10);
         }
@@ -482,16 +490,20 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         pdl_wait_prior();
         pdl_launch_dependents();
         trace_mark_t<TR>(a.trace, 6);
-        for (int u = 0; u < first; ++u) issue(u, u, 2);
+        // decode variant: the store thread loads the first stages'
+        // activations right after the dependency wait, while this thread is
+        // still issuing weights
+        if constexpr (!DEC)
+          for (int u = 0; u < first; ++u) issue(u, u, 2, ef);
       } else {
-        for (int u = 0; u < first; ++u) issue(u, u, 3);
+        for (int u = 0; u < first; ++u) issue(u, u, 3, ef);
       }
       *s_issued = first;
       for (int u = first; u < total; ++u) {
         const int stage = u % S;
         if (!mbar_wait_bounded(&empty[stage], ((u / S) - 1) & 1, a.err)) *s_bad = 1;
         if (*s_bad) break;
-        issue(u, stage, 3);
+        issue(u, stage, 3, ef);
         trace_unit_t<TR>(a.trace, u, 7);
         *s_issued = u + 1;
       }
@@ -519,7 +531,24 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       // For every expand stage whose y box is stored by TMA: wait until the
       // compute warps have written it (ydone), store it, wait until the store
       // has read shared memory, then free the stage for the producer.
-      if (lane != 0 || !do_ex) return;
+      if (lane != 0) return;
+      if (a.prefetch_weights) {
+        // the first stages' activations, as soon as the dependency is met
+        for (int u = 0; u < first; ++u) {
+          bool armed = *s_armed > u;
+          for (int spin = 0; !armed && spin < (1 << 22); ++spin) {
+            __nanosleep(32);
+            armed = *s_armed > u;
+          }
+          if (!armed) {
+            *s_bad = 1;
+            if (a.err) atomicOr(a.err, kErrWaitTimeout);
+            break;
+          }
+          issue(u, u, 2, 0ull);
+        }
+      }
+      if (!do_ex) return;
       uint32_t ypar = 0u;
       int u = 0;
       for (int sj = 0; sj < nmine; ++sj) {
@@ -1332,9 +1361,11 @@ struct ApplyKernel {
 
 template <typename T, int R>
 cudaError_t apply_variant(const ApplyArgs& a, const LaunchCfg& lc) {
-  if (a.trace)
-    return lc.dec ? ApplyKernel<T, R, true, true, false>::launch(a, lc) : ApplyKernel<T, R, false, true, false>::launch(a, lc);
   const bool live_fused = a.mode == kModeFused && !a.registry && a.nslices <= 1 && a.y_tma;
+  if (a.trace) {
+    if (lc.dec && live_fused) return ApplyKernel<T, R, true, true, true>::launch(a, lc);
+    return lc.dec ? ApplyKernel<T, R, true, true, false>::launch(a, lc) : ApplyKernel<T, R, false, true, false>::launch(a, lc);
+  }
   if (lc.dec && live_fused) return ApplyKernel<T, R, true, false, true>::launch(a, lc);
   return lc.dec ? ApplyKernel<T, R, true, false, false>::launch(a, lc) : ApplyKernel<T, R, false, false, false>::launch(a, lc);
 }
