@@ -131,11 +131,11 @@ struct ApplyCfg {
   static constexpr uint32_t UMMA_LAYOUT = R == 64 ? 2u : (R == 32 ? 4u : 6u);
   static constexpr int DPITCH = 256 + 4;  // floats per row of the expand result tile Ds (bank-shifted rows)
   static constexpr int DS = TC ? 32 * DPITCH * 4 : 0;
-  // decode variant: shrink partials of 4 warps (32 tokens x PITCH floats each) for the cross-warp sum
+  // decode variant: shrink partials of the 8 compute warps (32 tokens x PITCH floats each) for the cross-warp sum
   static constexpr int PSLOT = 32 * PITCH;
-  static constexpr int PW = DEC ? 4 * PSLOT * 4 : 0;
+  static constexpr int PW = DEC ? 8 * PSLOT * 4 : 0;
   // decode variant: receive slots of the cluster exchange, [2 segment parities][CLMAX ranks]
-  static constexpr int CLMAX = R == 64 ? 2 : 4;
+  static constexpr int CLMAX = DEC ? 2 : 4;
   static constexpr int RX = DEC ? 2 * CLMAX * PSLOT * 4 : 0;
   static constexpr int FIXED = OFF_END + DS + PW + RX + 1024 + (TC ? 2 * HT : 0);
   static constexpr int FIT = (kSmemMax - FIXED) / STAGE;
@@ -807,9 +807,10 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           default: shrink_units(IntC<4>{}); break;
         }
         tr.seg(0, sj);
-        // cross-warp sum: warps 4-7 park their partials, warps 0-3 add them and
-        // park the pair sums; the four slots are added below (fixed order)
-        auto park = [&](float* dst) {
+        // cross-warp sum: every warp parks its partial in a slot of its own;
+        // the eight slots are added per element below, in a fixed order
+        {
+          float* dst = Pw + warp * C::PSLOT;
 #pragma unroll
           for (int mt = 0; mt < MT; ++mt)
 #pragma unroll
@@ -820,81 +821,73 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
                 const int t = j * 8 + 2 * c + (e & 1);
                 if (r < R) dst[t * PITCH + r] = acc[mt][j][e];
               }
-        };
-        if (warp >= 4) park(Pw + (warp - 4) * C::PSLOT);
-        named_sync(kBarCompute, kComputeThreads);
-        if (warp < 4) {
-          const float* src = Pw + warp * C::PSLOT;
-#pragma unroll
-          for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-            for (int j = 0; j < 4; ++j)
-#pragma unroll
-              for (int e = 0; e < 4; ++e) {
-                const int r = mt * 16 + g + (e >> 1) * 8;
-                const int t = j * 8 + 2 * c + (e & 1);
-                if (r < R) acc[mt][j][e] += src[t * PITCH + r];
-              }
-          park(Pw + warp * C::PSLOT);
         }
         named_sync(kBarCompute, kComputeThreads);
-        // ---- 2. cluster exchange (push): this CTA's partial rows go into its
-        // own receive slot and, by st.async, into the same slot of every peer,
-        // completing bytes on the peer's rx_full barrier; the slot of a segment
-        // parity is rewritten only after every peer has released it (rx_free).
+        // ---- 2. cluster exchange (push): each thread sums the eight slots of
+        // its elements and pushes them by st.async into this CTA's slot of
+        // every peer, completing bytes on the peer's rx_full barrier; it keeps
+        // its own sums in registers. A slot of a segment parity is rewritten
+        // only after every peer has released it (rx_free). Every CTA adds the
+        // ranks' partials in rank order, so all of them get the same H.
         const int par = sj & 1;
         const uint32_t use = static_cast<uint32_t>(sj >> 1);  // uses of this parity so far
         float* rx = Rx + par * C::CLMAX * C::PSLOT;
         if (CL > 1 && use > 0 && !*s_bad && !mbar_wait_cluster_bounded(&rx_free[par], (use - 1) & 1, a.err)) *s_bad = 1;
         constexpr int Q4 = R / 4;  // 16-byte chunks per partial row
+        constexpr int KE = (32 * Q4 + kComputeThreads - 1) / kComputeThreads;  // elements per thread at most
         const int nch = n * Q4;
+        float4 own[KE];
         if (!*s_bad) {
-          for (int e4 = tid; e4 < nch; e4 += kComputeThreads) {
-            const int off = (e4 / Q4) * PITCH + (e4 % Q4) * 4;
-            float4 v;
-            {
-              const float4 p0 = *reinterpret_cast<const float4*>(Pw + off);
-              const float4 p1 = *reinterpret_cast<const float4*>(Pw + C::PSLOT + off);
-              const float4 p2 = *reinterpret_cast<const float4*>(Pw + 2 * C::PSLOT + off);
-              const float4 p3 = *reinterpret_cast<const float4*>(Pw + 3 * C::PSLOT + off);
-              v.x = (p0.x + p1.x) + (p2.x + p3.x);
-              v.y = (p0.y + p1.y) + (p2.y + p3.y);
-              v.z = (p0.z + p1.z) + (p2.z + p3.z);
-              v.w = (p0.w + p1.w) + (p2.w + p3.w);
-            }
-            float* mine = rx + q * C::PSLOT + off;
-            *reinterpret_cast<float4*>(mine) = v;
-            for (uint32_t i = 1; i < CL; ++i) {
-              const uint32_t peer = (q + i) % CL;
-              st_async_v4(mapa(smem_u32(mine), peer), v, mapa(smem_u32(&rx_full[par]), peer));
+#pragma unroll
+          for (int k = 0; k < KE; ++k) {
+            const int e4 = tid + k * kComputeThreads;
+            if (e4 < nch) {
+              const int off = (e4 / Q4) * PITCH + (e4 % Q4) * 4;
+              float4 p[8];
+#pragma unroll
+              for (int w = 0; w < 8; ++w) p[w] = *reinterpret_cast<const float4*>(Pw + w * C::PSLOT + off);
+              float4 v;
+              v.x = ((p[0].x + p[1].x) + (p[2].x + p[3].x)) + ((p[4].x + p[5].x) + (p[6].x + p[7].x));
+              v.y = ((p[0].y + p[1].y) + (p[2].y + p[3].y)) + ((p[4].y + p[5].y) + (p[6].y + p[7].y));
+              v.z = ((p[0].z + p[1].z) + (p[2].z + p[3].z)) + ((p[4].z + p[5].z) + (p[6].z + p[7].z));
+              v.w = ((p[0].w + p[1].w) + (p[2].w + p[3].w)) + ((p[4].w + p[5].w) + (p[6].w + p[7].w));
+              own[k] = v;
+              const uint32_t mine = smem_u32(rx + q * C::PSLOT + off);
+              for (uint32_t i = 1; i < CL; ++i) {
+                const uint32_t peer = (q + i) % CL;
+                st_async_v4(mapa(mine, peer), v, mapa(smem_u32(&rx_full[par]), peer));
+              }
             }
           }
         }
         if (tid == 0) mbar_arrive_expect_tx(&rx_full[par], (CL - 1) * static_cast<uint32_t>(nch) * 16u);
-        named_sync(kBarCompute, kComputeThreads);  // own slot written
         tr.seg(3, sj);
-        if (!*s_bad && !mbar_wait_cluster_bounded(&rx_full[par], use & 1, a.err)) *s_bad = 1;
+        if (CL > 1 && !*s_bad && !mbar_wait_cluster_bounded(&rx_full[par], use & 1, a.err)) *s_bad = 1;
         tr.seg(1, sj);
         if (!*s_bad) {
-          for (int e4 = tid; e4 < nch; e4 += kComputeThreads) {
-            const int t = e4 / Q4;
-            const int off = t * PITCH + (e4 % Q4) * 4;
-            float4 sum = *reinterpret_cast<const float4*>(rx + off);
-            for (uint32_t i = 1; i < CL; ++i) {
-              const float4 v = *reinterpret_cast<const float4*>(rx + i * C::PSLOT + off);
-              sum.x += v.x;
-              sum.y += v.y;
-              sum.z += v.z;
-              sum.w += v.w;
-            }
-            sum.x *= alpha;
-            sum.y *= alpha;
-            sum.z *= alpha;
-            sum.w *= alpha;
-            if (do_ex) {
-              *reinterpret_cast<float4*>(Hs + off) = sum;
-            } else {
-              *reinterpret_cast<float4*>(a.h + static_cast<int64_t>(s.token_start + t) * R + (e4 % Q4) * 4) = sum;
+#pragma unroll
+          for (int k = 0; k < KE; ++k) {
+            const int e4 = tid + k * kComputeThreads;
+            if (e4 < nch) {
+              const int t = e4 / Q4;
+              const int off = t * PITCH + (e4 % Q4) * 4;
+              float4 sum = q == 0 ? own[k] : *reinterpret_cast<const float4*>(rx + off);
+              for (uint32_t i = 1; i < CL; ++i) {
+                const float4 v = i == q ? own[k] : *reinterpret_cast<const float4*>(rx + i * C::PSLOT + off);
+                sum.x += v.x;
+                sum.y += v.y;
+                sum.z += v.z;
+                sum.w += v.w;
+              }
+              sum.x *= alpha;
+              sum.y *= alpha;
+              sum.z *= alpha;
+              sum.w *= alpha;
+              if (do_ex) {
+                *reinterpret_cast<float4*>(Hs + off) = sum;
+              } else {
+                *reinterpret_cast<float4*>(a.h + static_cast<int64_t>(s.token_start + t) * R + (e4 % Q4) * 4) = sum;
+              }
             }
           }
         }
