@@ -184,11 +184,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const int warp = tid >> 5;
   const int lane = tid & 31;
   const bool producer = warp == kProducerWarp;
-  // LF: the live fused single-slice call with a tensor-map-aligned y (the
-  // serving hot path), compiled without the other modes' branches
+  // LF: the live fused call with a tensor-map-aligned y (the serving hot
+  // path, one or several slices), compiled without the other modes' branches
   const bool registry = !LF && a.registry != 0;
   const bool y_tma = LF || a.y_tma != 0;
-  const int nslices = LF ? 1 : a.nslices;
+  const int nslices = a.nslices;
   const uint32_t q = cluster_ctarank();
   const uint32_t CL = cluster_nctarank();
   const int cid = static_cast<int>(cluster_id_x());
@@ -1354,7 +1354,7 @@ struct ApplyKernel {
 
 template <typename T, int R>
 cudaError_t apply_variant(const ApplyArgs& a, const LaunchCfg& lc) {
-  const bool live_fused = a.mode == kModeFused && !a.registry && a.nslices <= 1 && a.y_tma;
+  const bool live_fused = a.mode == kModeFused && !a.registry && a.y_tma;
   if (a.trace) {
     if (lc.dec && live_fused) return ApplyKernel<T, R, true, true, true>::launch(a, lc);
     return lc.dec ? ApplyKernel<T, R, true, true, false>::launch(a, lc) : ApplyKernel<T, R, false, true, false>::launch(a, lc);
