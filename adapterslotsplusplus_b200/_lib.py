@@ -81,7 +81,7 @@ SIGNATURES = {
                                   ctypes.POINTER(_vp), ctypes.POINTER(_i64), ctypes.POINTER(_i32), _i32, _f32,
                                   _i32, _i32, _i32, _i32, _i64, _i64, _i32, _vp]),
     "wp_add_lora_shrink": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _f32, _i32, _i32, _i32, _i64, _i32, _vp]),
-    "wp_add_lora_expand": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i64, _i32, _i32, _vp]),
+    "wp_add_lora_expand": (_int, [_vp, _vp, _vp, _vp, _i64, _i32, _i32, _i32, _i32, _i64, _i32, _i32, _vp]),
     "wp_prefetch_adapter": (_i32, [_vp, _i32]),
     "wp_prefetch_adapter_on": (_i32, [_vp, _i32, _vp]),
     "wp_is_prefetch_ready": (_i32, [_vp, _i32]),
@@ -96,6 +96,12 @@ SIGNATURES = {
     "wp_tp_init": (_int, [_vp, _vp, _i32, _i32]),
     "wp_tp_allreduce_f32": (_int, [_vp, _vp, _i64, _vp]),
     "wp_tp_destroy": (_int, [_vp]),
+    "wp_tp_mailbox_handle_bytes": (_i32, []),
+    "wp_tp_mailbox_create": (_int, [_vp, _i32, _i32, _i32, _vp]),
+    "wp_tp_mailbox_open": (_int, [_vp, _vp]),
+    "wp_tp_mailbox_close": (_int, [_vp]),
+    "wp_add_lora_row_parallel": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _f32, _i32, _i32, _i32, _i32, _i64,
+                                        _i64, _i32, _i32, _vp]),
 }
 
 _LIB = None

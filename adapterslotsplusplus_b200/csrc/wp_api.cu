@@ -122,6 +122,13 @@ struct wp_handle {
   // tensor parallel
   ncclComm_t comm = nullptr;
   int tp_rank = 0, tp_world = 1;
+  // row-parallel exchange over peer memory: this rank's mailbox, every
+  // rank's mailbox as mapped here (own at tp_rank), the exchange epoch
+  void* tp_mail_own = nullptr;
+  float* tp_mail[wp::kMaxTp] = {};
+  int mail_world = 0, mail_rank = 0, mail_tmax = 0;
+  int* d_tp_seq = nullptr;
+  bool tp_exchange = false;  // set for the duration of one row-parallel launch
 };
 
 namespace {
@@ -386,6 +393,7 @@ int wp_destroy(wp_handle* h) {
   if (!h) return WP_OK;
   DeviceGuard dg(h->device);
   if (h->comm) ncclCommDestroy(h->comm);
+  wp_tp_mailbox_close(h);
   if (h->prefetch_stream) cudaStreamSynchronize(h->prefetch_stream);
   cudaDeviceSynchronize();
   for (auto& kv : h->store) free_adapter(kv.second);
@@ -946,6 +954,14 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
                            y_ld, 8 << i))
         return fail(h, WP_ERR_CUDA, "apply: cuTensorMapEncodeTiled(y) failed");
   }
+  if (h->tp_exchange) {
+    a.tp_world = h->mail_world;
+    a.tp_rank = h->mail_rank;
+    a.tp_tmax = h->mail_tmax;
+    a.tp_smax = h->mail_tmax;
+    a.tp_seq = h->d_tp_seq;
+    for (int p = 0; p < wp::kMaxTp; ++p) a.tp_mail[p] = h->tp_mail[p];
+  }
   const bool pdl = h->cfg.use_pdl != 0;
   // Without PDL the kernel starts after its predecessor completed, so the
   // table and weights can always be read first. With PDL that needs the
@@ -957,8 +973,8 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   // the split kernel's item arithmetic is 32-bit (items x grid < 2^31) and its
   // run masks cover 2048 chunks
   const bool split_fits = static_cast<int64_t>(T) * nchunk_max * h->num_sms < (int64_t{1} << 31) && nchunk_max <= 2048;
-  bool want_split = kernel_choice(h) == 0;
-  if (kernel_choice(h) < 0 && mode == wp::kModeFused && !registry) {
+  bool want_split = kernel_choice(h) == 0 && !h->tp_exchange;
+  if (kernel_choice(h) < 0 && mode == wp::kModeFused && !registry && !h->tp_exchange) {
     int c0 = 1, g0 = 1;
     apply_plan(h, dtype, r, true, &c0, &g0);
     want_split = auto_split(h, stream, T, num_adapters, g0 / std::max(c0, 1), c0, d, o);
@@ -984,7 +1000,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
     }
   }
   int cluster = 1, grid = 1;
-  const bool dec = use_decode_kernel(h);
+  const bool dec = use_decode_kernel(h) || h->tp_exchange;  // the peer exchange lives in the decode variant
   apply_plan(h, dtype, r, dec, &cluster, &grid);
   a.split_len = round_up((std::max(d, 1) + cluster - 1) / cluster, wp::kStageK);
   a.oslice = round_up((std::max(o, 1) + cluster - 1) / cluster, wp::kStageCols);
@@ -1102,18 +1118,21 @@ int wp_add_lora_shrink(wp_handle* h, void* H, const void* x, const void* wa_base
                   static_cast<cudaStream_t>(stream_v));
 }
 
-int wp_add_lora_expand(wp_handle* h, void* y, const void* H, const void* wb_base, int64_t wb_stride0, int32_t T,
-                       int32_t out_features, int32_t rank, int64_t y_ld, int32_t y_offset, int32_t dtype,
-                       void* stream_v) {
+int wp_add_lora_expand(wp_handle* h, void* y, const void* H, const void* wb_base, int64_t wb_stride0,
+                       int32_t num_adapters, int32_t T, int32_t out_features, int32_t rank, int64_t y_ld,
+                       int32_t y_offset, int32_t dtype, void* stream_v) {
   if (!h) return fail(nullptr, WP_ERR_INVALID, "add_lora_expand: NULL handle");
   int rc = check_live(h, T, rank, dtype);
   if (!rc) rc = check_expand_args(h, y, y_ld, y_offset, out_features, wb_base, wb_stride0);
   if (rc) return rc;
+  if (num_adapters < 1) return fail(h, WP_ERR_INVALID, "add_lora_expand: num_adapters must be >= 1");
   if (!al16(H)) return fail(h, WP_ERR_INVALID, "add_lora_expand: H must be 16-byte aligned");
   DeviceGuard dg(h->device);
-  return do_apply(h, wp::kModeExpand, 0, h->d_live, h->d_live_num, T, rank, dtype, nullptr, 0, 0, nullptr, 0, 0, 0.f, y,
-                  y_ld, y_offset, out_features, wb_base, wb_stride0, const_cast<float*>(static_cast<const float*>(H)),
-                  static_cast<cudaStream_t>(stream_v));
+  // the B tensor map spans the whole stack (num_adapters), so every live
+  // adapter id addresses its own B
+  return do_apply(h, wp::kModeExpand, 0, h->d_live, h->d_live_num, T, rank, dtype, nullptr, 0, 0, nullptr, 0,
+                  num_adapters, 0.f, y, y_ld, y_offset, out_features, wb_base, wb_stride0,
+                  const_cast<float*>(static_cast<const float*>(H)), static_cast<cudaStream_t>(stream_v));
 }
 
 int wp_add_lora(wp_handle* h, void* y, const void* x, const void* wa_base, int64_t wa_stride0, const void* wb_base,
@@ -1263,6 +1282,88 @@ int wp_apply_plan(wp_handle* h, int32_t dtype, int32_t rank, int32_t* cluster, i
 }  // extern "C"
 
 // ---- tensor parallel ---------------------------------------------------------
+
+// ---- row-parallel exchange over peer memory -----------------------------------
+
+extern "C" int32_t wp_tp_mailbox_handle_bytes(void) { return static_cast<int32_t>(sizeof(cudaIpcMemHandle_t)); }
+
+extern "C" int wp_tp_mailbox_create(wp_handle* h, int32_t rank, int32_t world, int32_t max_tokens, void* handle_out) {
+  if (!h || !handle_out) return fail(h, WP_ERR_INVALID, "tp_mailbox_create: NULL argument");
+  if (world < 2 || world > wp::kMaxTp || rank < 0 || rank >= world)
+    return fail(h, WP_ERR_INVALID, "tp_mailbox_create: rank %d / world %d outside [2, %d] ranks", rank, world, wp::kMaxTp);
+  if (max_tokens < 1 || max_tokens > h->cfg.max_tokens)
+    return fail(h, WP_ERR_INVALID, "tp_mailbox_create: max_tokens %d outside [1, %d]", max_tokens, h->cfg.max_tokens);
+  DeviceGuard dg(h->device);
+  wp_tp_mailbox_close(h);
+  const size_t bytes = wp::TpMail::bytes(world, max_tokens, max_tokens);
+  WP_CUDA(h, cudaMalloc(&h->tp_mail_own, bytes));
+  WP_CUDA(h, cudaMemset(h->tp_mail_own, 0, bytes));
+  WP_CUDA(h, cudaMalloc(&h->d_tp_seq, 2 * sizeof(int)));
+  WP_CUDA(h, cudaMemset(h->d_tp_seq, 0, 2 * sizeof(int)));
+  cudaIpcMemHandle_t mh;
+  WP_CUDA(h, cudaIpcGetMemHandle(&mh, h->tp_mail_own));
+  std::memcpy(handle_out, &mh, sizeof(mh));
+  h->mail_world = world;
+  h->mail_rank = rank;
+  h->mail_tmax = max_tokens;
+  return WP_OK;
+}
+
+extern "C" int wp_tp_mailbox_open(wp_handle* h, const void* handles) {
+  if (!h || !handles) return fail(h, WP_ERR_INVALID, "tp_mailbox_open: NULL argument");
+  if (!h->tp_mail_own) return fail(h, WP_ERR_INVALID, "tp_mailbox_open: wp_tp_mailbox_create was not called");
+  DeviceGuard dg(h->device);
+  const char* hs = static_cast<const char*>(handles);
+  for (int p = 0; p < h->mail_world; ++p) {
+    if (p == h->mail_rank) {
+      h->tp_mail[p] = static_cast<float*>(h->tp_mail_own);
+      continue;
+    }
+    cudaIpcMemHandle_t mh;
+    std::memcpy(&mh, hs + p * sizeof(mh), sizeof(mh));
+    void* ptr = nullptr;
+    WP_CUDA(h, cudaIpcOpenMemHandle(&ptr, mh, cudaIpcMemLazyEnablePeerAccess));
+    h->tp_mail[p] = static_cast<float*>(ptr);
+  }
+  return WP_OK;
+}
+
+extern "C" int wp_tp_mailbox_close(wp_handle* h) {
+  if (!h) return WP_OK;
+  DeviceGuard dg(h->device);
+  if (h->tp_mail_own || h->d_tp_seq) cudaDeviceSynchronize();
+  for (int p = 0; p < wp::kMaxTp; ++p) {
+    if (h->tp_mail[p] && p != h->mail_rank) cudaIpcCloseMemHandle(h->tp_mail[p]);
+    h->tp_mail[p] = nullptr;
+  }
+  if (h->tp_mail_own) cudaFree(h->tp_mail_own);
+  if (h->d_tp_seq) cudaFree(h->d_tp_seq);
+  h->tp_mail_own = nullptr;
+  h->d_tp_seq = nullptr;
+  h->mail_world = 0;
+  return WP_OK;
+}
+
+extern "C" int wp_add_lora_row_parallel(wp_handle* h, void* y, const void* x, const void* wa_base, int64_t wa_stride0,
+                                        const void* wb_base, int64_t wb_stride0, int32_t num_adapters, float scale,
+                                        int32_t T, int32_t d_shard, int32_t out_features, int32_t rank, int64_t x_ld,
+                                        int64_t y_ld, int32_t y_offset, int32_t dtype, void* stream_v) {
+  if (!h) return fail(nullptr, WP_ERR_INVALID, "add_lora_row_parallel: NULL handle");
+  if (!h->tp_mail[h->mail_rank] || h->mail_world < 2)
+    return fail(h, WP_ERR_INVALID, "add_lora_row_parallel: the peer mailboxes are not open");
+  int rc = check_live(h, T, rank, dtype);
+  if (!rc) rc = check_shrink_args(h, x, x_ld, d_shard, wa_base, wa_stride0, num_adapters);
+  if (!rc) rc = check_expand_args(h, y, y_ld, y_offset, out_features, wb_base, wb_stride0);
+  if (rc) return rc;
+  if (T > h->mail_tmax) return fail(h, WP_ERR_INVALID, "add_lora_row_parallel: %d tokens exceed the mailbox (%d)", T, h->mail_tmax);
+  DeviceGuard dg(h->device);
+  h->tp_exchange = true;
+  rc = do_apply(h, wp::kModeFused, 0, h->d_live, h->d_live_num, T, rank, dtype, x, x_ld, d_shard, wa_base, wa_stride0,
+                num_adapters, scale, y, y_ld, y_offset, out_features, wb_base, wb_stride0, nullptr,
+                static_cast<cudaStream_t>(stream_v));
+  h->tp_exchange = false;
+  return rc;
+}
 
 extern "C" int32_t wp_tp_unique_id_bytes(void) { return static_cast<int32_t>(sizeof(ncclUniqueId)); }
 

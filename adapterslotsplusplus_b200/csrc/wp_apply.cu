@@ -258,6 +258,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
 
   // ---- segment table of this cluster (all threads) -------------------------
   int nmine = 0;
+  int seg_half = -1;  // helper pairs: which half of the output columns this cluster expands (0 / 1), else -1
   // Segments per cluster, for small tables (decode) ordered by decreasing
   // token count. Fewer segments than clusters: the largest segments get a
   // helper cluster each, and the pair splits the segment's output columns
@@ -295,6 +296,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     const int4 hdr = sh[0];
     const int count = reinterpret_cast<const int*>(sh + 1)[0];
     const int half = reinterpret_cast<const int*>(sh + 1)[1];
+    seg_half = half;
     __syncthreads();
     if (hdr.x == 0 || hdr.z != G || cid >= kPlanMaxClusters) return false;
     if (hdr.x == 1) {
@@ -347,6 +349,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       if (nmine) {
         const int pos = cid < solo ? helpers + cid : (cid - solo) >> 1;
         const int half = cid < solo ? -1 : ((cid - solo) & 1);
+        seg_half = half;
         const int ob = half == 1 ? osplit : 0;
         const int olen = half < 0 ? a.o : (half == 0 ? osplit : a.o - osplit);
         const int osl = (olen + static_cast<int>(CL) - 1) / static_cast<int>(CL);
@@ -673,6 +676,9 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     pdl_launch_dependents();
     tr.dep();
   }
+  // tensor parallelism: the epoch of this launch's peer exchange (after the
+  // dependency wait, so the previous launch's advance is visible)
+  const int tp_epoch = a.tp_world > 1 ? __ldcg(&a.tp_seq[0]) + 1 : 0;
   const int g = lane >> 2;
   const int c = lane & 3;
   const int quarter = warp & 3;  // TMEM lane quarter this warp may read
@@ -892,6 +898,56 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           }
         }
         named_sync(kBarCompute, kComputeThreads);  // slots read, H complete
+        if (a.tp_world > 1 && do_ex) {
+          // ---- 2b. tensor-parallel exchange over peer memory: H so far is
+          // this rank's slice of d. The primary cluster of the segment (its
+          // rank-0 CTA) writes it into every peer's mailbox, then raises its
+          // flag there (the launch epoch); every CTA of the segment waits for
+          // the peers' flags in its own mailbox and adds all ranks' partials in
+          // rank order, so every rank gets the same H.
+          const int W = a.tp_world, me = a.tp_rank, par = tp_epoch & 1;
+          const int nq = n * (R / 4);
+          if (q == 0 && seg_half <= 0) {
+            if (!*s_bad) {
+              for (int e4 = tid; e4 < nq; e4 += kComputeThreads) {
+                const int t = e4 / (R / 4), r0 = (e4 % (R / 4)) * 4;
+                const float4 v = *reinterpret_cast<const float4*>(Hs + t * PITCH + r0);
+                for (int p = 0; p < W; ++p)
+                  if (p != me)
+                    *reinterpret_cast<float4*>(TpMail::row(a.tp_mail[p], W, a.tp_tmax, par, me, s.token_start + t) + r0) = v;
+              }
+            }
+            __threadfence_system();  // this thread's rows reach the peers before any flag
+            named_sync(kBarCompute, kComputeThreads);
+            if (tid == 0)
+              for (int p = 0; p < W; ++p)
+                if (p != me)
+                  st_release_sys(TpMail::flag(a.tp_mail[p], W, a.tp_tmax, a.tp_smax, par, me, s.token_start), tp_epoch);
+          }
+          if (tid < W && tid != me && !*s_bad &&
+              !wait_flag_sys(TpMail::flag(a.tp_mail[me], W, a.tp_tmax, a.tp_smax, par, tid, s.token_start), tp_epoch, a.err))
+            *s_bad = 1;
+          named_sync(kBarCompute, kComputeThreads);
+          if (!*s_bad) {
+            for (int e4 = tid; e4 < nq; e4 += kComputeThreads) {
+              const int t = e4 / (R / 4), r0 = (e4 % (R / 4)) * 4;
+              float4* hp = reinterpret_cast<float4*>(Hs + t * PITCH + r0);
+              const float4 mine = *hp;
+              float4 sum = make_float4(0.f, 0.f, 0.f, 0.f);
+              for (int p = 0; p < W; ++p) {
+                const float4 v = p == me ? mine
+                                         : __ldcg(reinterpret_cast<const float4*>(
+                                               TpMail::row(a.tp_mail[me], W, a.tp_tmax, par, p, s.token_start + t) + r0));
+                sum.x += v.x;
+                sum.y += v.y;
+                sum.z += v.z;
+                sum.w += v.w;
+              }
+              *hp = sum;
+            }
+          }
+          named_sync(kBarCompute, kComputeThreads);  // full H
+        }
         // release the slots for the push two segments on (none after the last two)
         if (tid == 0 && CL > 1 && sj + 2 < nmine)
           for (uint32_t i = 1; i < CL; ++i) mbar_arrive_remote_relaxed(mapa(smem_u32(&rx_free[par]), (q + i) % CL));
@@ -1275,6 +1331,16 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     if (tid == 0) {
       const int issued = *s_issued;
       for (int u = max(0, issued - S); u < issued; ++u) mbar_wait_bounded(&full[u % S], (u / S) & 1, nullptr, kDrainNs);
+    }
+  }
+  if (a.tp_world > 1) {
+    // every wait of this CTA on the peers is over: count it; the last CTA
+    // advances the epoch for the next exchange launch
+    named_sync(kBarCompute, kComputeThreads);
+    if (tid == 0 && atomicAdd(&a.tp_seq[1], 1) == static_cast<int>(gridDim.x) - 1) {
+      a.tp_seq[1] = 0;
+      __threadfence();
+      atomicExch(&a.tp_seq[0], tp_epoch);
     }
   }
   if (use_tmem) {

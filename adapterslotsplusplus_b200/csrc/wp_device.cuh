@@ -86,6 +86,31 @@ __device__ __forceinline__ bool mbar_wait_bounded(uint64_t* bar, uint32_t parity
   }
 }
 
+// ---- flags shared with other GPUs (peer memory) ---------------------------
+
+__device__ __forceinline__ int ld_acquire_sys(const int* p) {
+  int v;
+  asm volatile("ld.acquire.sys.global.b32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+__device__ __forceinline__ void st_release_sys(int* p, int v) {
+  asm volatile("st.release.sys.global.b32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+// Waits (at most timeout_ns) for *p == want; raises kErrWaitTimeout on expiry.
+__device__ __forceinline__ bool wait_flag_sys(const int* p, int want, int* err,
+                                              unsigned long long timeout_ns = kWaitTimeoutNs) {
+  if (ld_acquire_sys(p) == want) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_sys(p) == want) return true;
+    if (global_timer_ns() - t0 > timeout_ns) {
+      if (err) atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
 // ---- bulk async copy (TMA, untiled) ---------------------------------------
 // dst (shared), src (global) 16-byte aligned, bytes a multiple of 16.
 

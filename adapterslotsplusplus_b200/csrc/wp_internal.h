@@ -56,6 +56,8 @@ struct ClusterPlan {
 
 // Slices of one multi-slice call (q, k, v of a fused qkv projection).
 constexpr int kMaxSlices = 3;
+constexpr int kMaxTp = 8;  // tensor-parallel ranks of the peer-memory exchange
+constexpr int kMaxRank = 64;  // largest LoRA rank
 
 // Which halves of the apply one launch runs.
 enum : int { kModeShrink = 1, kModeExpand = 2, kModeFused = 3 };
@@ -111,6 +113,34 @@ struct ApplyArgs {
   int64_t wb_stride_x[kMaxSlices - 1];
   const ClusterPlan* plan;  // clustered kernel: the segmenter's assignment for this table, or null
   int sync_cap;  // segments the counters cover
+  // Row-parallel tensor parallelism over peer memory (clustered decode
+  // kernel, tp_world > 1): after its cluster exchange, a segment's partial H
+  // (this rank's slice of d) goes into every peer's mailbox, and the full H is
+  // the sum of all ranks' partials in rank order. Mailbox of rank q (mapped
+  // in this process at tp_mail[q]): TpMail::data / flag below.
+  float* tp_mail[kMaxTp];
+  int* tp_seq;  // [2] on this rank: launch epoch of the exchange, CTAs finished in this launch
+  int tp_world;
+  int tp_rank;
+  int tp_tmax;  // token rows per (parity, source rank) in a mailbox
+  int tp_smax;  // segment flags per (parity, source rank)
+};
+
+// Mailbox layout: partial rows [2 parities][world][tmax][kMaxRank] fp32, then
+// flags [2][world][smax] int (the epoch that wrote the segment's rows).
+struct TpMail {
+  static __host__ __device__ size_t data_floats(int world, int tmax) {
+    return static_cast<size_t>(2) * world * tmax * kMaxRank;
+  }
+  static __host__ __device__ size_t bytes(int world, int tmax, int smax) {
+    return data_floats(world, tmax) * 4 + static_cast<size_t>(2) * world * smax * 4;
+  }
+  static __host__ __device__ float* row(float* mail, int world, int tmax, int par, int src, int t) {
+    return mail + ((static_cast<size_t>(par) * world + src) * tmax + t) * kMaxRank;
+  }
+  static __host__ __device__ int* flag(float* mail, int world, int tmax, int smax, int par, int src, int seg) {
+    return reinterpret_cast<int*>(mail + data_floats(world, tmax)) + (static_cast<size_t>(par) * world + src) * smax + seg;
+  }
 };
 
 // Per-CTA trace record (globaltimer ns): start, after the dependency wait,

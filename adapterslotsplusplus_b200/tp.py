@@ -11,9 +11,14 @@ tensor-parallel base model:
     (sum, fp32, T*r values) over the tensor-parallel group gives H on every
     rank; each rank then expands with the full B onto its replica of y.
 
-The shrink, all-reduce and expand are three launches on the caller's stream
-(libwp_b200.so: wp_add_lora_shrink, wp_tp_allreduce_f32, wp_add_lora_expand),
-so a whole step can be captured in one CUDA graph.
+By default a row-parallel layer is ONE launch (wp_add_lora_row_parallel):
+each segment's partial H is written straight into the peers' mailboxes (device
+memory mapped over NVLink through CUDA IPC), released with a flag, waited for
+(bounded) and summed in rank order inside the apply kernel, so the exchange
+overlaps the other segments' work. With fused=False it is three launches
+(wp_add_lora_shrink, wp_tp_allreduce_f32 over NCCL, wp_add_lora_expand).
+Either way everything runs on the caller's stream, so a whole step can be
+captured in one CUDA graph.
 
 The sharding helpers are pure tensor slicing and run anywhere; the apply
 methods need the CUDA engine.
@@ -66,7 +71,8 @@ class TensorParallelApply:
     runs build_seg_bounds on identical indices (the table is replicated, not
     exchanged)."""
 
-    def __init__(self, engine, rank: Optional[int] = None, world: Optional[int] = None, group=None):
+    def __init__(self, engine, rank: Optional[int] = None, world: Optional[int] = None, group=None,
+                 fused: bool = True):
         import torch.distributed as dist
 
         self.engine = engine
@@ -83,8 +89,27 @@ class TensorParallelApply:
         uid = (ctypes.c_char * nbytes).from_buffer_copy(obj[0])
         _lib.check(lib.wp_tp_init(engine.handle, uid, self.rank, self.world), engine.handle)
         self._H = torch.empty(engine.config.max_tokens * 64, dtype=torch.float32, device=engine.device)
+        self.fused = bool(fused) and self.world > 1
+        if self.fused:
+            # every rank's mailbox, mapped into every process (CUDA IPC over NVLink)
+            hb = int(lib.wp_tp_mailbox_handle_bytes())
+            mine = (ctypes.c_char * hb)()
+            _lib.check(lib.wp_tp_mailbox_create(engine.handle, self.rank, self.world, engine.config.max_tokens, mine),
+                       engine.handle)
+            got = [None] * self.world
+            dist.all_gather_object(got, bytes(mine), group=group)
+            allh = (ctypes.c_char * (hb * self.world)).from_buffer_copy(b"".join(got))
+            _lib.check(lib.wp_tp_mailbox_open(engine.handle, allh), engine.handle)
+            dist.barrier(group=group)
 
     def close(self):
+        import torch.distributed as dist
+
+        if self.fused:
+            # no rank unmaps a mailbox while a peer may still write into it
+            torch.cuda.synchronize(self.engine.device)
+            dist.barrier()
+            self._lib.wp_tp_mailbox_close(self.engine.handle)
         self._lib.wp_tp_destroy(self.engine.handle)
 
     def column_parallel(self, y_shard, x, wa_t_all, wb_shard, scale) -> bool:
@@ -96,7 +121,9 @@ class TensorParallelApply:
         return self.engine.add_lora_packed(full, x, wa_t_all, wb_shard, scale)
 
     def row_parallel(self, y, x_shard, wa_shard, wb_t_all, scale) -> bool:
-        """Partial shrink on this rank's d slice, fp32 all-reduce of H, full expand."""
+        """Partial shrink on this rank's d slice, sum of the ranks' H, full
+        expand: one launch with the peer-memory exchange (fused), else
+        shrink + NCCL all-reduce + expand."""
         eng, lib = self.engine, self._lib
         r = int(wb_t_all.size(-1))
         if not eng.rank_supported(r):
@@ -105,6 +132,14 @@ class TensorParallelApply:
         y2d = y.view(-1, y.size(-1))
         T, d = int(x2d.size(0)), int(x2d.size(1))
         dt = _lib.WP_DTYPE_BF16 if x2d.dtype == torch.bfloat16 else _lib.WP_DTYPE_F16
+        if self.fused:
+            h = eng.handle
+            stream = torch.cuda.current_stream(eng.device).cuda_stream
+            _lib.check(lib.wp_add_lora_row_parallel(
+                h, y2d.data_ptr(), x2d.data_ptr(), wa_shard.data_ptr(), wa_shard.stride(0), wb_t_all.data_ptr(),
+                wb_t_all.stride(0), int(wa_shard.size(0)), float(scale), T, d, int(wb_t_all.size(-2)), r,
+                x2d.stride(0), y2d.stride(0), 0, dt, stream), h)
+            return True
         H = self._H[:T * r].view(T, r)
         stream = torch.cuda.current_stream(eng.device).cuda_stream
         h = eng.handle
@@ -112,5 +147,5 @@ class TensorParallelApply:
                                           int(wa_shard.size(0)), float(scale), T, d, r, x2d.stride(0), dt, stream), h)
         _lib.check(lib.wp_tp_allreduce_f32(h, H.data_ptr(), T * r, stream), h)
         _lib.check(lib.wp_add_lora_expand(h, y2d.data_ptr(), H.data_ptr(), wb_t_all.data_ptr(), wb_t_all.stride(0),
-                                          T, int(wb_t_all.size(-2)), r, y2d.stride(0), 0, dt, stream), h)
+                                          int(wb_t_all.size(0)), T, int(wb_t_all.size(-2)), r, y2d.stride(0), 0, dt, stream), h)
         return True

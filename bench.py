@@ -314,7 +314,9 @@ def run_ours(args, rank, world, local_rank):
     # one launch per step). Per launch: the mean over the calls of the step on
     # one rank.
     dom = eng.last_apply_kernel() or "apply_kernel"
-    launches_per_step = LAYERS * sum(1 if (world == 1 or k == "col") else 2 for *_, k in PROJS)
+    # one apply launch per projection: row-parallel layers exchange their
+    # partial H over peer memory inside the launch
+    launches_per_step = LAYERS * len(PROJS)
     per_launch_ms = ms_apply / launches_per_step
     per_launch_b = total_b / world / launches_per_step
     achieved = per_launch_b / (per_launch_ms * 1e-3) / 1e9
@@ -354,7 +356,7 @@ def run_ours(args, rank, world, local_rank):
                      "launch_us": round(per_launch_ms * 1e3, 3)},
         "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "us/step", "h2d_bytes_per_step": int(ids.nbytes),
                 "d2h_bytes_per_step": int(out_host.numel() * 2),
-                "path": "WarpPipeEngine.build_seg_bounds + graph of the step's apply calls (tensor-parallel over NCCL when N > 1)"},
+                "path": "WarpPipeEngine.build_seg_bounds + graph of the step's apply calls (tensor-parallel when N > 1: column-parallel projections split B and y, row-parallel ones exchange the partial H over NVLink peer memory inside the apply kernel)"},
         "gpu_launches": args.steps * (1 + launches_per_step),
         "clocks": clk.summary(),
     }
@@ -598,6 +600,7 @@ def main():
 
     if world > 1:
         torch.cuda.set_device(local_rank)
+        os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout (one JSON line)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     eng, result = run_ours(args, rank, world, local_rank)
     if rank == 0 and world == 1:

@@ -226,10 +226,11 @@ int wp_add_lora_shrink(wp_handle* h, void* H, const void* x, const void* wa_base
                        int32_t num_adapters, float scale, int32_t T, int32_t d_model, int32_t rank, int64_t x_ld,
                        int32_t dtype, void* stream);
 
-/* Expand half of wp_add_lora: y[t, y_offset + j] += H[t,:] . B_i[j,:]. */
+/* Expand half of wp_add_lora: y[t, y_offset + j] += H[t,:] . B_i[j,:] for the
+ * num_adapters stacked B_i = wb_base + i*wb_stride0. */
 int wp_add_lora_expand(wp_handle* h, void* y, const void* H, const void* wb_base, int64_t wb_stride0,
-                       int32_t T, int32_t out_features, int32_t rank, int64_t y_ld, int32_t y_offset,
-                       int32_t dtype, void* stream);
+                       int32_t num_adapters, int32_t T, int32_t out_features, int32_t rank, int64_t y_ld,
+                       int32_t y_offset, int32_t dtype, void* stream);
 
 /* ---- staging slots / prefetch ------------------------------------------ */
 
@@ -285,6 +286,30 @@ int wp_tp_init(wp_handle* h, const void* id, int32_t rank, int32_t world);
  * partials [T, r]). Capturable in a CUDA graph. */
 int wp_tp_allreduce_f32(wp_handle* h, void* buf, int64_t n, void* stream);
 int wp_tp_destroy(wp_handle* h);
+
+/* Row-parallel layers over peer memory (one process per GPU, NVLink P2P):
+ * a fused alternative to wp_add_lora_shrink + wp_tp_allreduce_f32 +
+ * wp_add_lora_expand for the row-parallel LoRA layers of a tensor-parallel
+ * model (reference: single-GPU only; the sharding follows vLLM's
+ * RowParallelLinearWithLoRA). Each rank creates a mailbox (device memory
+ * for the [T, r] partials of every rank plus flags) and exports it; the
+ * caller all-gathers the handles (world x wp_tp_mailbox_handle_bytes()
+ * bytes, in rank order) and opens them. */
+int32_t wp_tp_mailbox_handle_bytes(void);
+int wp_tp_mailbox_create(wp_handle* h, int32_t rank, int32_t world, int32_t max_tokens, void* handle_out);
+int wp_tp_mailbox_open(wp_handle* h, const void* handles);
+int wp_tp_mailbox_close(wp_handle* h);
+
+/* One launch per row-parallel layer: each segment's partial H over this
+ * rank's d slice (x [T, d_shard], A stack sliced along d) is exchanged with
+ * the peers inside the kernel (stores into their mailboxes, a release flag,
+ * a bounded acquire wait), summed in rank order, and expanded with the full
+ * B onto y: y[t, y_offset + j] += (scale * sum_ranks x_p[t,:] . A_p^T) . B[j,:].
+ * Every rank calls it with the same segment table and T. */
+int wp_add_lora_row_parallel(wp_handle* h, void* y, const void* x, const void* wa_base, int64_t wa_stride0,
+                             const void* wb_base, int64_t wb_stride0, int32_t num_adapters, float scale, int32_t T,
+                             int32_t d_shard, int32_t out_features, int32_t rank, int64_t x_ld, int64_t y_ld,
+                             int32_t y_offset, int32_t dtype, void* stream);
 
 #ifdef __cplusplus
 }

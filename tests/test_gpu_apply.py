@@ -128,6 +128,35 @@ def test_sliced_output(engine, dtype):
     assert_close(y, ref, dtype, "unaligned slice")
 
 
+@pytest.mark.parametrize("dtype", DTYPES)
+def test_live_shrink_then_expand_halves(engine, dtype):
+    """wp_add_lora_shrink + wp_add_lora_expand (the halves a tensor-parallel
+    row-parallel layer runs around its all-reduce) equal add_lora, with many
+    adapters in the stack."""
+    from adapterslotsplusplus_b200 import _lib
+
+    T, d, o, r, L = 200, 4096, 1024, 32, 12
+    g = torch.Generator().manual_seed(21)
+    wa = (torch.randn(L, 1, r, d, generator=g) * 0.02).to(dtype)
+    wb = (torch.randn(L, 1, o, r, generator=g) * 0.02).to(dtype)
+    x = (torch.randn(T, d, generator=g) * 0.1).to(dtype)
+    y = (torch.randn(T, o, generator=g) * 0.1).to(dtype)
+    idx = torch.as_tensor(zipf_ids(L, T, seed=5), dtype=torch.int64)
+    ref = oa.add_lora_grouped(y, x, wa, wb, 0.75, idx)
+    assert engine.build_seg_bounds(idx.cuda())
+    lib, h = _lib.load(), engine.handle
+    dt = _lib.WP_DTYPE_BF16 if dtype == torch.bfloat16 else _lib.WP_DTYPE_F16
+    H = torch.zeros(T, r, dtype=torch.float32, device="cuda")
+    xd, wad, wbd, yd = x.cuda(), wa.cuda(), wb.cuda(), y.cuda()
+    st = torch.cuda.current_stream().cuda_stream
+    _lib.check(lib.wp_add_lora_shrink(h, H.data_ptr(), xd.data_ptr(), wad.data_ptr(), wad.stride(0), L, 0.75, T, d, r,
+                                      d, dt, st), h)
+    _lib.check(lib.wp_add_lora_expand(h, yd.data_ptr(), H.data_ptr(), wbd.data_ptr(), wbd.stride(0), L, T, o, r, o, 0,
+                                      dt, st), h)
+    torch.cuda.synchronize()
+    assert_close(yd, ref, dtype, "shrink + expand halves")
+
+
 @pytest.mark.parametrize("nslices,rank,o,dtype", [(3, 32, 4096, torch.bfloat16), (2, 32, 11008, torch.bfloat16),
                                                    (3, 16, 512, torch.float16), (2, 64, 1024, torch.bfloat16),
                                                    (2, 8, 256, torch.float16), (5, 32, 256, torch.bfloat16)])
