@@ -244,8 +244,8 @@ def run_ours(args, rank, world, local_rank):
     tpa = None
     if world > 1:
         # tensor parallel over the N GPUs: column-parallel projections expand
-        # their own output columns, row-parallel ones all-reduce the shrink
-        # partials over NCCL (libwp_b200.so's own communicator)
+        # their own output columns; row-parallel ones sum the ranks' shrink
+        # partials over NVLink peer memory inside the apply launch
         from adapterslotsplusplus_b200.tp import TensorParallelApply
 
         tpa = TensorParallelApply(eng)
