@@ -1356,6 +1356,8 @@ extern "C" int wp_add_lora_row_parallel(wp_handle* h, void* y, const void* x, co
   if (!rc) rc = check_expand_args(h, y, y_ld, y_offset, out_features, wb_base, wb_stride0);
   if (rc) return rc;
   if (T > h->mail_tmax) return fail(h, WP_ERR_INVALID, "add_lora_row_parallel: %d tokens exceed the mailbox (%d)", T, h->mail_tmax);
+  if (!al16(y) || y_ld % 8 || y_offset % 8)
+    return fail(h, WP_ERR_INVALID, "add_lora_row_parallel: y needs 16-byte aligned rows and column offset");
   DeviceGuard dg(h->device);
   h->tp_exchange = true;
   rc = do_apply(h, wp::kModeFused, 0, h->d_live, h->d_live_num, T, rank, dtype, x, x_ld, d_shard, wa_base, wa_stride0,

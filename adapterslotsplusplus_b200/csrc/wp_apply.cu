@@ -147,7 +147,7 @@ struct ApplyCfg {
   static_assert(!DEC || PW >= 4 * kSnakeMax * 4, "the partial slots hold the table-ordering scratch");
 };
 
-template <typename T, int R, bool DEC, bool TR, bool LF>
+template <typename T, int R, bool DEC, bool TR, int LF, bool TPX = false>
 __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constant__ ApplyArgs a) {
   using C = ApplyCfg<R, DEC>;
   using E = Elem<T>;
@@ -185,10 +185,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const int lane = tid & 31;
   const bool producer = warp == kProducerWarp;
   // LF: the live fused call with a tensor-map-aligned y (the serving hot
-  // path, one or several slices), compiled without the other modes' branches
+  // path), compiled without the other modes' branches; 1 = one slice,
+  // 2 = several slices (add_lora_packed_nslice)
   const bool registry = !LF && a.registry != 0;
   const bool y_tma = LF || a.y_tma != 0;
-  const int nslices = a.nslices;
+  const int nslices = LF == 1 ? 1 : a.nslices;
   const uint32_t q = cluster_ctarank();
   const uint32_t CL = cluster_nctarank();
   const int cid = static_cast<int>(cluster_id_x());
@@ -678,7 +679,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   }
   // tensor parallelism: the epoch of this launch's peer exchange (after the
   // dependency wait, so the previous launch's advance is visible)
-  const int tp_epoch = a.tp_world > 1 ? __ldcg(&a.tp_seq[0]) + 1 : 0;
+  const int tp_epoch = TPX ? __ldcg(&a.tp_seq[0]) + 1 : 0;
   const int g = lane >> 2;
   const int c = lane & 3;
   const int quarter = warp & 3;  // TMEM lane quarter this warp may read
@@ -898,7 +899,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           }
         }
         named_sync(kBarCompute, kComputeThreads);  // slots read, H complete
-        if (a.tp_world > 1 && do_ex) {
+        if (TPX && do_ex) {
           // ---- 2b. tensor-parallel exchange over peer memory: H so far is
           // this rank's slice of d. The primary cluster of the segment (its
           // rank-0 CTA) writes it into every peer's mailbox, then raises its
@@ -1333,7 +1334,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       for (int u = max(0, issued - S); u < issued; ++u) mbar_wait_bounded(&full[u % S], (u / S) & 1, nullptr, kDrainNs);
     }
   }
-  if (a.tp_world > 1) {
+  if (TPX) {
     // every wait of this CTA on the peers is over: count it; the last CTA
     // advances the epoch for the next exchange launch
     named_sync(kBarCompute, kComputeThreads);
@@ -1359,7 +1360,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
 
 namespace {
 
-template <typename T, int R, bool DEC, bool TR, bool LF>
+template <typename T, int R, bool DEC, bool TR, int LF, bool TPX = false>
 struct ApplyKernel {
   using C = ApplyCfg<R, DEC>;
   static bool prepare() {
@@ -1368,7 +1369,7 @@ struct ApplyKernel {
     cudaGetDevice(&dev);
     const uint64_t bit = 1ull << (dev & 63);
     if (done.load() & bit) return true;
-    if (cudaFuncSetAttribute(apply_kernel<T, R, DEC, TR, LF>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
+    if (cudaFuncSetAttribute(apply_kernel<T, R, DEC, TR, LF, TPX>, cudaFuncAttributeMaxDynamicSharedMemorySize, C::SMEM) !=
         cudaSuccess)
       return false;
     done.fetch_or(bit);
@@ -1392,7 +1393,7 @@ struct ApplyKernel {
     attr[1].val.programmaticStreamSerializationAllowed = 1;
     cfg.attrs = attr;
     cfg.numAttrs = lc.pdl ? 2 : 1;
-    return cudaLaunchKernelEx(&cfg, apply_kernel<T, R, DEC, TR, LF>, a);
+    return cudaLaunchKernelEx(&cfg, apply_kernel<T, R, DEC, TR, LF, TPX>, a);
   }
 
   static int max_grid(int cluster) {
@@ -1410,7 +1411,7 @@ struct ApplyKernel {
     cfg.attrs = attr;
     cfg.numAttrs = 1;
     int nclusters = 0;
-    if (cudaOccupancyMaxActiveClusters(&nclusters, apply_kernel<T, R, DEC, TR, LF>, &cfg) != cudaSuccess) {
+    if (cudaOccupancyMaxActiveClusters(&nclusters, apply_kernel<T, R, DEC, TR, LF, TPX>, &cfg) != cudaSuccess) {
       cudaGetLastError();
       return 0;
     }
@@ -1420,13 +1421,20 @@ struct ApplyKernel {
 
 template <typename T, int R>
 cudaError_t apply_variant(const ApplyArgs& a, const LaunchCfg& lc) {
-  const bool live_fused = a.mode == kModeFused && !a.registry && a.y_tma;
-  if (a.trace) {
-    if (lc.dec && live_fused) return ApplyKernel<T, R, true, true, true>::launch(a, lc);
-    return lc.dec ? ApplyKernel<T, R, true, true, false>::launch(a, lc) : ApplyKernel<T, R, false, true, false>::launch(a, lc);
+  const bool live_fused = lc.dec && a.mode == kModeFused && !a.registry && a.y_tma;
+  const int lf = live_fused ? (a.nslices > 1 ? 2 : 1) : 0;
+  if (a.tp_world > 1) {
+    // row-parallel exchange over peer memory (untraced): live fused single-slice calls on the decode variant
+    if (lf != 1) return cudaErrorInvalidValue;
+    return ApplyKernel<T, R, true, false, 1, true>::launch(a, lc);
   }
-  if (lc.dec && live_fused) return ApplyKernel<T, R, true, false, true>::launch(a, lc);
-  return lc.dec ? ApplyKernel<T, R, true, false, false>::launch(a, lc) : ApplyKernel<T, R, false, false, false>::launch(a, lc);
+  if (a.trace) {
+    if (lf == 1) return ApplyKernel<T, R, true, true, 1>::launch(a, lc);
+    return lc.dec ? ApplyKernel<T, R, true, true, 0>::launch(a, lc) : ApplyKernel<T, R, false, true, 0>::launch(a, lc);
+  }
+  if (lf == 1) return ApplyKernel<T, R, true, false, 1>::launch(a, lc);
+  if (lf == 2) return ApplyKernel<T, R, true, false, 2>::launch(a, lc);
+  return lc.dec ? ApplyKernel<T, R, true, false, 0>::launch(a, lc) : ApplyKernel<T, R, false, false, 0>::launch(a, lc);
 }
 
 template <typename T>
@@ -1443,10 +1451,10 @@ cudaError_t apply_by_rank(int rank, const ApplyArgs& a, const LaunchCfg& lc) {
 template <typename T>
 int max_grid_by_rank(int rank, int cluster, bool dec) {
   switch (rank) {
-    case 8: return dec ? ApplyKernel<T, 8, true, false, false>::max_grid(cluster) : ApplyKernel<T, 8, false, false, false>::max_grid(cluster);
-    case 16: return dec ? ApplyKernel<T, 16, true, false, false>::max_grid(cluster) : ApplyKernel<T, 16, false, false, false>::max_grid(cluster);
-    case 32: return dec ? ApplyKernel<T, 32, true, false, false>::max_grid(cluster) : ApplyKernel<T, 32, false, false, false>::max_grid(cluster);
-    case 64: return dec ? ApplyKernel<T, 64, true, false, false>::max_grid(cluster) : ApplyKernel<T, 64, false, false, false>::max_grid(cluster);
+    case 8: return dec ? ApplyKernel<T, 8, true, false, 0>::max_grid(cluster) : ApplyKernel<T, 8, false, false, 0>::max_grid(cluster);
+    case 16: return dec ? ApplyKernel<T, 16, true, false, 0>::max_grid(cluster) : ApplyKernel<T, 16, false, false, 0>::max_grid(cluster);
+    case 32: return dec ? ApplyKernel<T, 32, true, false, 0>::max_grid(cluster) : ApplyKernel<T, 32, false, false, 0>::max_grid(cluster);
+    case 64: return dec ? ApplyKernel<T, 64, true, false, 0>::max_grid(cluster) : ApplyKernel<T, 64, false, false, 0>::max_grid(cluster);
     default: return 0;
   }
 }
