@@ -253,6 +253,43 @@ class WarpPipeEngine:
                 int(x2d.stride(0)), int(y2d.stride(0)), dt, _stream_ptr(x.device)))
         return True
 
+    def add_lora_shrink(self, H, x, wa_t_all, scale) -> bool:
+        """Shrink half of add_lora: H[t] = scale * x[t] . A_id(t)^T (fp32 H
+        [T, rank]) for the rows of the live segments; other rows are left as
+        they are."""
+        rank = int(wa_t_all.size(-2))
+        if not self.rank_supported(rank):
+            return False
+        dt = _dtype_code(x, "add_lora_shrink: x")
+        x2d = x.reshape(-1, x.size(-1))
+        if H.dtype != torch.float32 or not H.is_contiguous() or tuple(H.shape) != (x2d.size(0), rank):
+            raise RuntimeError("add_lora_shrink: H must be contiguous fp32 [T, rank]")
+        if wa_t_all.dtype != x.dtype or not wa_t_all.is_contiguous():
+            raise RuntimeError("add_lora_shrink: wa_t_all must be contiguous, of x's dtype")
+        self._check(self._lib.wp_add_lora_shrink(
+            self._h, H.data_ptr(), x2d.data_ptr(), wa_t_all.data_ptr(), int(wa_t_all.stride(0)),
+            int(wa_t_all.size(0)), float(scale), int(x2d.size(0)), int(x2d.size(1)), rank, int(x2d.stride(0)), dt,
+            _stream_ptr(x.device)))
+        return True
+
+    def add_lora_expand(self, y, H, wb_t_all, y_offset: int = 0) -> bool:
+        """Expand half of add_lora: y[t, y_offset + j] += H[t] . B_id(t)[j] for
+        the rows of the live segments (H fp32 [T, rank])."""
+        rank = int(wb_t_all.size(-1))
+        if not self.rank_supported(rank):
+            return False
+        dt = _dtype_code(y, "add_lora_expand: y")
+        y2d = y.view(-1, y.size(-1))
+        if H.dtype != torch.float32 or not H.is_contiguous() or tuple(H.shape) != (y2d.size(0), rank):
+            raise RuntimeError("add_lora_expand: H must be contiguous fp32 [T, rank]")
+        if wb_t_all.dtype != y.dtype or not wb_t_all.is_contiguous():
+            raise RuntimeError("add_lora_expand: wb_t_all must be contiguous, of y's dtype")
+        self._check(self._lib.wp_add_lora_expand(
+            self._h, y2d.data_ptr(), H.data_ptr(), wb_t_all.data_ptr(), int(wb_t_all.stride(0)),
+            int(wb_t_all.size(0)), int(y2d.size(0)), int(wb_t_all.size(-2)), rank, int(y2d.stride(0)),
+            int(y_offset), dt, _stream_ptr(y.device)))
+        return True
+
     def add_lora_strided(self, y_view, x, wa_t_all, wb_t_all, scale) -> bool:
         """add_lora onto a column view of a wider row-major y (e.g. a
         tensor-parallel output shard): the view's row stride is used as is."""
