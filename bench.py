@@ -15,8 +15,14 @@ implies against the measured peak. One JSON line on rank 0.
 With N > 1 (launched under torch.distributed.run, one rank per GPU) the same
 step runs tensor-parallel over the N GPUs: column-parallel projections (q, k,
 v, gate, up) expand their own out_features slice, row-parallel ones (o, down)
-shrink their d_in slice and all-reduce the fp32 [T, r] partials over NCCL
-(strong scaling; the time is the max over ranks).
+shrink their d_in slice and sum the ranks' fp32 [T, r] partials over NVLink
+peer memory inside the apply launch (strong scaling; the time is the max over
+ranks).
+
+  python bench.py --config3 [--gpus N]
+
+times BASELINE config 3 (13B shapes, rank 64, 512 tokens, 128 resident),
+tensor-parallel over the N GPUs, and prints its own JSON line.
 
   python bench.py --profile-case q|gate|down [--launches 12] [--kernel auto|cluster|split|tc]
 
@@ -539,6 +545,89 @@ def prefill_mix(device, kernels=("cluster", "split", "tc"), iters=10):
             "algorithmic_mb": round((sb + eb) / 1e6, 1), "per_kernel": out}
 
 
+def config3(args, rank, world, local_rank):
+    """a Llama-2-13B-shaped stack (40 layers, hidden 5120,
+    intermediate 13824), rank 64, bf16, 128 resident adapters, 512 tokens,
+    Zipf(1.1), tensor-parallel over the N GPUs (column-parallel q/k/v/gate/up,
+    row-parallel o/down with the peer-memory exchange). Four distinct layer
+    weight sets (6.4 GB per GPU at N = 1, far larger than L2) are cycled over
+    the 40 layers, so every launch streams its weights from HBM. One JSON
+    line on rank 0: us per step (max over ranks) and the per-GPU HBM GB/s."""
+    from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
+
+    layers, hid, inter, r, resident, T = 40, 5120, 13824, 64, 128, 512
+    projs = [("q", hid, hid, "h", "col"), ("k", hid, hid, "h", "col"), ("v", hid, hid, "h", "col"),
+             ("o", hid, hid, "attn", "row"), ("gate", hid, inter, "h", "col"), ("up", hid, inter, "h", "col"),
+             ("down", inter, hid, "inter", "row")]
+    device = torch.device("cuda", local_rank)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    g = torch.Generator(device=device).manual_seed(3 + 1000 * rank)
+    sets = []
+    for _ in range(4):
+        L = {}
+        for name, d, o, _, kind in projs:
+            dl = d // world if (world > 1 and kind == "row") else d
+            ol = o // world if (world > 1 and kind == "col") else o
+            L[name] = (torch.randn(resident, 1, r, dl, device=device, dtype=torch.bfloat16, generator=g) * 0.02,
+                       torch.randn(resident, 1, ol, r, device=device, dtype=torch.bfloat16, generator=g) * 0.02,
+                       torch.zeros(T, ol, device=device, dtype=torch.bfloat16))
+        sets.append(L)
+    xs = {"h": torch.randn(T, hid, device=device, dtype=torch.bfloat16, generator=g) * 0.1,
+          "attn": torch.randn(T, hid // world, device=device, dtype=torch.bfloat16, generator=g) * 0.1,
+          "inter": torch.randn(T, inter // world, device=device, dtype=torch.bfloat16, generator=g) * 0.1}
+    ids = zipf_ids(resident, T, seed=SEED)
+    U = int(np.unique(ids).size)
+    eng.build_seg_bounds(torch.as_tensor(ids, device=device))
+    tpa = None
+    if world > 1:
+        from adapterslotsplusplus_b200.tp import TensorParallelApply
+
+        tpa = TensorParallelApply(eng)
+    scale = 1.0
+
+    def step():
+        for li in range(layers):
+            L = sets[li % 4]
+            for name, d, o, src, kind in projs:
+                wa, wb, y = L[name]
+                if tpa is None:
+                    eng.add_lora_packed(y, xs[src], wa, wb, scale)
+                elif kind == "col":
+                    tpa.column_parallel(y, xs[src], wa, wb, scale)
+                else:
+                    tpa.row_parallel(y, xs[src], wa, wb, scale)
+
+    gr = capture(step)
+    for _ in range(max(3, args.warmup)):
+        gr.replay()
+    torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
+    ms = time_graph(gr, None, args.steps)
+    if world > 1:
+        t = torch.tensor([ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        ms = float(t.item())
+    per_gpu = 0
+    for name, d, o, src, kind in projs:
+        dl = d // world if (world > 1 and kind == "row") else d
+        ol = o // world if (world > 1 and kind == "col") else o
+        sb, eb = algorithmic_bytes(U, T, dl, ol, r)
+        per_gpu += sb + eb
+    per_gpu *= layers
+    peaks = measured_peaks()
+    hbm = peaks.get("hbm_gbs") or 6650.0
+    del gr
+    if tpa is not None:
+        tpa.close()
+    return {"config": "3 (llama2-13b: 40 layers, r64, bf16, 128 resident, 512 tokens, Zipf(1.1))",
+            "n_gpus": world, "parallelism": f"tp{world}" if world > 1 else "single",
+            "us_per_step": round(ms * 1e3, 1), "launches_per_step": layers * len(projs),
+            "active_adapters": U, "bytes_per_gpu_per_step": int(per_gpu),
+            "gbs_per_gpu": round(per_gpu / (ms * 1e-3) / 1e9, 1),
+            "frac_of_hbm": round(per_gpu / (ms * 1e-3) / 1e9 / hbm, 4)}
+
+
 def profile_case(args):
     """A few launches of one projection of the workload, for profilers: the
     decode-step call shape (T = 256, Zipf routing over 64 resident adapters,
@@ -579,6 +668,8 @@ def main():
     ap.add_argument("--kernel", choices=["auto", "cluster", "split", "tc"], default="auto",
                     help="apply kernel of --profile-case")
     ap.add_argument("--prefill-mix", action="store_true", help="time config 2's prefill mix per kernel and exit")
+    ap.add_argument("--config3", action="store_true",
+                    help="time BASELINE config 3 (13B, r64, T=512, tensor-parallel over the N GPUs) and exit")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args)
@@ -598,6 +689,18 @@ def main():
             print(json.dumps(res), flush=True)
         return
 
+    if args.config3:
+        if world > 1:
+            torch.cuda.set_device(local_rank)
+            os.environ.setdefault("NCCL_DEBUG", "WARN")
+            torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
+        res = config3(args, rank, world, local_rank)
+        if world > 1:
+            torch.distributed.barrier()
+            torch.distributed.destroy_process_group()
+        if rank == 0:
+            print(json.dumps(res), flush=True)
+        return
     if world > 1:
         torch.cuda.set_device(local_rank)
         os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout (one JSON line)
