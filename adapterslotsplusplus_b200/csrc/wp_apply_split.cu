@@ -143,6 +143,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_kernel(const __grid_consta
   uint64_t* hread = reinterpret_cast<uint64_t*>(smem + 192);  // [2] compute warps read a run's partials
   volatile int* s_bad = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS);
   volatile int* s_issued = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS + 4);
+  volatile int* s_armed = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS + 8);  // stages armed by the producer
   int4* sdesc = reinterpret_cast<int4*>(smem + C::OFF_DESC);  // [2 lists][kSDesc][2]
   float* Pw = reinterpret_cast<float*>(smem + C::OFF_PW);
   float* Hsl = reinterpret_cast<float*>(smem + C::OFF_H);  // [32][R]: H of the current expand run
@@ -166,6 +167,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_kernel(const __grid_consta
     for (int b = 0; b < 2; ++b) mbar_init(&hread[b], 1);
     *s_bad = 0;
     *s_issued = 0;
+    *s_armed = 0;
     fence_mbar_init();
   }
   if (warp == kSProducer && lane == 0) {
@@ -228,84 +230,85 @@ __global__ void __launch_bounds__(kSThreads, 1) split_kernel(const __grid_consta
   auto y_by_tma = [&](int n) -> bool { return a.y_tma && a.o_sliced && (n == 8 || n == 16 || n == 32); };
   int* done = a.sync;
 
+  // TMA issue of stage-unit (sh, s, c) into `stage`; parts: 1 = arm the
+  // stage and load the weights (ef: their L2 evict-first policy), 2 = the
+  // activations
+  auto issue = [&](bool sh, int s, int c, int stage, int parts, uint64_t ef) {
+    const DevSeg g = desc(sh ? 0 : 1, s);
+    const int n = clamp_rows(g.token_count);
+    const int bi = box_index(n);
+    const uint32_t box_bytes = (8u << bi) * 128u;  // one 64-column slice of x or y
+    uint8_t* st = stage_base + stage * C::STAGE;
+    uint64_t* bar = &full[stage];
+    if (sh) {
+      const int k0 = c * kStageK;
+      if (parts & 1) {
+        mbar_arrive_expect_tx(bar, 4 * C::ABOX + 4 * box_bytes);
+        if (a.d_sliced) {
+          tma_load_4d_ef(st, &a.tmap_a, 0, 0, k0 / kBoxCols, g.adapter_id, bar, ef);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_3d_ef(st + j * C::ABOX, &a.tmap_a, k0 + j * kBoxCols, 0, g.adapter_id, bar, ef);
+        }
+      }
+      if (parts & 2) {
+        if (a.d_sliced) {
+          tma_load_3d(st + 4 * C::ABOX, &a.tmap_x[bi], 0, g.token_start, k0 / kBoxCols, bar);
+        } else {
+#pragma unroll
+          for (int j = 0; j < 4; ++j)
+            tma_load_2d(st + 4 * C::ABOX + j * box_bytes, &a.tmap_x[bi], k0 + j * kBoxCols, g.token_start, bar);
+        }
+      }
+    } else {
+      const int oc = c * kStageCols;
+      const int wc = min(kStageCols, a.o - oc);
+      if (parts & 1) {
+        if constexpr (R >= 16) {
+          mbar_arrive_expect_tx(bar, 256 * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
+          tma_load_3d_ef(st + 4 * C::XBOX, &a.tmap_b, 0, oc, g.adapter_id, bar, ef);
+        } else {
+          mbar_arrive_expect_tx(bar, wc * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
+          const T* B = static_cast<const T*>(a.wb_base) + static_cast<int64_t>(g.adapter_id) * a.wb_stride;
+          bulk_g2s(st + 4 * C::XBOX, B + static_cast<int64_t>(oc) * R, wc * R * 2, bar);
+        }
+      }
+      if (parts & 2) {
+        if (a.y_tma) {
+          if (a.o_sliced) {
+            tma_load_3d(st, &a.tmap_y[bi], 0, g.token_start, oc / kBoxCols, bar);
+          } else {
+#pragma unroll
+            for (int j = 0; j < 4; ++j)
+              tma_load_2d(st + j * box_bytes, &a.tmap_y[bi], oc + j * kBoxCols, g.token_start, bar);
+          }
+        }
+      }
+    }
+  };
+  const int first = min(S, U);  // stages issued before any is consumed
   if (warp == kSProducer) {
     // =========================== producer ====================================
     if (lane == 0) {
       const uint64_t ef = l2_evict_first_policy();
-      // parts: 1 = arm the stage and load the weights, 2 = the activations
-      auto issue = [&](bool sh, int s, int c, int stage, int parts) {
-        const DevSeg g = desc(sh ? 0 : 1, s);
-        const int n = clamp_rows(g.token_count);
-        const int bi = box_index(n);
-        const uint32_t box_bytes = (8u << bi) * 128u;  // one 64-column slice of x or y
-        uint8_t* st = stage_base + stage * C::STAGE;
-        uint64_t* bar = &full[stage];
-        if (sh) {
-          const int k0 = c * kStageK;
-          if (parts & 1) {
-            mbar_arrive_expect_tx(bar, 4 * C::ABOX + 4 * box_bytes);
-            if (a.d_sliced) {
-              tma_load_4d_ef(st, &a.tmap_a, 0, 0, k0 / kBoxCols, g.adapter_id, bar, ef);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                tma_load_3d_ef(st + j * C::ABOX, &a.tmap_a, k0 + j * kBoxCols, 0, g.adapter_id, bar, ef);
-            }
-          }
-          if (parts & 2) {
-            if (a.d_sliced) {
-              tma_load_3d(st + 4 * C::ABOX, &a.tmap_x[bi], 0, g.token_start, k0 / kBoxCols, bar);
-            } else {
-#pragma unroll
-              for (int j = 0; j < 4; ++j)
-                tma_load_2d(st + 4 * C::ABOX + j * box_bytes, &a.tmap_x[bi], k0 + j * kBoxCols, g.token_start, bar);
-            }
-          }
-        } else {
-          const int oc = c * kStageCols;
-          const int wc = min(kStageCols, a.o - oc);
-          if (parts & 1) {
-            if constexpr (R >= 16) {
-              mbar_arrive_expect_tx(bar, 256 * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
-              tma_load_3d_ef(st + 4 * C::XBOX, &a.tmap_b, 0, oc, g.adapter_id, bar, ef);
-            } else {
-              mbar_arrive_expect_tx(bar, wc * R * 2 + (a.y_tma ? 4 * box_bytes : 0u));
-              const T* B = static_cast<const T*>(a.wb_base) + static_cast<int64_t>(g.adapter_id) * a.wb_stride;
-              bulk_g2s(st + 4 * C::XBOX, B + static_cast<int64_t>(oc) * R, wc * R * 2, bar);
-            }
-          }
-          if (parts & 2) {
-            if (a.y_tma) {
-              if (a.o_sliced) {
-                tma_load_3d(st, &a.tmap_y[bi], 0, g.token_start, oc / kBoxCols, bar);
-              } else {
-#pragma unroll
-                for (int j = 0; j < 4; ++j)
-                  tma_load_2d(st + j * box_bytes, &a.tmap_y[bi], oc + j * kBoxCols, g.token_start, bar);
-              }
-            }
-          }
-        }
-      };
-      const int first = min(S, U);
       if (a.prefetch_weights) {
+        // the store thread loads these stages' activations as soon as the
+        // dependency wait ends, while this thread still issues weights
         for (int u = 0; u < first; ++u) {
           int s, c;
           const bool sh = unit(u, s, c);
-          issue(sh, s, c, u, 1);
+          issue(sh, s, c, u, 1, ef);
+          __threadfence_block();
+          *s_armed = u + 1;
         }
         pdl_wait_prior();
         pdl_launch_dependents();
-        for (int u = 0; u < first; ++u) {
-          int s, c;
-          const bool sh = unit(u, s, c);
-          issue(sh, s, c, u, 2);
-        }
       } else {
         for (int u = 0; u < first; ++u) {
           int s, c;
           const bool sh = unit(u, s, c);
-          issue(sh, s, c, u, 3);
+          issue(sh, s, c, u, 3, ef);
         }
       }
       *s_issued = first;
@@ -316,7 +319,7 @@ __global__ void __launch_bounds__(kSThreads, 1) split_kernel(const __grid_consta
         const int stage = u % S;
         if (!mbar_wait_bounded(&empty[stage], ((u / S) - 1) & 1, a.err)) *s_bad = 1;
         if (*s_bad) break;
-        issue(sh, s, c, stage, 3);
+        issue(sh, s, c, stage, 3, ef);
         *s_issued = u + 1;
         // next unit
         if (u + 1 == nS) {
@@ -369,6 +372,24 @@ __global__ void __launch_bounds__(kSThreads, 1) split_kernel(const __grid_consta
       pdl_launch_dependents();
     }
     if (lane != 0) return;
+    if (a.prefetch_weights) {
+      // the first stages' activations, as soon as the dependency is met
+      for (int u = 0; u < first; ++u) {
+        bool armed = *s_armed > u;
+        for (int spin = 0; !armed && spin < (1 << 22); ++spin) {
+          __nanosleep(32);
+          armed = *s_armed > u;
+        }
+        if (!armed) {
+          *s_bad = 1;
+          if (a.err) atomicOr(a.err, kErrWaitTimeout);
+          break;
+        }
+        int s2, c2;
+        const bool sh2 = unit(u, s2, c2);
+        issue(sh2, s2, c2, u, 2, 0ull);
+      }
+    }
     uint32_t ypar = 0u;
     int s = s_ex0, c = c_ex0;
     DevSeg g = desc(1, s);
