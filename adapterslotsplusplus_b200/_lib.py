@@ -44,6 +44,7 @@ class WpConfig(ctypes.Structure):
         ("use_pdl", ctypes.c_int32),
         ("prefetch_weights", ctypes.c_int32),
         ("kernel", ctypes.c_int32),
+        ("peer_wait_ms", ctypes.c_int32),
     ]
 
 

@@ -64,14 +64,20 @@ def build(force: bool = False, verbose: bool = False) -> Path:
     objdir.mkdir(exist_ok=True)
     common = [nvcc, *ARCH, "-O3", "-lineinfo", "-std=c++17", "-Xcompiler", "-fPIC", "-I", str(INCLUDE), "-I", inc,
               *os.environ.get("WP_NVCC_EXTRA", "").split()]
+    from concurrent.futures import ThreadPoolExecutor
+
+    cmds = []
     objs = []
     for src in SOURCES:
         obj = objdir / (Path(src).stem + ".o")
-        cmd = [*common, "-c", str(CSRC / src), "-o", str(obj)]
-        if verbose:
-            print(" ".join(cmd), file=sys.stderr)
-        subprocess.run(cmd, check=True)
+        cmds.append([*common, "-c", str(CSRC / src), "-o", str(obj)])
         objs.append(str(obj))
+        if verbose:
+            print(" ".join(cmds[-1]), file=sys.stderr)
+    # the sources compile independently: one nvcc per source, in parallel
+    with ThreadPoolExecutor(max_workers=len(cmds)) as pool:
+        for f in [pool.submit(subprocess.run, c, check=True) for c in cmds]:
+            f.result()
     ncclso = Path(libdir) / "libnccl.so.2"
     link = [
         nvcc, *ARCH, "-shared", "-o", str(LIB_PATH) + ".tmp", *objs,

@@ -31,3 +31,6 @@ class WarpPipeConfig:
     # mma.sync), "split" (balanced: one CTA per SM, equal one-stage items),
     # "tc" (clustered, tcgen05)
     kernel: str = "auto"
+    # bound of each in-kernel wait on a tensor-parallel peer (the fused
+    # row-parallel exchange), in ms; 0 = 5000
+    peer_wait_ms: int = 0

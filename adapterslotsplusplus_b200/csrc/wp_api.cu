@@ -66,10 +66,13 @@ struct wp_handle {
   // registry table (build_segments): unsplit host copy + split device copy
   DevSeg* d_reg = nullptr;
   int* d_reg_num = nullptr;
-  DevSeg* h_reg_stage = nullptr;  // pinned upload buffer (cap + 1 entries, count in the tail)
+  // pinned upload buffers, double-buffered so that a build_segments call
+  // waits only for the upload two calls back (cap + 1 entries, count in the tail)
+  DevSeg* h_reg_stage[2] = {nullptr, nullptr};
   CUtensorMap* d_reg_maps = nullptr;  // TMA descriptors of the registry table's A matrices
-  CUtensorMap* h_reg_maps = nullptr;  // pinned upload buffer of the descriptors
-  cudaEvent_t reg_uploaded = nullptr;
+  CUtensorMap* h_reg_maps[2] = {nullptr, nullptr};  // pinned upload buffers of the descriptors
+  cudaEvent_t reg_uploaded[2] = {nullptr, nullptr};
+  int reg_buf = 0;  // upload buffer of the next build_segments call
   std::vector<wp_segment> reg_table;
   std::vector<DevSeg> reg_pieces;
   int reg_rank = 0;
@@ -84,6 +87,7 @@ struct wp_handle {
   int* d_rflag = nullptr;  // per shrink item publication flags (zero between launches)
   size_t rflag_bytes = 0;
   int* d_sync = nullptr;  // 3 x cap ints, zero between launches
+  std::vector<void*> retired;  // outgrown split buffers, freed by wp_destroy (graphs may hold them)
   // segment count of the latest build_seg_bounds, copied to pinned memory
   // without a sync; a hint for the automatic kernel choice
   int* h_nseg = nullptr;
@@ -356,11 +360,13 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
   if ((e = cudaMalloc(&h->d_run_starts, sizeof(int) * cap)) != cudaSuccess) return bail("run starts", e);
   if ((e = cudaMalloc(&h->d_reg, sizeof(DevSeg) * (cap + 1))) != cudaSuccess) return bail("registry table", e);
   if ((e = cudaMalloc(&h->d_reg_num, sizeof(int) * 4)) != cudaSuccess) return bail("registry count", e);
-  if ((e = cudaHostAlloc(&h->h_reg_stage, sizeof(DevSeg) * (cap + 1), cudaHostAllocDefault)) != cudaSuccess)
-    return bail("registry upload buffer", e);
+  for (int b = 0; b < 2; ++b)
+    if ((e = cudaHostAlloc(&h->h_reg_stage[b], sizeof(DevSeg) * (cap + 1), cudaHostAllocDefault)) != cudaSuccess)
+      return bail("registry upload buffer", e);
   if ((e = cudaMalloc(&h->d_reg_maps, sizeof(CUtensorMap) * cap)) != cudaSuccess) return bail("registry maps", e);
-  if ((e = cudaHostAlloc(&h->h_reg_maps, sizeof(CUtensorMap) * cap, cudaHostAllocDefault)) != cudaSuccess)
-    return bail("registry map upload buffer", e);
+  for (int b = 0; b < 2; ++b)
+    if ((e = cudaHostAlloc(&h->h_reg_maps[b], sizeof(CUtensorMap) * cap, cudaHostAllocDefault)) != cudaSuccess)
+      return bail("registry map upload buffer", e);
   if ((e = cudaMalloc(&h->d_err, sizeof(int) * 4)) != cudaSuccess) return bail("error word", e);
   if ((e = cudaMalloc(&h->d_sync, sizeof(int) * 3 * cap)) != cudaSuccess) return bail("segment counters", e);
   if ((e = cudaHostAlloc(&h->h_nseg, sizeof(int) * 4, cudaHostAllocDefault)) != cudaSuccess)
@@ -375,7 +381,7 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
   cudaMemset(h->d_err, 0, sizeof(int) * 4);
   if ((e = cudaStreamCreateWithFlags(&h->prefetch_stream, cudaStreamNonBlocking)) != cudaSuccess)
     return bail("prefetch stream", e);
-  cudaEventCreateWithFlags(&h->reg_uploaded, cudaEventDisableTiming);
+  for (int b = 0; b < 2; ++b) cudaEventCreateWithFlags(&h->reg_uploaded[b], cudaEventDisableTiming);
   cudaEventCreateWithFlags(&h->caller_ready, cudaEventDisableTiming);
   cudaEventCreateWithFlags(&h->registry_done, cudaEventDisableTiming);
   if (cfg.num_staging_slots > 0) {
@@ -405,20 +411,24 @@ int wp_destroy(wp_handle* h) {
   cudaFree(h->d_run_starts);
   cudaFree(h->d_reg);
   cudaFree(h->d_reg_num);
-  if (h->h_reg_stage) cudaFreeHost(h->h_reg_stage);
+  for (int b = 0; b < 2; ++b)
+    if (h->h_reg_stage[b]) cudaFreeHost(h->h_reg_stage[b]);
   cudaFree(h->d_reg_maps);
-  if (h->h_reg_maps) cudaFreeHost(h->h_reg_maps);
+  for (int b = 0; b < 2; ++b)
+    if (h->h_reg_maps[b]) cudaFreeHost(h->h_reg_maps[b]);
   cudaFree(h->d_trace[0]);
   cudaFree(h->d_trace[1]);
   cudaFree(h->d_err);
   cudaFree(h->d_part);
   cudaFree(h->d_hsplit);
   cudaFree(h->d_rflag);
+  for (void* p : h->retired) cudaFree(p);
   cudaFree(h->d_sync);
   cudaFree(h->d_plan);
   if (h->h_nseg) cudaFreeHost(h->h_nseg);
   if (h->nseg_ready) cudaEventDestroy(h->nseg_ready);
-  if (h->reg_uploaded) cudaEventDestroy(h->reg_uploaded);
+  for (int b = 0; b < 2; ++b)
+    if (h->reg_uploaded[b]) cudaEventDestroy(h->reg_uploaded[b]);
   if (h->caller_ready) cudaEventDestroy(h->caller_ready);
   if (h->registry_done) cudaEventDestroy(h->registry_done);
   if (h->prefetch_stream) cudaStreamDestroy(h->prefetch_stream);
@@ -686,20 +696,24 @@ int wp_build_segments(wp_handle* h, const int32_t* ids, const int32_t* offs, int
     return fail(h, WP_ERR_CAPACITY, "build_segments: %zu pieces exceed the table capacity", pieces.size());
   for (int si : wait_slots) WP_CUDA(h, cudaStreamWaitEvent(stream, h->slots[si].ready, 0));
 
-  // upload through the pinned buffer (the previous upload must have left it)
-  WP_CUDA(h, cudaEventSynchronize(h->reg_uploaded));
+  // upload through one of the two pinned buffers; the host waits only until
+  // the upload that used it two calls back has left it
+  const int ub = h->reg_buf;
+  h->reg_buf ^= 1;
+  WP_CUDA(h, cudaEventSynchronize(h->reg_uploaded[ub]));
+  DevSeg* stage = h->h_reg_stage[ub];
   const int np = static_cast<int>(pieces.size());
-  if (np) std::memcpy(h->h_reg_stage, pieces.data(), sizeof(DevSeg) * np);
-  int* cnt = reinterpret_cast<int*>(h->h_reg_stage + h->cfg.max_tokens);
+  if (np) std::memcpy(stage, pieces.data(), sizeof(DevSeg) * np);
+  int* cnt = reinterpret_cast<int*>(stage + h->cfg.max_tokens);
   *cnt = np;
-  if (np) WP_CUDA(h, cudaMemcpyAsync(h->d_reg, h->h_reg_stage, sizeof(DevSeg) * np, cudaMemcpyHostToDevice, stream));
+  if (np) WP_CUDA(h, cudaMemcpyAsync(h->d_reg, stage, sizeof(DevSeg) * np, cudaMemcpyHostToDevice, stream));
   if (!maps.empty()) {
-    std::memcpy(h->h_reg_maps, maps.data(), sizeof(CUtensorMap) * maps.size());
-    WP_CUDA(h, cudaMemcpyAsync(h->d_reg_maps, h->h_reg_maps, sizeof(CUtensorMap) * maps.size(),
+    std::memcpy(h->h_reg_maps[ub], maps.data(), sizeof(CUtensorMap) * maps.size());
+    WP_CUDA(h, cudaMemcpyAsync(h->d_reg_maps, h->h_reg_maps[ub], sizeof(CUtensorMap) * maps.size(),
                                cudaMemcpyHostToDevice, stream));
   }
   WP_CUDA(h, cudaMemcpyAsync(h->d_reg_num, cnt, sizeof(int), cudaMemcpyHostToDevice, stream));
-  WP_CUDA(h, cudaEventRecord(h->reg_uploaded, stream));
+  WP_CUDA(h, cudaEventRecord(h->reg_uploaded[ub], stream));
   h->reg_table.swap(table);
   h->reg_pieces.swap(pieces);
   h->reg_rank = rank;
@@ -875,9 +889,29 @@ bool auto_split(wp_handle* h, cudaStream_t stream, int T, int64_t num_adapters, 
 bool use_decode_kernel(const wp_handle* h) { return kernel_choice(h) != 2; }
 
 // Makes the split kernel's buffers hold T tokens of nchunk partials of rank r.
-// Outside stream capture they grow as needed; under capture (no allocation
-// allowed) a call that does not fit returns false and runs the clustered
-// kernel instead.
+// Outside stream capture they grow as needed (at least doubling); under
+// capture (no allocation allowed) a call that does not fit returns false and
+// runs the clustered kernel instead. A buffer that is outgrown is never freed
+// before wp_destroy: a CUDA graph captured earlier keeps its address in its
+// kernel arguments and may still be replayed.
+bool grow_buffer(wp_handle* h, void** buf, size_t* have, size_t need, bool zero, cudaStream_t stream) {
+  if (need <= *have) return true;
+  const size_t want = std::max(need, *have * 2);
+  void* p = nullptr;
+  if (cudaMalloc(&p, want) != cudaSuccess) {
+    cudaGetLastError();
+    return false;
+  }
+  if (zero && cudaMemsetAsync(p, 0, want, stream) != cudaSuccess) {
+    cudaFree(p);
+    return false;
+  }
+  if (*buf) h->retired.push_back(*buf);
+  *buf = p;
+  *have = want;
+  return true;
+}
+
 bool split_buffers(wp_handle* h, int T, int nchunk, int r, cudaStream_t stream) {
   const size_t part = static_cast<size_t>(T) * nchunk * r * 4;
   const size_t hs = static_cast<size_t>(T) * r * 4;
@@ -885,32 +919,9 @@ bool split_buffers(wp_handle* h, int T, int nchunk, int r, cudaStream_t stream) 
   if (part <= h->part_bytes && hs <= h->hsplit_bytes && rf <= h->rflag_bytes) return true;
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (cudaStreamIsCapturing(stream, &cs) != cudaSuccess || cs != cudaStreamCaptureStatusNone) return false;
-  if (part > h->part_bytes) {
-    cudaStreamSynchronize(stream);
-    cudaFree(h->d_part);
-    h->d_part = nullptr;
-    h->part_bytes = 0;
-    if (cudaMalloc(&h->d_part, part) != cudaSuccess) return false;
-    h->part_bytes = part;
-  }
-  if (hs > h->hsplit_bytes) {
-    cudaStreamSynchronize(stream);
-    cudaFree(h->d_hsplit);
-    h->d_hsplit = nullptr;
-    h->hsplit_bytes = 0;
-    if (cudaMalloc(&h->d_hsplit, hs) != cudaSuccess) return false;
-    h->hsplit_bytes = hs;
-  }
-  if (rf > h->rflag_bytes) {
-    cudaStreamSynchronize(stream);
-    cudaFree(h->d_rflag);
-    h->d_rflag = nullptr;
-    h->rflag_bytes = 0;
-    if (cudaMalloc(&h->d_rflag, rf) != cudaSuccess) return false;
-    if (cudaMemsetAsync(h->d_rflag, 0, rf, stream) != cudaSuccess) return false;
-    h->rflag_bytes = rf;
-  }
-  return true;
+  return grow_buffer(h, reinterpret_cast<void**>(&h->d_part), &h->part_bytes, part, false, stream) &&
+         grow_buffer(h, reinterpret_cast<void**>(&h->d_hsplit), &h->hsplit_bytes, hs, false, stream) &&
+         grow_buffer(h, reinterpret_cast<void**>(&h->d_rflag), &h->rflag_bytes, rf, true, stream);
 }
 
 // One apply launch. mode: wp::kModeShrink / kModeExpand / kModeFused.
@@ -960,6 +971,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
     a.tp_tmax = h->mail_tmax;
     a.tp_smax = h->mail_tmax;
     a.tp_seq = h->d_tp_seq;
+    a.tp_wait_ns = static_cast<unsigned long long>(h->cfg.peer_wait_ms > 0 ? h->cfg.peer_wait_ms : 5000) * 1000000ull;
     for (int p = 0; p < wp::kMaxTp; ++p) a.tp_mail[p] = h->tp_mail[p];
   }
   const bool pdl = h->cfg.use_pdl != 0;

@@ -9,45 +9,69 @@
 //
 // One launch does both halves of one LoRA layer call. The grid is persistent
 // (a fixed number of co-resident CTAs, so the launch can be captured in a CUDA
-// graph) and organised in thread-block clusters of CL CTAs; cluster c takes
-// segments c, c + G, c + 2G, ... of the device-resident table. For one segment
-// the CL CTAs of the cluster
+// graph) and organised in thread-block clusters of CL CTAs (CL = 2 on B200);
+// the segmenter's ClusterPlan gives each cluster its segments (whole
+// segments on the lowest clusters, helper clusters that take half of the
+// output columns of the largest segments when clusters are left over). For one
+// segment the CL CTAs of the cluster
 //   1. split d in CL slices: CTA q streams A[:, slice q] and x[segment rows,
-//      slice q] and accumulates a [r x <=32] fp32 partial in tensor memory;
-//   2. reduce the partials through distributed shared memory: after a
-//      cluster barrier, CTA q sums rows [q*n/CL, (q+1)*n/CL) over the CL
-//      partials (fixed order: deterministic) and writes the scaled rows into
-//      the H tile of every CTA of the cluster (reduce-scatter + all-gather);
+//      slice q] and accumulates a [r x <=32] fp32 partial;
+//   2. exchange the partials through distributed shared memory (st.async
+//      pushes into the peers' receive slots, completed on the peer's
+//      mbarrier) and add them in cluster-rank order: deterministic, and the
+//      same H on every CTA; with tensor parallelism (row-parallel "fused"
+//      mode) the partial then goes through the peers' mailboxes as well;
 //   3. split o in CL slices: CTA q streams B[slice q, :] and y[segment rows,
 //      slice q] and adds H . B^T to y, rounding once.
 // H never leaves the cluster; there are no global atomics and no second launch.
 // The same kernel runs the shrink alone (H written to global memory, for the
-// tensor-parallel all-reduce and the registry-path shrink()) or the expand
-// alone (H read from global memory).
+// registry-path shrink() and the NCCL row-parallel mode) or the expand alone
+// (H read from global memory).
+//
+// Two compute variants share this skeleton (template flag DEC):
+//   DEC = true, the production decode kernel: the compute warps run
+//     mma.sync m16n8k16 (bf16/fp16 in, fp32 accumulate) on fragments loaded
+//     with ldmatrix from the swizzled TMA boxes. Shrink: D[rank, token] +=
+//     A . x^T, warp w owning 32 columns of every stage, the eight warp
+//     partials added in a fixed order. Expand, transposed: D^T[o, t] = y +
+//     B[o, :] . H[t, :]^T with M = 16 output columns and N = 8 tokens per
+//     tile, y entering the accumulator through ldmatrix.trans and leaving
+//     through stmatrix.trans. The stage bodies are compiled once per
+//     token-tile count (1-4 tiles of 8 tokens). Decode segments are at most
+//     32 tokens, where one tcgen05.mma costs as much as a whole mma.sync stage.
+//   DEC = false, the tcgen05 variant: a dedicated MMA warp issues
+//     tcgen05.mma with the accumulators in tensor memory (described below).
+//     Selected by wp_config.kernel = 3; kept as the tensor-memory
+//     alternative for the decode shapes.
+// Prefill-sized runs of one adapter (>= 128 tokens) have their own tcgen05
+// GEMM kernels in wp_prefill.cu.
 //
 // Warp roles, handing off only through mbarriers:
 //   warp 8 (producer): lane 0 issues every TMA load of the CTA into a ring of
 //     STAGES shared-memory stages ("full" barriers) and refills a stage when
 //     its "empty" barrier fires; it runs ahead across segment and phase
 //     boundaries (the expand-phase loads of B and y do not depend on H).
-//   warp 9 (MMA): lane 0 issues every tcgen05.mma. Shrink stages are freed by
+//   warp 9: DEC = true: the y-store thread (a segment that fills its box
+//     exactly leaves through one tensor store); DEC = false: the MMA warp.
+//     Lane 0 issues every tcgen05.mma. Shrink stages are freed by
 //     the MMA commit itself; accumulators are handed to the compute warps by
 //     commits ("sh_full", "acc_full") and handed back after their TMEM reads
 //     ("sh_free", "acc_free"); two expand accumulators let the MMAs of the
 //     next stage run while the compute warps drain the current one.
-//   warps 0-7 (compute): read accumulators, run the cluster reduction, write
-//     the H tiles ("ht_full"), add y and store, and free expand stages.
+//   warps 0-7 (compute): the mma.sync math (DEC = true) or the accumulator
+//     reads (DEC = false), the cluster exchange, y add and store, and the
+//     release of expand stages.
 //
 // Data movement: A and x arrive as tiled tensor loads (cp.async.bulk.tensor)
 // of 64-column boxes with the 128-byte swizzle -- conflict-free fragment
 // loads, zero fill past the ends of d and T; x and y boxes are 8, 16 or 32
 // rows high to match the segment. B arrives as tensor boxes of 128 rows whose
 // swizzle matches its 2r-byte rows (rank 8: one 1-D bulk copy). One stage
-// carries 256 elements of d (shrink) or 256 output columns (expand). The cluster's segment descriptors
-// are cached in shared memory once per launch.
+// carries 256 elements of d (shrink) or 256 output columns (expand). The
+// cluster's segment descriptors are cached in shared memory once per launch.
 //
-// Math on the 5th-generation tensor cores (tcgen05.mma, issued by one thread,
-// accumulating in tensor memory):
+// tcgen05 variant (DEC = false), math on the 5th-generation tensor cores
+// (tcgen05.mma, issued by one thread, accumulating in tensor memory):
 //   shrink: D[rank, t] += A[rank, k] . x[t, k]^T per 64-column box, M = 64
 //     (rows past r are never read back), N = tokens rounded up to 8, K = 16
 //     per instruction, over the CTA's slice of d. The MMA commit itself frees the
@@ -69,7 +93,8 @@
 // reads the table and starts the weight loads (A, B) before the wait;
 // activations (x, y, H) are always loaded after it.
 //
-// Waits are bounded (1 s). A timed-out wait raises an error bit and marks the
+// Waits are bounded (1 s; a wait on a tensor-parallel peer by
+// wp_config.peer_wait_ms). A timed-out wait raises an error bit and marks the
 // CTA bad: compute stops, the producer stops issuing, the compute warps keep
 // arriving on the empty barriers and keep taking part in the cluster barriers
 // (so no partner is left waiting), copies in flight are drained with a short
@@ -909,6 +934,16 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           const int W = a.tp_world, me = a.tp_rank, par = tp_epoch & 1;
           const int nq = n * (R / 4);
           if (q == 0 && seg_half <= 0) {
+            // The rows and flag of parity(e) in a peer's mailbox were last
+            // used in epoch e - 2: write them only once that peer has
+            // finished its launch of epoch e - 2 (its done word, which it
+            // raises in this rank's mailbox, even for a launch without
+            // segments), so no rank overwrites a slot a slower peer still reads.
+            if (tid < W && tid != me && tp_epoch > 2 && !*s_bad &&
+                !wait_ge_sys(TpMail::done(a.tp_mail[me], W, a.tp_tmax, a.tp_smax, tid), tp_epoch - 2, a.err,
+                             a.tp_wait_ns))
+              *s_bad = 1;
+            named_sync(kBarCompute, kComputeThreads);
             if (!*s_bad) {
               for (int e4 = tid; e4 < nq; e4 += kComputeThreads) {
                 const int t = e4 / (R / 4), r0 = (e4 % (R / 4)) * 4;
@@ -926,7 +961,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
                   st_release_sys(TpMail::flag(a.tp_mail[p], W, a.tp_tmax, a.tp_smax, par, me, s.token_start), tp_epoch);
           }
           if (tid < W && tid != me && !*s_bad &&
-              !wait_flag_sys(TpMail::flag(a.tp_mail[me], W, a.tp_tmax, a.tp_smax, par, tid, s.token_start), tp_epoch, a.err))
+              !wait_flag_sys(TpMail::flag(a.tp_mail[me], W, a.tp_tmax, a.tp_smax, par, tid, s.token_start), tp_epoch, a.err,
+                             a.tp_wait_ns))
             *s_bad = 1;
           named_sync(kBarCompute, kComputeThreads);
           if (!*s_bad) {
@@ -1342,6 +1378,10 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       a.tp_seq[1] = 0;
       __threadfence();
       atomicExch(&a.tp_seq[0], tp_epoch);
+      // tell every peer that this rank has read all it will read of this
+      // epoch (also for a launch without segments)
+      for (int p = 0; p < a.tp_world; ++p)
+        if (p != a.tp_rank) st_release_sys(TpMail::done(a.tp_mail[p], a.tp_world, a.tp_tmax, a.tp_smax, a.tp_rank), tp_epoch);
     }
   }
   if (use_tmem) {

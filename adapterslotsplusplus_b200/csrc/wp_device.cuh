@@ -111,6 +111,21 @@ __device__ __forceinline__ bool wait_flag_sys(const int* p, int want, int* err,
   }
 }
 
+// Bounded wait until the int at p (written by a peer, system scope) is >= want.
+__device__ __forceinline__ bool wait_ge_sys(const int* p, int want, int* err,
+                                           unsigned long long timeout_ns = kWaitTimeoutNs) {
+  if (ld_acquire_sys(p) >= want) return true;
+  const unsigned long long t0 = global_timer_ns();
+  while (true) {
+    __nanosleep(64);
+    if (ld_acquire_sys(p) >= want) return true;
+    if (global_timer_ns() - t0 > timeout_ns) {
+      if (err) atomicOr(err, kErrWaitTimeout);
+      return false;
+    }
+  }
+}
+
 // ---- bulk async copy (TMA, untiled) ---------------------------------------
 // dst (shared), src (global) 16-byte aligned, bytes a multiple of 16.
 

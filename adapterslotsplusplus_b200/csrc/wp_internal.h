@@ -124,16 +124,22 @@ struct ApplyArgs {
   int tp_rank;
   int tp_tmax;  // token rows per (parity, source rank) in a mailbox
   int tp_smax;  // segment flags per (parity, source rank)
+  unsigned long long tp_wait_ns;  // bound of each wait on a peer (wp_config.peer_wait_ms)
 };
 
 // Mailbox layout: partial rows [2 parities][world][tmax][kMaxRank] fp32, then
-// flags [2][world][smax] int (the epoch that wrote the segment's rows).
+// flags [2][world][smax] int (the epoch that wrote the segment's rows), then
+// done[world] int: the latest epoch whose launch has finished on rank `src`
+// (after which that rank reads nothing more of that epoch's parity).
 struct TpMail {
   static __host__ __device__ size_t data_floats(int world, int tmax) {
     return static_cast<size_t>(2) * world * tmax * kMaxRank;
   }
   static __host__ __device__ size_t bytes(int world, int tmax, int smax) {
-    return data_floats(world, tmax) * 4 + static_cast<size_t>(2) * world * smax * 4;
+    return data_floats(world, tmax) * 4 + static_cast<size_t>(2) * world * smax * 4 + static_cast<size_t>(world) * 4;
+  }
+  static __host__ __device__ int* done(float* mail, int world, int tmax, int smax, int src) {
+    return reinterpret_cast<int*>(mail + data_floats(world, tmax)) + static_cast<size_t>(2) * world * smax + src;
   }
   static __host__ __device__ float* row(float* mail, int world, int tmax, int par, int src, int t) {
     return mail + ((static_cast<size_t>(par) * world + src) * tmax + t) * kMaxRank;

@@ -61,6 +61,7 @@ class WarpPipeEngine:
             use_pdl=1 if self.config.use_pdl else 0,
             prefetch_weights=1 if self.config.prefetch_weights else 0,
             kernel={"auto": 0, "cluster": 1, "split": 2, "tc": 3}[self.config.kernel],
+            peer_wait_ms=int(self.config.peer_wait_ms),
         )
         handle = ctypes.c_void_p()
         _lib.check(self._lib.wp_create(ctypes.byref(cfg), ctypes.byref(handle)), None)

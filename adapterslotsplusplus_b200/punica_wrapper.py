@@ -46,10 +46,19 @@ _engine: Optional[WarpPipeEngine] = None
 
 def _get_engine() -> WarpPipeEngine:
     """Lazy singleton: the engine allocates device memory, so it is created
-    on first use, after the CUDA context exists."""
+    on first use, after the CUDA context exists.
+
+    Serving contract: adapter weights are not written while a step runs
+    (vLLM loads them between steps), and the kernel right before a LoRA call
+    is the base layer's GEMM. So the engine runs with prefetch_weights: each
+    apply launch starts streaming its adapter weights while the preceding
+    kernel finishes (programmatic dependent launch). Activations are always
+    read after that kernel completes."""
     global _engine
     if _engine is None:
-        _engine = WarpPipeEngine()
+        from .config import WarpPipeConfig
+
+        _engine = WarpPipeEngine(WarpPipeConfig(prefetch_weights=True))
     return _engine
 
 

@@ -1,24 +1,32 @@
 """Tensor-parallel grouped LoRA apply (one process per GPU, NCCL over NVLink).
 
 The reference is single-GPU; this is the sharding of the apply path for a
-tensor-parallel base model:
+tensor-parallel base model, following vLLM's LoRA layers
+(vllm/lora/layers/column_parallel_linear.py, row_parallel_linear.py):
 
   column-parallel layers (q, k, v, gate, up): x and A are replicated, B and
     the output y are split along out_features. Each rank shrinks the full
     [T, r] H and expands only its own output columns -- no collective.
-  row-parallel layers (o, down): x and A are split along d_model. Each rank
-    shrinks its slice into a partial fp32 H_p [T, r]; one NCCL all-reduce
-    (sum, fp32, T*r values) over the tensor-parallel group gives H on every
-    rank; each rank then expands with the full B onto its replica of y.
+  row-parallel layers (o, down): x and A are split along d_model; B is full.
+    Three ways to combine the ranks, chosen by ``row_mode``:
 
-By default a row-parallel layer is ONE launch (wp_add_lora_row_parallel):
-each segment's partial H is written straight into the peers' mailboxes (device
-memory mapped over NVLink through CUDA IPC), released with a flag, waited for
-(bounded) and summed in rank order inside the apply kernel, so the exchange
-overlaps the other segments' work. With fused=False it is three launches
-(wp_add_lora_shrink, wp_tp_allreduce_f32 over NCCL, wp_add_lora_expand).
-Either way everything runs on the caller's stream, so a whole step can be
-captured in one CUDA graph.
+    "partial" (default; vLLM's RowParallelLinearWithLoRA): each rank adds
+      (scale * x_p . A_p^T) . B^T into its own *partial* output, the base
+      layer's row-parallel partial sum. The base layer's all-reduce of that
+      output, which a tensor-parallel model runs anyway, sums the ranks'
+      LoRA terms with the base terms: by linearity the sum over ranks is
+      (scale * x . A^T) . B^T. The LoRA path itself moves no bytes between
+      GPUs and waits on no peer.
+    "fused": ONE launch (wp_add_lora_row_parallel) that produces the full
+      LoRA term on every rank: each segment's partial H is written straight
+      into the peers' mailboxes (device memory mapped over NVLink through
+      CUDA IPC), released with a flag, waited for (bounded) and summed in
+      rank order inside the apply kernel.
+    "nccl": three launches (wp_add_lora_shrink, wp_tp_allreduce_f32 of the
+      fp32 [T, r] partials, wp_add_lora_expand), the S-LoRA form.
+
+Everything runs on the caller's stream, so a whole step can be captured in
+one CUDA graph.
 
 The sharding helpers are pure tensor slicing and run anywhere; the apply
 methods need the CUDA engine.
@@ -72,8 +80,14 @@ class TensorParallelApply:
     exchanged)."""
 
     def __init__(self, engine, rank: Optional[int] = None, world: Optional[int] = None, group=None,
-                 fused: bool = True):
+                 fused: Optional[bool] = None, row_mode: str = "partial"):
         import torch.distributed as dist
+
+        if fused is not None:  # older spelling: fused=True -> "fused", fused=False -> "nccl"
+            row_mode = "fused" if fused else "nccl"
+        if row_mode not in ("partial", "fused", "nccl"):
+            raise ValueError(f"row_mode must be 'partial', 'fused' or 'nccl', not {row_mode!r}")
+        self.row_mode = row_mode
 
         self.engine = engine
         self.rank = dist.get_rank(group) if rank is None else rank
@@ -89,7 +103,7 @@ class TensorParallelApply:
         uid = (ctypes.c_char * nbytes).from_buffer_copy(obj[0])
         _lib.check(lib.wp_tp_init(engine.handle, uid, self.rank, self.world), engine.handle)
         self._H = torch.empty(engine.config.max_tokens * 64, dtype=torch.float32, device=engine.device)
-        self.fused = bool(fused) and self.world > 1
+        self.fused = row_mode == "fused" and self.world > 1
         if self.fused:
             # every rank's mailbox, mapped into every process (CUDA IPC over NVLink)
             hb = int(lib.wp_tp_mailbox_handle_bytes())
@@ -100,7 +114,10 @@ class TensorParallelApply:
             dist.all_gather_object(got, bytes(mine), group=group)
             allh = (ctypes.c_char * (hb * self.world)).from_buffer_copy(b"".join(got))
             _lib.check(lib.wp_tp_mailbox_open(engine.handle, allh), engine.handle)
-            dist.barrier(group=group)
+        # every rank is past its set-up before any rank's first exchange
+        # launch (a peer still initialising would otherwise eat into the
+        # exchange's bounded wait)
+        dist.barrier(group=group)
 
     def close(self):
         import torch.distributed as dist
@@ -121,13 +138,17 @@ class TensorParallelApply:
         return self.engine.add_lora_packed(full, x, wa_t_all, wb_shard, scale)
 
     def row_parallel(self, y, x_shard, wa_shard, wb_t_all, scale) -> bool:
-        """Partial shrink on this rank's d slice, sum of the ranks' H, full
-        expand: one launch with the peer-memory exchange (fused), else
-        shrink + NCCL all-reduce + expand."""
+        """Row-parallel LoRA term from this rank's d slice of x and A and the
+        full B. row_mode "partial": y is this rank's partial output and
+        receives this rank's share (the caller's all-reduce of y completes
+        it). "fused" / "nccl": y is the replicated output and receives the
+        full term (sum of the ranks' H, then the expand)."""
         eng, lib = self.engine, self._lib
         r = int(wb_t_all.size(-1))
         if not eng.rank_supported(r):
             return False
+        if self.row_mode == "partial" or self.world == 1:
+            return self.engine.add_lora_packed(y, x_shard, wa_shard, wb_t_all, scale)
         x2d = x_shard.reshape(-1, x_shard.size(-1))
         y2d = y.view(-1, y.size(-1))
         T, d = int(x2d.size(0)), int(x2d.size(1))

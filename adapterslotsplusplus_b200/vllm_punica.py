@@ -36,12 +36,16 @@ _engine = None
 
 
 def _get_engine():
-    """Lazy singleton (the engine allocates device memory)."""
+    """Lazy singleton (the engine allocates device memory). Runs with
+    prefetch_weights: vLLM writes the LoRA stacks only between steps, so an
+    apply launch may start streaming adapter weights while the preceding
+    kernel (the base layer's GEMM) finishes; activations are read after it."""
     global _engine
     if _engine is None:
+        from .config import WarpPipeConfig
         from .engine import WarpPipeEngine
 
-        _engine = WarpPipeEngine()
+        _engine = WarpPipeEngine(WarpPipeConfig(prefetch_weights=True))
     return _engine
 
 

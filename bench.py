@@ -13,11 +13,15 @@ implies against the measured peak. One JSON line on rank 0.
   python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference] [--no-sweep]
 
 With N > 1 (launched under torch.distributed.run, one rank per GPU) the same
-step runs tensor-parallel over the N GPUs: column-parallel projections (q, k,
-v, gate, up) expand their own out_features slice, row-parallel ones (o, down)
-shrink their d_in slice and sum the ranks' fp32 [T, r] partials over NVLink
-peer memory inside the apply launch (strong scaling; the time is the max over
-ranks).
+step runs tensor-parallel over the N GPUs the way vLLM shards LoRA layers:
+column-parallel projections (q, k, v, gate, up) expand their own out_features
+slice; row-parallel ones (o, down) shrink their d_in slice and add their
+share into the base layer's partial output, which the base model's
+all-reduce completes (--row-mode partial, the default; "fused" sums the
+ranks' [T, r] partials over NVLink peer memory inside the apply launch,
+"nccl" all-reduces them with NCCL). Strong scaling; the time is the max over
+ranks. The line carries `tp_parity` (layer 0's q, o and down against the
+unsharded single-GPU result on the same box) and per-kind launch times.
 
   python bench.py --config3 [--gpus N]
 
@@ -32,7 +36,10 @@ for profilers).
 --impl reference times the reference's CPU implementation of the path (its
 torch per-segment fp32 math, tests/correctness/reference_bgmv.py:4-18,
 restated in oracle/apply.py) on the host cores, on a bounded sample of the
-same workload (a few layers, extrapolated to 32).
+same workload (a few layers, extrapolated to 32). Its `reference_gpu` key
+times the reference's own CUDA kernels (built from its sources into
+oracle/_ref) on the same step in fp16; our line's `fp16_step` is the same
+step through this library.
 """
 
 from __future__ import annotations
@@ -78,11 +85,11 @@ def algorithmic_bytes(U: int, T: int, d: int, o: int, r: int, elt: int = 2) -> t
     return shrink, expand
 
 
-def step_bytes(U: int, T: int, r: int = RANK, world: int = 1) -> tuple[int, int]:
+def step_bytes(U: int, T: int, r: int = RANK, world: int = 1, exchange: bool = False) -> tuple[int, int]:
     """Algorithmic bytes of one step on one rank of a tensor-parallel group of
     `world` (world = 1: the whole model). Column-parallel projections split
     B and y along out_features; row-parallel ones split x and A along d_in
-    and exchange the [T, r] fp32 partials (counted as read + write)."""
+    (with `exchange`, plus the [T, r] fp32 partials, counted as read + write)."""
     s = e = 0
     for _, d, o, _, kind in PROJS:
         if world > 1 and kind == "col":
@@ -92,7 +99,7 @@ def step_bytes(U: int, T: int, r: int = RANK, world: int = 1) -> tuple[int, int]
         bs, be = algorithmic_bytes(U, T, d, o, r)
         s += bs
         e += be
-        if world > 1 and kind == "row":
+        if world > 1 and kind == "row" and exchange:
             e += 2 * T * r * 4
     return s * LAYERS, e * LAYERS
 
@@ -230,6 +237,61 @@ def time_graph(g, pre, iters):
     return start.elapsed_time(end) / iters  # ms
 
 
+def tp_parity(eng, tpa, device, rank, world, scale):
+    """Tensor-parallel results of layer 0's q (column-parallel), o and down
+    (row-parallel) against the unsharded result of the same library on one
+    GPU, on identical inputs (every rank draws the full weights from one
+    seed and keeps its shard). Row-parallel partial outputs are summed with
+    an all-reduce, as the base layer's all-reduce would. Returns, on every
+    rank, max-abs error / RMS per projection and whether all ranks hold
+    bit-identical full outputs."""
+    import torch.distributed as dist
+
+    from adapterslotsplusplus_b200.tp import shard_column, shard_row, shard_row_input
+
+    g = torch.Generator(device=device).manual_seed(77)
+    out = {}
+    same = True
+    for name, d, o, _, kind in [p for p in PROJS if p[0] in ("q", "o", "down")]:
+        wa = torch.randn(RESIDENT, 1, RANK, d, device=device, dtype=torch.bfloat16, generator=g) * 0.02
+        wb = torch.randn(RESIDENT, 1, o, RANK, device=device, dtype=torch.bfloat16, generator=g) * 0.02
+        x = torch.randn(TOKENS, d, device=device, dtype=torch.bfloat16, generator=g) * 0.1
+        y0 = torch.randn(TOKENS, o, device=device, dtype=torch.bfloat16, generator=g) * 0.1
+        ref = y0.clone()
+        assert eng.add_lora_packed(ref, x, wa, wb, scale)
+        if kind == "col":
+            a, b = rank * (o // world), (rank + 1) * (o // world)
+            ys = y0[:, a:b].contiguous()
+            assert tpa.column_parallel(ys, x, wa, shard_column(wb, rank, world), scale)
+            parts = [torch.empty_like(ys) for _ in range(world)]
+            dist.all_gather(parts, ys)
+            full = torch.cat(parts, dim=1)
+        else:
+            if tpa.row_mode == "partial":
+                # the base layer's bias-like share goes to rank 0 only
+                yp = y0.clone() if rank == 0 else torch.zeros_like(y0)
+                assert tpa.row_parallel(yp, shard_row_input(x, rank, world), shard_row(wa, rank, world), wb, scale)
+                ypf = yp.float()
+                dist.all_reduce(ypf)
+                full = ypf.to(torch.bfloat16)
+            else:
+                full = y0.clone()
+                assert tpa.row_parallel(full, shard_row_input(x, rank, world), shard_row(wa, rank, world), wb, scale)
+        torch.cuda.synchronize()
+        rms = float(ref.float().pow(2).mean().sqrt())
+        err = float((full.float() - ref.float()).abs().max()) / rms
+        # bit-identity across ranks: compare every rank's output with rank 0's
+        r0 = full.clone()
+        dist.broadcast(r0, src=0)
+        diff = torch.tensor([int(not torch.equal(r0, full))], device=device)
+        dist.all_reduce(diff)
+        same = same and int(diff.item()) == 0
+        out[name] = round(err, 6)
+    return {"max_abs_err_over_rms": out, "bound": 2e-2, "ok": all(v <= 2e-2 for v in out.values()) and same,
+            "ranks_bit_identical": same, "row_mode": tpa.row_mode,
+            "against": "the unsharded add_lora_packed of the same inputs on this GPU"}
+
+
 def run_ours(args, rank, world, local_rank):
     from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
 
@@ -237,7 +299,9 @@ def run_ours(args, rank, world, local_rank):
     torch.cuda.set_device(device)
     # prefetch_weights: the serving contract (adapter weights are static during
     # a step) lets each apply launch start streaming weights while the
-    # previous launch finishes.
+    # previous launch finishes. The serving hooks (punica_wrapper.py,
+    # vllm_punica.py) build their engine with the same setting; the step
+    # without it is reported as `strict_order`.
     eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
     plan = eng.apply_plan(torch.bfloat16, RANK)
     scale = 16.0 / RANK
@@ -248,26 +312,34 @@ def run_ours(args, rank, world, local_rank):
     stack = Stack(device, RESIDENT, rank=rank, world=world)
     calls = list(stack.calls())
     tpa = None
+    parity = None
     if world > 1:
-        # tensor parallel over the N GPUs: column-parallel projections expand
-        # their own output columns; row-parallel ones sum the ranks' shrink
-        # partials over NVLink peer memory inside the apply launch
+        # tensor parallel over the N GPUs (vLLM's sharding): column-parallel
+        # projections expand their own output columns; row-parallel ones
+        # add their d_in slice's share into the partial output (row_mode
+        # "partial"), or exchange the partial H ("fused" / "nccl")
         from adapterslotsplusplus_b200.tp import TensorParallelApply
 
-        tpa = TensorParallelApply(eng)
+        tpa = TensorParallelApply(eng, row_mode=args.row_mode)
+        eng.build_seg_bounds(idx_dev)
+        parity = tp_parity(eng, tpa, device, rank, world, scale)
 
-    def full_step():
-        for kind, y, x, wa, wb in calls:
-            if tpa is None:
-                eng.add_lora_packed(y, x, wa, wb, scale)
-            elif kind == "col":
-                tpa.column_parallel(y, x, wa, wb, scale)
-            else:
-                tpa.row_parallel(y, x, wa, wb, scale)
+    def run(kinds=("col", "row")):
+        def f():
+            for kind, y, x, wa, wb in calls:
+                if kind not in kinds:
+                    continue
+                if tpa is None:
+                    eng.add_lora_packed(y, x, wa, wb, scale)
+                elif kind == "col":
+                    tpa.column_parallel(y, x, wa, wb, scale)
+                else:
+                    tpa.row_parallel(y, x, wa, wb, scale)
+        return f
 
     seg = lambda: eng.build_seg_bounds(idx_dev)  # noqa: E731
     seg()
-    g_full = capture(full_step)
+    g_full = capture(run())
 
     for _ in range(args.warmup):
         seg()
@@ -281,26 +353,37 @@ def run_ours(args, rank, world, local_rank):
         ms = time_graph(g_full, seg, args.steps)  # the step: segmenter + 224 apply launches
         ms_apply = time_graph(g_full, None, args.steps)  # the 224 apply launches alone
     torch.cuda.synchronize()
+    per_kind = {}
+    if world > 1 or args.per_kind:
+        # column- and row-parallel launches timed apart (each kind's calls of
+        # the step in a graph of their own)
+        for kind in ("col", "row"):
+            gk = capture(run((kind,)), warm=1)
+            n = sum(1 for c in calls if c[0] == kind)
+            per_kind[kind] = time_graph(gk, None, args.steps) * 1e3 / n
+            del gk
     if world > 1:
-        t = torch.tensor([ms, ms_apply], device=device)
+        t = torch.tensor([ms, ms_apply, per_kind.get("col", 0.0), per_kind.get("row", 0.0)], device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, ms_apply = t.tolist()
+        ms, ms_apply, per_kind["col"], per_kind["row"] = t.tolist()
 
     # e2e through the public API: token ids from pinned host memory, the step,
     # and a read back of one output row, all on the stream, every step.
     ids_host = torch.as_tensor(ids).pin_memory()
-    out_host = torch.empty(HIDDEN, dtype=torch.bfloat16).pin_memory()
+    out_host = torch.empty(calls[-1][1].size(-1), dtype=torch.bfloat16).pin_memory()
     y_last = calls[-1][1]
 
     def e2e_step():
         idx_dev.copy_(ids_host, non_blocking=True)
         eng.build_seg_bounds(idx_dev)
         g_full.replay()
-        out_host.copy_(y_last[0, :HIDDEN], non_blocking=True)
+        out_host.copy_(y_last[0], non_blocking=True)
 
     for _ in range(2):
         e2e_step()
     torch.cuda.synchronize()
+    if world > 1:
+        torch.distributed.barrier()
     t0 = time.perf_counter()
     st, en = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
     st.record()
@@ -309,8 +392,13 @@ def run_ours(args, rank, world, local_rank):
     en.record()
     torch.cuda.synchronize()
     e2e_ms = max(st.elapsed_time(en), (time.perf_counter() - t0) * 1e3) / args.steps
+    if world > 1:
+        t = torch.tensor([e2e_ms], device=device)
+        torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
+        e2e_ms = float(t.item())
 
-    shr_b, exp_b = step_bytes(U, TOKENS, world=world)
+    exchange = tpa is not None and tpa.row_mode != "partial"
+    shr_b, exp_b = step_bytes(U, TOKENS, world=world, exchange=exchange)
     total_b = (shr_b + exp_b) * world  # whole job: every rank's share of the step
     peaks = measured_peaks()
     hbm = peaks.get("hbm_gbs")
@@ -320,19 +408,29 @@ def run_ours(args, rank, world, local_rank):
     # one launch per step). Per launch: the mean over the calls of the step on
     # one rank.
     dom = eng.last_apply_kernel() or "apply_kernel"
-    # one apply launch per projection: row-parallel layers exchange their
-    # partial H over peer memory inside the launch
     launches_per_step = LAYERS * len(PROJS)
+    if tpa is not None and tpa.row_mode == "nccl":
+        apply_launches = launches_per_step + 2 * LAYERS * sum(1 for p in PROJS if p[4] == "row")
+    else:
+        apply_launches = launches_per_step
     per_launch_ms = ms_apply / launches_per_step
     per_launch_b = total_b / world / launches_per_step
     achieved = per_launch_b / (per_launch_ms * 1e-3) / 1e9
     traffic = None
     tf = ROOT / "profiles" / "traffic.json"
-    if tf.exists():
+    if tf.exists() and world == 1:
         try:
             traffic = json.loads(tf.read_text()).get(dom)
         except Exception:
             traffic = None
+    if tpa is None:
+        tp_desc = "single GPU"
+    elif tpa.row_mode == "partial":
+        tp_desc = ("tensor-parallel: column-parallel projections split B and y; row-parallel ones add their "
+                   "d_in slice's share into the base layer's partial output (vLLM RowParallelLinearWithLoRA), "
+                   "completed by the base model's all-reduce, which is not LoRA work and is not timed")
+    else:
+        tp_desc = f"tensor-parallel, row-parallel partial H summed over the ranks ({tpa.row_mode})"
 
     result = {
         "metric": METRIC,
@@ -343,16 +441,16 @@ def run_ours(args, rank, world, local_rank):
         "warmup": args.warmup,
         "ms_per_step": round(ms, 4),
         "higher_is_better": False,
-        "scaling": "strong" if world > 1 else "weak",
+        "scaling": "strong",
         "vs_baseline": None,
         "dtype": "bf16",
         "data": "synthetic (seeded random weights and activations, Zipf(1.1) routing)",
         "config": {"workload": WORKLOAD, "layers": LAYERS, "projections": len(PROJS), "rank": RANK,
                    "resident_adapters": RESIDENT, "active_adapters": U, "tokens": TOKENS,
-                   "parallelism": f"tp{world}" if world > 1 else "single",
+                   "parallelism": f"tp{world}" if world > 1 else "single", "tp": tp_desc,
                    "l2": "inputs exceed L2 (10.2 GB of adapter weights per step), no flush needed"},
         "step_gbs": round(total_b / (ms * 1e-3) / 1e9, 1),
-        "step_frac_of_hbm": round(total_b / (ms * 1e-3) / 1e9 / hbm, 4),
+        "step_frac_of_hbm": round(total_b / (ms * 1e-3) / 1e9 / hbm / world, 4),
         "step_bytes": total_b,
         "kernels_ms_per_step": {dom: round(ms_apply, 4), "segmenter_and_gaps": round(ms - ms_apply, 4)},
         "apply_plan": {"cluster": plan[0], "ctas": plan[1]},
@@ -362,15 +460,73 @@ def run_ours(args, rank, world, local_rank):
                      "launch_us": round(per_launch_ms * 1e3, 3)},
         "e2e": {"value": round(e2e_ms * 1e3, 2), "unit": "us/step", "h2d_bytes_per_step": int(ids.nbytes),
                 "d2h_bytes_per_step": int(out_host.numel() * 2),
-                "path": "WarpPipeEngine.build_seg_bounds + graph of the step's apply calls (tensor-parallel when N > 1: column-parallel projections split B and y, row-parallel ones exchange the partial H over NVLink peer memory inside the apply kernel)"},
-        "gpu_launches": args.steps * (1 + launches_per_step),
+                "path": "WarpPipeEngine.build_seg_bounds + graph of the step's apply calls; per step the token "
+                        "ids come from pinned host memory and one output row goes back. The activations and "
+                        "outputs stay on the device, as they do for a LoRA hook inside a served model (" + tp_desc + ")"},
+        "gpu_launches": args.steps * (1 + apply_launches),
         "clocks": clk.summary(),
     }
+    if per_kind:
+        result["per_kind_us_per_launch"] = {k: round(v, 3) for k, v in per_kind.items()}
+        result["per_kind_us_per_launch"]["outside_graph_us_per_step"] = round((ms - ms_apply) * 1e3, 2)
+    if parity is not None:
+        result["tp_parity"] = parity
     del g_full, stack, calls
     if tpa is not None:
         tpa.close()
     torch.cuda.empty_cache()
     return eng, result
+
+
+def fp16_step(device, steps):
+    """The headline step in fp16 (the reference kernels' only type), for the
+    side-by-side with the reference's own GPU kernels that the reference arm
+    (`--impl reference`, key `reference_gpu`) times on the same workload."""
+    from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
+
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    idx = torch.as_tensor(make_ids(RESIDENT), device=device)
+    stack = Stack(device, RESIDENT, dtype=torch.float16)
+    calls = list(stack.calls())
+
+    def step():
+        for _, y, x, wa, wb in calls:
+            eng.add_lora_packed(y, x, wa, wb, 16.0 / RANK)
+
+    eng.build_seg_bounds(idx)
+    g = capture(step, warm=1)
+    for _ in range(3):
+        g.replay()
+    ms = time_graph(g, lambda: eng.build_seg_bounds(idx), steps)
+    del g, stack, calls, eng
+    torch.cuda.empty_cache()
+    return {"us_per_step": round(ms * 1e3, 2), "dtype": "fp16"}
+
+
+def strict_order(device, steps):
+    """The step with prefetch_weights off (strict stream order: no load of a
+    launch starts before the previous launch has finished)."""
+    from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
+
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=False), device=device)
+    ids = make_ids(RESIDENT)
+    idx = torch.as_tensor(ids, device=device)
+    stack = Stack(device, RESIDENT)
+    calls = list(stack.calls())
+    scale = 16.0 / RANK
+
+    def step():
+        for _, y, x, wa, wb in calls:
+            eng.add_lora_packed(y, x, wa, wb, scale)
+
+    eng.build_seg_bounds(idx)
+    g = capture(step, warm=1)
+    for _ in range(3):
+        g.replay()
+    ms = time_graph(g, lambda: eng.build_seg_bounds(idx), steps)
+    del g, stack, calls, eng
+    torch.cuda.empty_cache()
+    return {"us_per_step": round(ms * 1e3, 2), "prefetch_weights": False}
 
 
 def fused_slices(eng, device, steps):
@@ -488,6 +644,62 @@ def cpu_reference_layers(n_layers: int, resident: int = RESIDENT, threads: int |
     return dt, threads
 
 
+def reference_gpu(steps: int, warmup: int):
+    """The reference's own CUDA kernels (warp_pipe_r32.cu, built from the
+    reference's sources into oracle/_ref/libwpref.so by oracle/build_ref.sh)
+    on the same decode step in fp16, their only type: one
+    build_seg_bounds_kernel, then per call bgmv_shrink_dsak + bgmv_expand_dsak
+    (WarpPipeExtension::add_lora_packed, warp_pipe_bindings.cpp:195-234),
+    the 224 calls replayed from one CUDA graph. Config 1 fits every limit of
+    those kernels (T = 256, d and o multiples of 256, rank 32)."""
+    import ctypes
+
+    so = ROOT / "oracle" / "_ref" / "libwpref.so"
+    if not torch.cuda.is_available():
+        return {"unavailable": "no CUDA device"}
+    if not so.exists():
+        return {"unavailable": "oracle/_ref/libwpref.so was not built (reference sources absent at build time)"}
+    lib = ctypes.CDLL(str(so))
+    lib.ref_seg_bounds.argtypes = [ctypes.c_void_p, ctypes.c_int, ctypes.c_void_p, ctypes.c_void_p]
+    lib.ref_add_lora_r32.argtypes = [ctypes.c_void_p] * 3 + [ctypes.c_int64, ctypes.c_void_p, ctypes.c_int64,
+                                                             ctypes.c_float, ctypes.c_int, ctypes.c_int, ctypes.c_void_p]
+    device = torch.device("cuda", 0)
+    torch.cuda.set_device(device)
+    ids = make_ids(RESIDENT)
+    idx = torch.as_tensor(ids, device=device, dtype=torch.int64)
+    table = (ctypes.c_int32 * (3 * 256))()
+    num = ctypes.c_int32()
+    if lib.ref_seg_bounds(idx.data_ptr(), len(ids), table, ctypes.byref(num)) != 0:
+        return {"unavailable": "reference build_seg_bounds refused the table"}
+    stack = Stack(device, RESIDENT, dtype=torch.float16)
+    calls = list(stack.calls())
+    scale = 16.0 / RANK
+
+    def step():
+        st = torch.cuda.current_stream().cuda_stream
+        for _, y, x, wa, wb in calls:
+            rc = lib.ref_add_lora_r32(y.data_ptr(), x.data_ptr(), wa.data_ptr(), wa.stride(0), wb.data_ptr(),
+                                      wb.stride(0), scale, x.size(-1), y.size(-1), st)
+            if rc != 0:
+                raise RuntimeError(f"ref_add_lora_r32 failed ({rc})")
+
+    step()  # first call allocates the reference's buffers (outside capture)
+    torch.cuda.synchronize()
+    g = capture(step, warm=1)
+    for _ in range(max(3, warmup)):
+        g.replay()
+    ms = time_graph(g, None, steps)
+    U = int(np.unique(ids).size)
+    sb, eb = step_bytes(U, TOKENS)
+    del g, stack, calls
+    torch.cuda.empty_cache()
+    return {"us_per_step": round(ms * 1e3, 2), "dtype": "fp16", "segments": int(num.value),
+            "step_gbs": round((sb + eb) / (ms * 1e-3) / 1e9, 1),
+            "kernels": "reference build_seg_bounds once (outside the graph) + 224 x (bgmv_shrink_dsak_r32, "
+                       "bgmv_expand_dsak_r32) in a CUDA graph",
+            "compare_with": "our line's fp16_step.us_per_step (same workload, fp16)"}
+
+
 def run_reference(args, rank, world):
     if rank != 0:
         return None
@@ -500,6 +712,10 @@ def run_reference(args, rank, world):
         per_layer.append(dt)
     us = float(np.median(per_layer)) * LAYERS * 1e6
     sample = f"1 of {LAYERS} layers (7 projections) per step, extrapolated x{LAYERS}"
+    try:
+        gpu = reference_gpu(args.steps, args.warmup)
+    except Exception as exc:  # reported, never fatal to the CPU arm
+        gpu = {"unavailable": f"{type(exc).__name__}: {exc}"[:200]}
     return {
         "metric": METRIC, "value": round(us, 1), "unit": "us/step", "n_gpus": world, "steps": args.steps,
         "warmup": args.warmup, "ms_per_step": round(us / 1e3, 3), "higher_is_better": False, "scaling": "weak",
@@ -508,10 +724,11 @@ def run_reference(args, rank, world):
         "cpu_baseline": {"value": round(us, 1), "unit": "us/step", "cores": threads, "kind": "port",
                          "sample": sample},
         "e2e": {"value": round(us, 1), "unit": "us/step", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "reference_gpu": gpu,
     }
 
 
-def prefill_mix(device, kernels=("cluster", "split", "tc"), iters=10):
+def prefill_mix(device, kernels=("auto", "cluster", "split"), iters=10):
     """BASELINE config 2's prefill mix on one 4096 -> 4096 projection: 4096
     tokens in 8 contiguous 512-token runs (8 adapters), rank 32, bf16. Per
     kernel: device us per call (CUDA graph of one call, 8 rotating weight
@@ -545,11 +762,62 @@ def prefill_mix(device, kernels=("cluster", "split", "tc"), iters=10):
             "algorithmic_mb": round((sb + eb) / 1e6, 1), "per_kernel": out}
 
 
+def config2_sweep(device, iters=5, ranks=(8, 16, 32, 64), residents=(1, 8, 64, 512), tokens=(1, 16, 256, 4096),
+                  routings=("uniform", "zipf")):
+    """one 4096 -> 4096 projection, bf16, rank x resident
+    adapters x tokens x routing (uniform or Zipf(1.1), stable-sorted ids).
+    Per case: device us per call (a CUDA graph of calls over rotating weight
+    sets, together larger than L2 where the resident set allows it), the
+    algorithmic GB/s and its fraction of the measured HBM bandwidth. Compact
+    rows: [rank, resident, tokens, routing, active, us, GB/s, frac]."""
+    from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
+
+    d = o = HIDDEN
+    hbm = measured_peaks().get("hbm_gbs") or 6650.0
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    rows = []
+    g = torch.Generator(device=device).manual_seed(2)
+    for r in ranks:
+        for resident in residents:
+            set_bytes = resident * (d + o) * r * 2
+            nsets = int(min(16, max(2, -(-300_000_000 // set_bytes))))
+            sets = [(torch.randn(resident, 1, r, d, device=device, dtype=torch.bfloat16, generator=g) * 0.02,
+                     torch.randn(resident, 1, o, r, device=device, dtype=torch.bfloat16, generator=g) * 0.02)
+                    for _ in range(nsets)]
+            for T in tokens:
+                x = torch.randn(T, d, device=device, dtype=torch.bfloat16, generator=g) * 0.1
+                y = torch.zeros(T, o, device=device, dtype=torch.bfloat16)
+                for routing in routings:
+                    if routing == "zipf":
+                        ids = zipf_ids(resident, T, seed=SEED)
+                    else:
+                        ids = np.sort(np.random.default_rng(0).integers(0, resident, T), kind="stable")
+                    U = int(np.unique(ids).size)
+                    eng.build_seg_bounds(torch.as_tensor(ids, device=device))
+
+                    def step():
+                        for wa, wb in sets:
+                            eng.add_lora_packed(y, x, wa, wb, 16.0 / r)
+
+                    gr = capture(step, warm=1)
+                    ms = time_graph(gr, None, iters) / nsets
+                    del gr
+                    sb, eb = algorithmic_bytes(U, T, d, o, r)
+                    gbs = (sb + eb) / (ms * 1e-3) / 1e9
+                    rows.append([r, resident, T, routing, U, round(ms * 1e3, 2), round(gbs, 1), round(gbs / hbm, 3)])
+                del x, y
+            del sets
+            torch.cuda.empty_cache()
+    del eng
+    return {"d": d, "o": o, "dtype": "bf16", "columns": ["rank", "resident", "tokens", "routing", "active",
+                                                         "us_per_call", "gbs", "frac_of_hbm"], "rows": rows}
+
+
 def config3(args, rank, world, local_rank):
     """a Llama-2-13B-shaped stack (40 layers, hidden 5120,
     intermediate 13824), rank 64, bf16, 128 resident adapters, 512 tokens,
     Zipf(1.1), tensor-parallel over the N GPUs (column-parallel q/k/v/gate/up,
-    row-parallel o/down with the peer-memory exchange). Four distinct layer
+    row-parallel o/down as --row-mode says). Four distinct layer
     weight sets (6.4 GB per GPU at N = 1, far larger than L2) are cycled over
     the 40 layers, so every launch streams its weights from HBM. One JSON
     line on rank 0: us per step (max over ranks) and the per-GPU HBM GB/s."""
@@ -582,7 +850,7 @@ def config3(args, rank, world, local_rank):
     if world > 1:
         from adapterslotsplusplus_b200.tp import TensorParallelApply
 
-        tpa = TensorParallelApply(eng)
+        tpa = TensorParallelApply(eng, row_mode=args.row_mode)
     scale = 1.0
 
     def step():
@@ -620,8 +888,11 @@ def config3(args, rank, world, local_rank):
     del gr
     if tpa is not None:
         tpa.close()
+    del sets, xs
+    torch.cuda.empty_cache()
     return {"config": "3 (llama2-13b: 40 layers, r64, bf16, 128 resident, 512 tokens, Zipf(1.1))",
             "n_gpus": world, "parallelism": f"tp{world}" if world > 1 else "single",
+            "row_mode": args.row_mode if world > 1 else None,
             "us_per_step": round(ms * 1e3, 1), "launches_per_step": layers * len(projs),
             "active_adapters": U, "bytes_per_gpu_per_step": int(per_gpu),
             "gbs_per_gpu": round(per_gpu / (ms * 1e-3) / 1e9, 1),
@@ -670,6 +941,11 @@ def main():
     ap.add_argument("--prefill-mix", action="store_true", help="time config 2's prefill mix per kernel and exit")
     ap.add_argument("--config3", action="store_true",
                     help="time BASELINE config 3 (13B, r64, T=512, tensor-parallel over the N GPUs) and exit")
+    ap.add_argument("--row-mode", choices=["partial", "fused", "nccl"], default="partial",
+                    help="row-parallel layers under tensor parallelism (N > 1)")
+    ap.add_argument("--per-kind", action="store_true", help="also time column/row-parallel launches apart at N = 1")
+    ap.add_argument("--no-extras", action="store_true",
+                    help="only the headline step (no flatness, config 2 / 3, prefill or fused-slice keys)")
     args = ap.parse_args()
     if args.profile_case:
         profile_case(args)
@@ -706,11 +982,19 @@ def main():
         os.environ.setdefault("NCCL_DEBUG", "WARN")  # keep NCCL's banner off stdout (one JSON line)
         torch.distributed.init_process_group("nccl", device_id=torch.device("cuda", local_rank))
     eng, result = run_ours(args, rank, world, local_rank)
-    if rank == 0 and world == 1:
+    device = torch.device("cuda", local_rank)
+    if not args.no_extras:
+        # config 3 (13B, r64, T = 512) on the same N GPUs, in the same line
+        result["config3"] = config3(args, rank, world, local_rank)
+    if rank == 0 and world == 1 and not args.no_extras:
         if not args.no_sweep:
-            result["flatness"] = sweep_resident(eng, torch.device("cuda", local_rank), [1, 8, 64, 128, 512],
-                                                max(3, args.steps // 4))
-        result["fused_slices"] = fused_slices(eng, torch.device("cuda", local_rank), max(3, args.steps // 2))
+            result["flatness"] = sweep_resident(eng, device, [1, 8, 64, 128, 512], max(3, args.steps // 4))
+            result["config2_sweep"] = config2_sweep(device)
+        result["fused_slices"] = fused_slices(eng, device, max(3, args.steps // 2))
+        result["strict_order"] = strict_order(device, max(3, args.steps // 2))
+        result["fp16_step"] = fp16_step(device, max(3, args.steps // 2))
+        result["prefill_mix"] = prefill_mix(device)
+    if rank == 0 and world == 1:
         dt, threads = cpu_reference_layers(args.cpu_layers)
         result["cpu_baseline"] = {"value": round(dt * LAYERS * 1e6, 1), "unit": "us/step", "cores": threads,
                                   "kind": "port",

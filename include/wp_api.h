@@ -69,6 +69,9 @@ typedef struct wp_config {
                                 "split", "dec", "tc"), 1 = clustered decode (mma.sync),
                                 2 = balanced decode ("split": one CTA per SM, equal
                                 one-stage items), 3 = clustered tcgen05 */
+  int32_t peer_wait_ms;      /* bound of each in-kernel wait on a tensor-parallel peer
+                                (wp_add_lora_row_parallel); 0 = 5000 ms. On expiry the
+                                kernel sets WP_ERR_DEVICE_TIMEOUT's flag and returns. */
 } wp_config;
 
 /* One entry of the segment table, as read back by wp_read_seg_table.

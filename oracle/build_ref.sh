@@ -2,10 +2,12 @@
 # TEST INFRASTRUCTURE ONLY. Builds oracle/_ref/libwpref.so from the
 # reference's own CUDA kernel sources, where they lie in the reference
 # checkout (never copied into this repository), plus oracle/ref_shim.cu.
-# Usage: oracle/build_ref.sh [REFERENCE_ROOT]   (default: /root/reference)
+# Usage: oracle/build_ref.sh [REFERENCE_ROOT]
+# (default: $WP_REFERENCE_ROOT, else a checkout named "reference" beside
+# this repository's directory)
 set -euo pipefail
-REF="${1:-${WP_REFERENCE_ROOT:-/root/reference}}"
 HERE="$(cd "$(dirname "${BASH_SOURCE[0]}")" && pwd)"
+REF="${1:-${WP_REFERENCE_ROOT:-$HERE/../../reference}}"
 OUT="$HERE/_ref"
 K="$REF/csrc/kernels"
 if [ ! -f "$K/warp_pipe_r32.cu" ]; then

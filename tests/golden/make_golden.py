@@ -1,7 +1,8 @@
 """Generate tests/golden/golden_apply.npz with the REFERENCE's own Python oracle.
 
 Run in a checkout where the reference (vac014/AdapterSlotsPlusPlus) is
-available (default /root/reference, or WP_REFERENCE_ROOT):
+available (WP_REFERENCE_ROOT, else a checkout named "reference" beside this
+repository's directory):
 
     python tests/golden/make_golden.py
 
@@ -36,7 +37,7 @@ from tests.golden.cases import (  # noqa: E402
 )
 
 COL_STRIDE = 8  # column sample of the small cases (row sums cover every column)
-REF = Path(os.environ.get("WP_REFERENCE_ROOT", "/root/reference"))
+REF = Path(os.environ.get("WP_REFERENCE_ROOT", str(Path(__file__).resolve().parents[3] / "reference")))
 
 
 def load_reference_functions():

@@ -1,12 +1,16 @@
 """Tensor-parallel apply on 2 GPUs (one process per GPU, NCCL for the
-plumbing): column-parallel layers, row-parallel layers through the NCCL
-all-reduce path and through the fused peer-memory exchange
-(wp_add_lora_row_parallel), all against the unsharded oracle result, plus the
-bounded wait of the exchange when the peer never joins (error status, no
-hang). Skipped on a box with fewer than 2 GPUs."""
+plumbing): column-parallel layers, row-parallel layers in all three modes --
+"partial" (each rank's share added into its partial output, summed by an
+all-reduce as the base layer's would), "nccl" (all-reduce of the [T, r]
+partials) and "fused" (the in-kernel peer-memory exchange,
+wp_add_lora_row_parallel) -- all against the unsharded oracle result; the
+fused exchange across alternating empty and non-empty launches with one rank
+lagging; and the bounded wait of the exchange when the peer never joins
+(error status, no hang). Skipped on a box with fewer than 2 GPUs."""
 
 import os
 import socket
+import time
 
 import pytest
 import torch
@@ -49,10 +53,35 @@ def _worker(rank, port, q, mode):
     try:
         wa, wb, x, y, idx = _inputs()
         scale = 0.5
-        eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096), device=dev)
+        eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, peer_wait_ms=300 if mode == "timeout" else 0),
+                             device=dev)
         assert eng.build_seg_bounds(idx.to(dev))
+        if mode == "alternate":
+            # launches without segments advance the exchange epoch too; rank 1
+            # lags on the host before every launch, so rank 0 runs ahead and
+            # must not overwrite a mailbox slot rank 1 still reads
+            tpa = tp.TensorParallelApply(eng, row_mode="fused")
+            empty = torch.full((T,), -1, dtype=torch.int64, device=dev)
+            full = oa.add_lora_grouped(y, x, wa, wb, scale, idx)
+            rms = float(full.pow(2).mean().sqrt())
+            errs = []
+            xs, was, wbd = tp.shard_row_input(x, rank, WORLD).to(dev), tp.shard_row(wa, rank, WORLD).to(dev), wb.to(dev)
+            for i in range(8):
+                if rank == 1:
+                    time.sleep(0.05)
+                eng.build_seg_bounds(empty if i % 3 else idx.to(dev))
+                yd = y.to(dev)
+                assert tpa.row_parallel(yd, xs, was, wbd, scale)
+                if i % 3 == 0:
+                    torch.cuda.synchronize(dev)
+                    errs.append(float((yd.float().cpu() - full).abs().max()) / rms)
+            torch.cuda.synchronize(dev)
+            q.put((rank, (errs, eng.device_error(clear=True))))
+            dist.barrier()
+            tpa.close()
+            return
         if mode == "timeout":
-            tpa = tp.TensorParallelApply(eng, fused=True)
+            tpa = tp.TensorParallelApply(eng, row_mode="fused")
             if rank == 0:
                 # the peer never runs its half: the wait gives up after its bound
                 yd = y.to(dev)
@@ -67,14 +96,23 @@ def _worker(rank, port, q, mode):
             return
         full = oa.add_lora_grouped(y, x, wa, wb, scale, idx)
         out = {}
-        for fused in (True, False):
-            tpa = tp.TensorParallelApply(eng, fused=fused)
-            # row-parallel: this rank's d slice of x and A, full B, replicated y
+        for fused in ("fused", "nccl", "partial"):
+            tpa = tp.TensorParallelApply(eng, row_mode=fused)
+            # row-parallel: this rank's d slice of x and A, full B
             yd = y.to(dev)
             for _ in range(3):  # repeated launches: the exchange epochs advance
-                yd.copy_(y.to(dev))
+                if fused == "partial":
+                    # this rank's partial output (the base term on rank 0 only),
+                    # completed by the all-reduce the base layer runs
+                    yd.copy_(y.to(dev) if rank == 0 else torch.zeros_like(y, device=dev))
+                else:
+                    yd.copy_(y.to(dev))
                 assert tpa.row_parallel(yd, tp.shard_row_input(x, rank, WORLD).to(dev),
                                         tp.shard_row(wa, rank, WORLD).to(dev), wb.to(dev), scale)
+            if fused == "partial":
+                ysum = yd.float()
+                dist.all_reduce(ysum)
+                yd = ysum
             torch.cuda.synchronize(dev)
             out[("row", fused)] = yd.float().cpu()
             # column-parallel: this rank's output columns
@@ -90,7 +128,7 @@ def _worker(rank, port, q, mode):
             ref = full if kind == "row" else full[:, a0:a1]
             rms = float(ref.pow(2).mean().sqrt())
             res[(kind, fused)] = float((v - ref).abs().max()) / rms
-        q.put((rank, (res, err, out[("row", True)])))
+        q.put((rank, (res, err, out[("row", "fused")], out[("row", "partial")])))
     finally:
         dist.destroy_process_group()
 
@@ -112,15 +150,27 @@ def _run(mode):
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
 def test_tp2_row_and_column_parallel_match_unsharded():
     got = _run("parity")
-    rows = []
+    rows, parts = [], []
     for rank in range(WORLD):
-        res, err, row = got[rank]
+        res, err, row, part = got[rank]
         assert err == 0, f"rank {rank}: device error {err}"
+        assert len(res) == 6
         for key, rel in res.items():
             assert rel <= 2e-2, f"rank {rank} {key}: max_abs_err / rms = {rel:.3e}"
         rows.append(row)
+        parts.append(part)
     # every rank ends with the same full result (ranks sum in one order)
     assert torch.equal(rows[0], rows[1])
+    assert torch.equal(parts[0], parts[1])
+
+
+@pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
+def test_tp2_exchange_survives_empty_launches_and_lag():
+    got = _run("alternate")
+    for rank in range(WORLD):
+        errs, err = got[rank]
+        assert err == 0, f"rank {rank}: device error {err}"
+        assert len(errs) == 3 and all(e <= 2e-2 for e in errs), errs
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < WORLD, reason="needs 2 GPUs")
