@@ -261,6 +261,53 @@ def test_graph_capture_replays_live_table(engine):
         assert_close(y_buf, ref, dtype, f"replay {indices[:3]}")
 
 
+def test_graph_survives_scratch_growth(engine):
+    """A graph captured with a small call keeps working after an eager call
+    with a larger T and d has grown the kernels' scratch (the outgrown
+    buffers stay allocated while graphs may hold their addresses)."""
+    dtype = torch.bfloat16
+    g = torch.Generator().manual_seed(5)
+    small_idx = [0] * 5 + [1] * 11
+    wa = (torch.randn(4, 1, 32, 1024, generator=g) * 0.02).to(dtype).cuda()
+    wb = (torch.randn(4, 1, 1024, 32, generator=g) * 0.02).to(dtype).cuda()
+    x = (torch.randn(16, 1024, generator=g) * 0.1).to(dtype).cuda()
+    y_base = (torch.randn(16, 1024, generator=g) * 0.1).to(dtype).cuda()
+    y_buf = y_base.clone()
+    idx_buf = torch.tensor(small_idx, dtype=torch.int64, device="cuda")
+    assert engine.build_seg_bounds(idx_buf)
+    s = torch.cuda.Stream()
+    s.wait_stream(torch.cuda.current_stream())
+    with torch.cuda.stream(s):
+        engine.add_lora_packed(y_buf, x, wa, wb, 0.5)
+    torch.cuda.current_stream().wait_stream(s)
+    torch.cuda.synchronize()
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.graph(graph):
+        assert engine.add_lora_packed(y_buf, x, wa, wb, 0.5)
+    # an eager call with far more tokens and a wider d grows the scratch
+    big_idx = sorted(zipf_ids(8, 4096, seed=2).tolist())
+    yb, refb = live_case(engine, big_idx, dtype, 11008, 1024, 32, n_adapters=8, seed=6)
+    assert_close(yb, refb, dtype, "large eager call")
+    del yb
+    torch.cuda.synchronize()
+    assert engine.build_seg_bounds(idx_buf)
+    for _ in range(2):
+        y_buf.copy_(y_base)
+        graph.replay()
+        torch.cuda.synchronize()
+        ref = oa.add_lora_grouped(y_base.cpu(), x.cpu(), wa.cpu(), wb.cpu(), 0.5, torch.tensor(small_idx))
+        assert_close(y_buf, ref, dtype, "replay after growth")
+
+
+def test_small_and_empty_calls(engine):
+    """One token, one adapter; every token without an adapter; a run of 33."""
+    for idx in ([3], [-1] * 40, [2] * 33, [0, -1, 1]):
+        for dtype in DTYPES:
+            yd, ref = live_case(engine, idx, dtype, 512, 768, 16, n_adapters=4, seed=len(idx))
+            assert_close(yd, ref, dtype, f"idx {idx[:4]}")
+    assert engine.device_error(clear=True) == 0
+
+
 # ---- registry path: build_segments + shrink + expand --------------------------
 
 @pytest.mark.parametrize("rank", [8, 16, 32, 64])
