@@ -48,6 +48,26 @@ class WpConfig(ctypes.Structure):
     ]
 
 
+class WpBridge(ctypes.Structure):
+    """wp_bridge (include/wp_api.h): one scheduler tick."""
+
+    _fields_ = [
+        ("whittle_scores", ctypes.c_float * 64),
+        ("t_remaining_ms", ctypes.c_float * 64),
+        ("gwar_pred_next3", ctypes.c_float * 64),
+        ("lambda_hat", ctypes.c_float * 64),
+        ("burst_active", ctypes.c_uint8 * 64),
+        ("promo_eligible", ctypes.c_uint8 * 64),
+        ("is_hot", ctypes.c_uint8 * 64),
+        ("prefetch_ready", ctypes.c_uint8 * 64),
+        ("tile_size_code", ctypes.c_uint8 * 64),
+        ("step_id", ctypes.c_uint32),
+        ("num_active_adapters", ctypes.c_uint32),
+        ("num_segments", ctypes.c_uint32),
+        ("global_load", ctypes.c_float),
+    ]
+
+
 class WpSegment(ctypes.Structure):
     _fields_ = [("adapter_id", ctypes.c_int32), ("token_start", ctypes.c_int32), ("token_count", ctypes.c_int32)]
 
@@ -103,6 +123,22 @@ SIGNATURES = {
     "wp_tp_mailbox_close": (_int, [_vp]),
     "wp_add_lora_row_parallel": (_int, [_vp, _vp, _vp, _vp, _i64, _vp, _i64, _i32, _f32, _i32, _i32, _i32, _i32, _i64,
                                         _i64, _i32, _i32, _vp]),
+    "wp_pool_create": (_int, [_vp, _i32, _i32, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32), _i32, _i32,
+                              ctypes.POINTER(_vp)]),
+    "wp_pool_destroy": (_int, [_vp]),
+    "wp_pool_layout": (_int, [_vp, _i32, ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_i64)]),
+    "wp_pool_stack": (_int, [_vp, _i32, ctypes.POINTER(_vp), ctypes.POINTER(_vp), ctypes.POINTER(_i64)]),
+    "wp_pool_register_host": (_int, [_vp, _i32, _vp]),
+    "wp_pool_evict": (_int, [_vp, _i32]),
+    "wp_pool_prefetch": (_i32, [_vp, _i32]),
+    "wp_pool_is_ready": (_i32, [_vp, _i32]),
+    "wp_pool_release": (_int, [_vp, _i32]),
+    "wp_pool_prepare": (_int, [_vp, ctypes.POINTER(_i32), _i32, _vp]),
+    "wp_pool_stats": (_int, [_vp, ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_i32)]),
+    "wp_build_seg_bounds_pool": (_int, [_vp, _vp, _vp, _i32, _i32, _vp]),
+    "wp_write_bridge": (_int, [_vp, ctypes.POINTER(WpBridge)]),
+    "wp_read_bridge": (_int, [_vp, ctypes.POINTER(WpBridge)]),
+    "wp_read_bridge_kernel": (_int, [_vp, ctypes.POINTER(ctypes.c_float), _i32, ctypes.POINTER(_i32)]),
 }
 
 _LIB = None

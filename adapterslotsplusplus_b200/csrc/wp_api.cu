@@ -15,6 +15,7 @@
 #include <cstdio>
 #include <cstdlib>
 #include <cstring>
+#include <memory>
 #include <string>
 #include <unordered_map>
 #include <vector>
@@ -133,6 +134,11 @@ struct wp_handle {
   int mail_world = 0, mail_rank = 0, mail_tmax = 0;
   int* d_tp_seq = nullptr;
   bool tp_exchange = false;  // set for the duration of one row-parallel launch
+
+  // scheduler bridge: page-locked, mapped into the device address space
+  wp_bridge* bridge = nullptr;
+  wp_bridge* d_bridge = nullptr;  // device alias of `bridge`
+  float* d_bridge_out = nullptr;  // readback kernel output [WP_BRIDGE_MAX + 3]
 };
 
 namespace {
@@ -425,6 +431,8 @@ int wp_destroy(wp_handle* h) {
   for (void* p : h->retired) cudaFree(p);
   cudaFree(h->d_sync);
   cudaFree(h->d_plan);
+  if (h->bridge) cudaFreeHost(h->bridge);
+  cudaFree(h->d_bridge_out);
   if (h->h_nseg) cudaFreeHost(h->h_nseg);
   if (h->nseg_ready) cudaEventDestroy(h->nseg_ready);
   for (int b = 0; b < 2; ++b)
@@ -1428,3 +1436,416 @@ extern "C" int wp_tp_destroy(wp_handle* h) {
   }
   return WP_OK;
 }
+
+// ---- adapter pool (live path over a pinned-host store) -------------------------
+//
+// The reference stages host-store adapters only for its registry path
+// (StagingBufferPool, csrc/memory/staging_buffer.h:29-105; prefetch_adapter,
+// csrc/pybind/warp_pipe_bindings.cpp:46-64), and its live DSAK path reads
+// only device stacks (warp_pipe_r32.cu:263-269). The pool gives the live
+// path the same store: a tenant's adapter for every LoRA projection of a
+// model (one pinned host blob per adapter) is paged into one of num_slots
+// GPU slots, and the slots of projection p form the stacked tensors the
+// live apply takes (A_p at slot * slot_bytes + a_off[p], B_p likewise). The
+// segmenter translates adapter ids to slots through a device map, so the
+// apply kernels run unchanged.
+
+struct wp_pool {
+  wp_handle* h = nullptr;
+  int32_t num_slots = 0, num_proj = 0, rank = 0, dtype = 0, max_adapters = 0;
+  std::vector<int32_t> d, o;
+  std::vector<int64_t> a_off, b_off;  // byte offsets of projection p inside a slot
+  int64_t slot_bytes = 0;
+  char* dev = nullptr;  // [num_slots][slot_bytes]
+  std::unordered_map<int32_t, const void*> host;  // adapter id -> caller's pinned blob (slot layout)
+  struct PSlot {
+    int32_t adapter = -1;
+    cudaEvent_t ready = nullptr;
+    bool issued = false;
+    bool pinned = false;  // held by wp_pool_prefetch until wp_pool_release
+    uint64_t last_use = 0;  // step (prepare generation) that last read the slot; 0 = never
+  };
+  std::vector<PSlot> slots;
+  std::vector<int32_t> map_host;  // adapter id -> slot (-1: not resident)
+  int32_t* d_map = nullptr;
+  int32_t* h_map[2] = {nullptr, nullptr};  // pinned upload buffers
+  cudaEvent_t map_up[2] = {nullptr, nullptr};
+  int map_buf = 0;
+  cudaStream_t side = nullptr;  // copies
+  // step_done[g % kRing] is recorded on the step stream when prepare(g + 1)
+  // starts, i.e. after every kernel of step g was queued
+  static constexpr int kRing = 8;
+  cudaEvent_t step_done[kRing] = {};
+  uint64_t gen = 0;  // steps prepared so far
+  cudaStream_t last_stream = nullptr;
+  int64_t copies = 0, bytes = 0;
+};
+
+namespace {
+
+int pool_fail(wp_pool* p, int code, const char* fmt, ...) {
+  char buf[512];
+  va_list ap;
+  va_start(ap, fmt);
+  vsnprintf(buf, sizeof(buf), fmt, ap);
+  va_end(ap);
+  if (p && p->h)
+    p->h->err = buf;
+  else
+    g_err = buf;
+  return code;
+}
+
+int pool_find(const wp_pool* p, int32_t id) {
+  if (id < 0 || id >= p->max_adapters) return -1;
+  return p->map_host[id];
+}
+
+// A slot for a new adapter: a free one, else the least recently used that is
+// neither pinned nor read by the step being prepared or run (`busy_gen`).
+int pool_victim(wp_pool* p, uint64_t busy_gen) {
+  int best = -1;
+  uint64_t best_use = ~0ull;
+  for (int i = 0; i < p->num_slots; ++i) {
+    const wp_pool::PSlot& s = p->slots[i];
+    if (s.adapter < 0) return i;
+    if (s.pinned || s.last_use >= busy_gen) continue;
+    if (s.last_use < best_use) {
+      best_use = s.last_use;
+      best = i;
+    }
+  }
+  return best;
+}
+
+// Copies adapter `id` into slot `si` on the side stream. A slot that a
+// previous step read is overwritten only after that step's kernels (the side
+// stream waits on the event recorded after them).
+int pool_issue(wp_pool* p, int si, int32_t id) {
+  wp_pool::PSlot& s = p->slots[si];
+  if (s.adapter >= 0 && s.adapter < p->max_adapters) p->map_host[s.adapter] = -1;
+  if (s.last_use > 0) {
+    // step_done[j % kRing] holds the event of step j or of a later step
+    // j + m * kRing (recorded further down the stream): waiting on it covers
+    // every kernel of step j
+    if (s.last_use >= p->gen) return pool_fail(p, WP_ERR_INVALID, "pool: slot %d is read by the current step", si);
+    WP_CUDA(p->h, cudaStreamWaitEvent(p->side, p->step_done[s.last_use % wp_pool::kRing], 0));
+  }
+  WP_CUDA(p->h, cudaMemcpyAsync(p->dev + static_cast<int64_t>(si) * p->slot_bytes, p->host[id], p->slot_bytes,
+                                cudaMemcpyHostToDevice, p->side));
+  WP_CUDA(p->h, cudaEventRecord(s.ready, p->side));
+  s.adapter = id;
+  s.issued = true;
+  s.pinned = false;
+  p->map_host[id] = si;
+  ++p->copies;
+  p->bytes += p->slot_bytes;
+  return WP_OK;
+}
+
+}  // namespace
+
+extern "C" {
+
+int wp_pool_create(wp_handle* h, int32_t num_slots, int32_t num_proj, int32_t rank, const int32_t* d,
+                   const int32_t* o, int32_t dtype, int32_t max_adapters, wp_pool** out) {
+  if (!h || !out) return fail(nullptr, WP_ERR_INVALID, "pool_create: NULL handle or output");
+  if (num_slots < 1 || num_proj < 1 || !d || !o || max_adapters < 1 || !rank_ok(rank) || !dtype16(dtype))
+    return fail(h, WP_ERR_INVALID, "pool_create: bad sizes, rank or dtype");
+  DeviceGuard dg(h->device);
+  auto p = std::make_unique<wp_pool>();
+  p->h = h;
+  p->num_slots = num_slots;
+  p->num_proj = num_proj;
+  p->rank = rank;
+  p->dtype = dtype;
+  p->max_adapters = max_adapters;
+  int64_t off = 0;
+  for (int i = 0; i < num_proj; ++i) {
+    if (d[i] < 1 || o[i] < 1) return fail(h, WP_ERR_INVALID, "pool_create: projection %d has no size", i);
+    p->d.push_back(d[i]);
+    p->o.push_back(o[i]);
+    p->a_off.push_back(off);
+    off += (static_cast<int64_t>(rank) * d[i] * 2 + 255) / 256 * 256;
+    p->b_off.push_back(off);
+    off += (static_cast<int64_t>(o[i]) * rank * 2 + 255) / 256 * 256;
+  }
+  p->slot_bytes = off;
+  cudaError_t e;
+  if ((e = cudaMalloc(&p->dev, static_cast<size_t>(p->slot_bytes) * num_slots)) != cudaSuccess)
+    return fail(h, WP_ERR_CUDA, "pool_create: %zu bytes of slots: %s", static_cast<size_t>(p->slot_bytes) * num_slots,
+                cudaGetErrorString(e));
+  cudaMemset(p->dev, 0, static_cast<size_t>(p->slot_bytes) * num_slots);
+  if ((e = cudaMalloc(&p->d_map, sizeof(int32_t) * max_adapters)) != cudaSuccess)
+    return fail(h, WP_ERR_CUDA, "pool_create: slot map: %s", cudaGetErrorString(e));
+  cudaMemset(p->d_map, 0xff, sizeof(int32_t) * max_adapters);
+  for (int b = 0; b < 2; ++b) {
+    if ((e = cudaHostAlloc(&p->h_map[b], sizeof(int32_t) * max_adapters, cudaHostAllocDefault)) != cudaSuccess)
+      return fail(h, WP_ERR_CUDA, "pool_create: map upload buffer: %s", cudaGetErrorString(e));
+    cudaEventCreateWithFlags(&p->map_up[b], cudaEventDisableTiming);
+  }
+  for (auto& ev : p->step_done) cudaEventCreateWithFlags(&ev, cudaEventDisableTiming);
+  if ((e = cudaStreamCreateWithFlags(&p->side, cudaStreamNonBlocking)) != cudaSuccess)
+    return fail(h, WP_ERR_CUDA, "pool_create: copy stream: %s", cudaGetErrorString(e));
+  p->slots.resize(num_slots);
+  for (auto& s : p->slots) cudaEventCreateWithFlags(&s.ready, cudaEventDisableTiming);
+  p->map_host.assign(max_adapters, -1);
+  *out = p.release();
+  return WP_OK;
+}
+
+int wp_pool_destroy(wp_pool* p) {
+  if (!p) return WP_OK;
+  DeviceGuard dg(p->h->device);
+  if (p->side) cudaStreamSynchronize(p->side);
+  cudaDeviceSynchronize();
+  for (auto& s : p->slots)
+    if (s.ready) cudaEventDestroy(s.ready);
+  for (auto& ev : p->step_done)
+    if (ev) cudaEventDestroy(ev);
+  for (int b = 0; b < 2; ++b) {
+    if (p->h_map[b]) cudaFreeHost(p->h_map[b]);
+    if (p->map_up[b]) cudaEventDestroy(p->map_up[b]);
+  }
+  cudaFree(p->d_map);
+  cudaFree(p->dev);
+  if (p->side) cudaStreamDestroy(p->side);
+  delete p;
+  return WP_OK;
+}
+
+int wp_pool_layout(wp_pool* p, int32_t proj, int64_t* a_off, int64_t* b_off, int64_t* slot_bytes) {
+  if (!p || proj < 0 || proj >= p->num_proj) return fail(p ? p->h : nullptr, WP_ERR_INVALID, "pool_layout: bad projection");
+  if (a_off) *a_off = p->a_off[proj];
+  if (b_off) *b_off = p->b_off[proj];
+  if (slot_bytes) *slot_bytes = p->slot_bytes;
+  return WP_OK;
+}
+
+int wp_pool_stack(wp_pool* p, int32_t proj, void** wa, void** wb, int64_t* stride0) {
+  if (!p || proj < 0 || proj >= p->num_proj) return fail(p ? p->h : nullptr, WP_ERR_INVALID, "pool_stack: bad projection");
+  if (wa) *wa = p->dev + p->a_off[proj];
+  if (wb) *wb = p->dev + p->b_off[proj];
+  if (stride0) *stride0 = p->slot_bytes / 2;  // elements of the 16-bit type
+  return WP_OK;
+}
+
+int wp_pool_register_host(wp_pool* p, int32_t adapter_id, const void* blob) {
+  if (!p) return fail(nullptr, WP_ERR_INVALID, "pool_register_host: NULL pool");
+  if (adapter_id < 0 || adapter_id >= p->max_adapters)
+    return pool_fail(p, WP_ERR_INVALID, "pool_register_host: adapter id %d outside [0, %d)", adapter_id, p->max_adapters);
+  if (!blob) return pool_fail(p, WP_ERR_INVALID, "pool_register_host: NULL blob");
+  cudaPointerAttributes at{};
+  if (cudaPointerGetAttributes(&at, blob) != cudaSuccess || at.type != cudaMemoryTypeHost) {
+    cudaGetLastError();
+    return pool_fail(p, WP_ERR_INVALID, "pool_register_host: the blob must be page-locked host memory");
+  }
+  // re-registering a resident adapter drops its slot copy
+  const int si = pool_find(p, adapter_id);
+  if (si >= 0 && !(p->slots[si].last_use >= p->gen && p->gen > 0)) {
+    p->slots[si].adapter = -1;
+    p->slots[si].issued = false;
+    p->slots[si].pinned = false;
+    p->map_host[adapter_id] = -1;
+  }
+  p->host[adapter_id] = blob;
+  return WP_OK;
+}
+
+int wp_pool_evict(wp_pool* p, int32_t adapter_id) {
+  if (!p) return fail(nullptr, WP_ERR_INVALID, "pool_evict: NULL pool");
+  const int si = pool_find(p, adapter_id);
+  if (si >= 0) {
+    if (p->slots[si].last_use >= p->gen && p->gen > 0)
+      return pool_fail(p, WP_ERR_INVALID, "pool_evict: adapter %d is read by the current step", adapter_id);
+    p->slots[si].adapter = -1;
+    p->slots[si].issued = false;
+    p->slots[si].pinned = false;
+    p->map_host[adapter_id] = -1;
+  }
+  p->host.erase(adapter_id);
+  return WP_OK;
+}
+
+int32_t wp_pool_prefetch(wp_pool* p, int32_t adapter_id) {
+  if (!p || p->host.find(adapter_id) == p->host.end()) return -1;
+  DeviceGuard dg(p->h->device);
+  int si = pool_find(p, adapter_id);
+  if (si < 0) {
+    si = pool_victim(p, p->gen);  // not a slot the current step reads
+    if (si < 0) return -1;
+    if (pool_issue(p, si, adapter_id) != WP_OK) return -1;
+  }
+  p->slots[si].pinned = true;
+  return si;
+}
+
+int32_t wp_pool_is_ready(wp_pool* p, int32_t adapter_id) {
+  if (!p) return 0;
+  const int si = pool_find(p, adapter_id);
+  if (si < 0 || !p->slots[si].issued) return 0;
+  const cudaError_t e = cudaEventQuery(p->slots[si].ready);
+  if (e == cudaErrorNotReady) cudaGetLastError();
+  return e == cudaSuccess ? 1 : 0;
+}
+
+int wp_pool_release(wp_pool* p, int32_t adapter_id) {
+  if (!p) return WP_OK;
+  const int si = pool_find(p, adapter_id);
+  if (si >= 0) p->slots[si].pinned = false;
+  return WP_OK;
+}
+
+int wp_pool_prepare(wp_pool* p, const int32_t* ids, int32_t n, void* stream_v) {
+  if (!p) return fail(nullptr, WP_ERR_INVALID, "pool_prepare: NULL pool");
+  if (n < 0 || (n > 0 && !ids)) return pool_fail(p, WP_ERR_INVALID, "pool_prepare: bad id list");
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  DeviceGuard dg(p->h->device);
+  // the previous step's kernels are all queued before this point
+  if (p->gen > 0) WP_CUDA(p->h, cudaEventRecord(p->step_done[p->gen % wp_pool::kRing], stream));
+  ++p->gen;
+  p->last_stream = stream;
+  int misses = 0;
+  std::vector<int> used;
+  used.reserve(n);
+  for (int i = 0; i < n; ++i) {
+    const int32_t id = ids[i];
+    if (id < 0) continue;  // tokens without an adapter
+    if (p->host.find(id) == p->host.end())
+      return pool_fail(p, WP_ERR_UNKNOWN_ADAPTER, "pool_prepare: adapter %d is not registered", id);
+    int si = pool_find(p, id);
+    if (si < 0) {
+      si = pool_victim(p, p->gen);
+      if (si < 0) return pool_fail(p, WP_ERR_CAPACITY, "pool_prepare: more adapters than free slots in one step");
+      const int rc = pool_issue(p, si, id);
+      if (rc != WP_OK) return rc;
+      ++misses;
+    }
+    if (p->slots[si].last_use != p->gen) {
+      p->slots[si].last_use = p->gen;
+      used.push_back(si);
+    }
+  }
+  // the step's kernels wait for every copy they read (no host sync)
+  for (int si : used) WP_CUDA(p->h, cudaStreamWaitEvent(stream, p->slots[si].ready, 0));
+  // slot map upload through a pinned double buffer
+  const int ub = p->map_buf;
+  p->map_buf ^= 1;
+  WP_CUDA(p->h, cudaEventSynchronize(p->map_up[ub]));
+  std::memcpy(p->h_map[ub], p->map_host.data(), sizeof(int32_t) * p->max_adapters);
+  WP_CUDA(p->h, cudaMemcpyAsync(p->d_map, p->h_map[ub], sizeof(int32_t) * p->max_adapters, cudaMemcpyHostToDevice,
+                                stream));
+  WP_CUDA(p->h, cudaEventRecord(p->map_up[ub], stream));
+  return misses;
+}
+
+int wp_pool_stats(wp_pool* p, int64_t* copies, int64_t* bytes, int32_t* resident) {
+  if (!p) return fail(nullptr, WP_ERR_INVALID, "pool_stats: NULL pool");
+  if (copies) *copies = p->copies;
+  if (bytes) *bytes = p->bytes;
+  if (resident) {
+    int r = 0;
+    for (const auto& s : p->slots) r += s.adapter >= 0 ? 1 : 0;
+    *resident = r;
+  }
+  return WP_OK;
+}
+
+int wp_build_seg_bounds_pool(wp_handle* h, wp_pool* p, const void* idx, int32_t idx_dtype, int32_t T,
+                             void* stream_v) {
+  if (!h || !p || p->h != h) return fail(h, WP_ERR_INVALID, "build_seg_bounds_pool: NULL or foreign pool");
+  if (idx_dtype != WP_DTYPE_I32 && idx_dtype != WP_DTYPE_I64)
+    return fail(h, WP_ERR_INVALID, "build_seg_bounds_pool: token_lora_indices must be int32 or int64");
+  if (T < 0) return fail(h, WP_ERR_INVALID, "build_seg_bounds_pool: negative token count");
+  if (T > h->cfg.max_tokens) return WP_NOT_HANDLED;
+  if (T > 0 && !idx) return fail(h, WP_ERR_INVALID, "build_seg_bounds_pool: NULL indices");
+  DeviceGuard dg(h->device);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (h->plan_g == 0) {
+    int c = 1, g = 1;
+    apply_plan(h, WP_DTYPE_BF16, 32, true, &c, &g);
+    h->plan_g = g / std::max(c, 1);
+  }
+  cudaError_t e = wp::launch_seg_bounds(idx, idx_dtype, T, h->d_live, h->d_live_num, h->d_plan, h->plan_g,
+                                        h->d_run_starts, stream, p->d_map, p->max_adapters, h->d_err);
+  if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "build_seg_bounds_pool launch: %s", cudaGetErrorString(e));
+  ++h->launches;
+  h->last_was_segmenter = true;
+  return WP_OK;
+}
+
+}  // extern "C"
+
+// ---- scheduler bridge ------------------------------------------------------------
+
+namespace wp {
+// One thread per adapter slot: the bridge is read through the device mapping
+// of the host's page-locked copy, as the reference's bridge_ptr is.
+__global__ void bridge_readback_kernel(const wp_bridge* b, float* out) {
+  const uint32_t n = b->num_active_adapters < WP_BRIDGE_MAX ? b->num_active_adapters : WP_BRIDGE_MAX;
+  const uint32_t i = threadIdx.x;
+  if (i < n) out[i] = b->whittle_scores[i];
+  if (i == 0) {
+    out[n] = static_cast<float>(n);
+    out[n + 1] = static_cast<float>(b->num_segments);
+    out[n + 2] = static_cast<float>(b->step_id);
+  }
+}
+}  // namespace wp
+
+namespace {
+int bridge_init(wp_handle* h) {
+  if (h->bridge) return WP_OK;
+  void* p = nullptr;
+  WP_CUDA(h, cudaHostAlloc(&p, sizeof(wp_bridge), cudaHostAllocMapped));
+  std::memset(p, 0, sizeof(wp_bridge));
+  h->bridge = static_cast<wp_bridge*>(p);
+  void* dp = nullptr;
+  WP_CUDA(h, cudaHostGetDevicePointer(&dp, p, 0));
+  h->d_bridge = static_cast<wp_bridge*>(dp);
+  WP_CUDA(h, cudaMalloc(&h->d_bridge_out, sizeof(float) * (WP_BRIDGE_MAX + 3)));
+  return WP_OK;
+}
+}  // namespace
+
+extern "C" {
+
+int wp_write_bridge(wp_handle* h, const wp_bridge* b) {
+  if (!h || !b) return fail(h, WP_ERR_INVALID, "write_bridge: NULL handle or bridge");
+  if (b->num_active_adapters > WP_BRIDGE_MAX)
+    return fail(h, WP_ERR_INVALID, "write_bridge: num_active_adapters %u exceeds WP_MAX_ADAPTERS (%d)",
+                b->num_active_adapters, WP_BRIDGE_MAX);
+  DeviceGuard dg(h->device);
+  const int rc = bridge_init(h);
+  if (rc) return rc;
+  std::memcpy(h->bridge, b, sizeof(wp_bridge));
+  return WP_OK;
+}
+
+int wp_read_bridge(wp_handle* h, wp_bridge* out) {
+  if (!h || !out) return fail(h, WP_ERR_INVALID, "read_bridge: NULL handle or output");
+  if (!h->bridge) {
+    std::memset(out, 0, sizeof(wp_bridge));
+    return WP_OK;
+  }
+  std::memcpy(out, h->bridge, sizeof(wp_bridge));
+  return WP_OK;
+}
+
+int wp_read_bridge_kernel(wp_handle* h, float* out, int32_t cap, int32_t* count) {
+  if (!h) return fail(nullptr, WP_ERR_INVALID, "read_bridge_kernel: NULL handle");
+  DeviceGuard dg(h->device);
+  const int rc = bridge_init(h);
+  if (rc) return rc;
+  wp::bridge_readback_kernel<<<1, WP_BRIDGE_MAX>>>(h->d_bridge, h->d_bridge_out);
+  WP_CUDA(h, cudaGetLastError());
+  ++h->launches;
+  WP_CUDA(h, cudaDeviceSynchronize());
+  const uint32_t n = std::min<uint32_t>(h->bridge->num_active_adapters, WP_BRIDGE_MAX);
+  if (count) *count = static_cast<int32_t>(n + 3);
+  if (out && cap > 0)
+    WP_CUDA(h, cudaMemcpy(out, h->d_bridge_out, sizeof(float) * std::min<int64_t>(cap, n + 3), cudaMemcpyDeviceToHost));
+  return WP_OK;
+}
+
+}  // extern "C"

@@ -185,8 +185,10 @@ int apply_split_max_grid(int dtype, int rank);
 int apply_max_grid(int dtype, int rank, int cluster, bool dec);
 
 // idx_dtype: WP_DTYPE_I32 or WP_DTYPE_I64.
+// slot_map / map_size (optional): translate adapter ids to adapter-pool
+// slots as the table is written (see wp_segment.cu).
 cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs, ClusterPlan* plan,
-                              int plan_g,
-                              int* run_starts, cudaStream_t stream);
+                              int plan_g, int* run_starts, cudaStream_t stream, const int* slot_map = nullptr,
+                              int map_size = 0, int* err = nullptr);
 
 }  // namespace wp

@@ -116,10 +116,15 @@ __device__ void write_cluster_plan(const DevSeg* segs, int nseg, ClusterPlan* pl
   if (tid == 0) plan->hdr = make_int4(mode, nseg, G, helpers);
 }
 
+// slot_map (optional): the adapter pool's device map from adapter id to the
+// slot holding it (-1: not resident); table entries then carry the slot,
+// and a run whose adapter is not resident is dropped with kErrBadSegment
+// raised in *err. Runs are found on the original ids either way.
 template <typename I>
 __global__ void __launch_bounds__(kSegThreads, 1)
     seg_bounds_kernel(const I* __restrict__ idx, int T, DevSeg* __restrict__ segs, int* __restrict__ num_segs,
-                      int* __restrict__ run_starts, ClusterPlan* __restrict__ plan, int plan_g) {
+                      int* __restrict__ run_starts, ClusterPlan* __restrict__ plan, int plan_g,
+                      const int* __restrict__ slot_map, int map_size, int* err) {
   __shared__ int warp_buf[33];
   const int tid = threadIdx.x;
 
@@ -149,7 +154,11 @@ __global__ void __launch_bounds__(kSegThreads, 1)
       const I raw = idx[start];
       if (raw >= 0) {
         id = static_cast<int32_t>(raw);
-        pieces = (len + kSegTokens - 1) / kSegTokens;
+        if (slot_map) {
+          id = raw < static_cast<I>(map_size) ? __ldcg(slot_map + raw) : -1;
+          if (id < 0 && err) atomicOr(err, 2);  // kErrBadSegment: adapter not resident
+        }
+        if (id >= 0) pieces = (len + kSegTokens - 1) / kSegTokens;
       }
     }
     int total;
@@ -174,13 +183,14 @@ __global__ void __launch_bounds__(kSegThreads, 1)
 }
 
 cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs, ClusterPlan* plan,
-                              int plan_g, int* run_starts, cudaStream_t stream) {
+                              int plan_g, int* run_starts, cudaStream_t stream, const int* slot_map, int map_size,
+                              int* err) {
   if (idx_dtype == 4) {
-    seg_bounds_kernel<int64_t><<<1, kSegThreads, 0, stream>>>(static_cast<const int64_t*>(idx), T, segs,
-                                                               num_segs, run_starts, plan, plan_g);
+    seg_bounds_kernel<int64_t><<<1, kSegThreads, 0, stream>>>(static_cast<const int64_t*>(idx), T, segs, num_segs,
+                                                               run_starts, plan, plan_g, slot_map, map_size, err);
   } else {
-    seg_bounds_kernel<int32_t><<<1, kSegThreads, 0, stream>>>(static_cast<const int32_t*>(idx), T, segs,
-                                                               num_segs, run_starts, plan, plan_g);
+    seg_bounds_kernel<int32_t><<<1, kSegThreads, 0, stream>>>(static_cast<const int32_t*>(idx), T, segs, num_segs,
+                                                               run_starts, plan, plan_g, slot_map, map_size, err);
   }
   return cudaGetLastError();
 }

@@ -359,31 +359,46 @@ class WarpPipeEngine:
         return int(self._lib.wp_kernel_launch_count(self._h))
 
     # -- scheduler bridge (engine.py:34-42, 64-69) -------------------------------
-    # The reference keeps Whittle/GWAR scheduler metadata in mapped memory that
-    # no compute kernel reads. Kept callable as host-side state.
+    # One scheduler tick of Whittle / GWAR / arrival-rate state, held in
+    # page-locked memory mapped into the device (wp_write_bridge); the
+    # scheduler-aware prefetch policy (scheduler_bridge.PrefetchPolicy) reads
+    # it back each tick.
+    _BRIDGE_F = ("whittle_scores", "t_remaining_ms", "gwar_pred_next3", "lambda_hat")
+    _BRIDGE_U8 = ("burst_active", "promo_eligible", "is_hot", "tile_size_code")
+
     def write_bridge(self, whittle_scores, t_remaining_ms, gwar_pred_next3, lambda_hat, burst_active,
                      promo_eligible, is_hot, tile_size_code, num_active_adapters, num_segments, step_id,
                      global_load):
         n = int(num_active_adapters)
         if n > 64:
             raise RuntimeError("write_bridge: num_active_adapters exceeds WP_MAX_ADAPTERS")
-
-        def f32(t):
-            return [float(v) for v in torch.as_tensor(t).reshape(-1)[:n].tolist()]
-
-        def u8(t):
-            return [int(v) for v in torch.as_tensor(t).reshape(-1)[:n].tolist()]
-
-        self._bridge = dict(whittle_scores=f32(whittle_scores), t_remaining_ms=f32(t_remaining_ms),
-                            gwar_pred_next3=f32(gwar_pred_next3), lambda_hat=f32(lambda_hat),
-                            burst_active=u8(burst_active), promo_eligible=u8(promo_eligible), is_hot=u8(is_hot),
-                            tile_size_code=u8(tile_size_code), num_active_adapters=n,
-                            num_segments=int(num_segments), step_id=int(step_id), global_load=float(global_load))
+        b = _lib.WpBridge()
+        for name, t in zip(self._BRIDGE_F, (whittle_scores, t_remaining_ms, gwar_pred_next3, lambda_hat)):
+            vals = torch.as_tensor(t).reshape(-1)[:n].float().tolist()
+            getattr(b, name)[:len(vals)] = vals
+        for name, t in zip(self._BRIDGE_U8, (burst_active, promo_eligible, is_hot, tile_size_code)):
+            vals = [int(v) & 0xFF for v in torch.as_tensor(t).reshape(-1)[:n].tolist()]
+            getattr(b, name)[:len(vals)] = vals
+        b.num_active_adapters = n
+        b.num_segments = int(num_segments)
+        b.step_id = int(step_id)
+        b.global_load = float(global_load)
+        self._check(self._lib.wp_write_bridge(self._h, ctypes.byref(b)))
 
     def read_bridge_debug(self):
-        return dict(self._bridge) if self._bridge is not None else {}
+        b = _lib.WpBridge()
+        self._check(self._lib.wp_read_bridge(self._h, ctypes.byref(b)))
+        n = int(b.num_active_adapters)
+        out = {name: list(getattr(b, name))[:n] for name in self._BRIDGE_F + self._BRIDGE_U8}
+        out.update(num_active_adapters=n, num_segments=int(b.num_segments), step_id=int(b.step_id),
+                   global_load=float(b.global_load))
+        return out
 
     def read_bridge_via_kernel(self):
-        b = self._bridge or {"whittle_scores": [], "num_active_adapters": 0, "num_segments": 0, "step_id": 0}
-        return list(b["whittle_scores"]) + [float(b["num_active_adapters"]), float(b["num_segments"]),
-                                            float(b["step_id"])]
+        """[whittle_scores..., n, num_segments, step_id], read on the device by a
+        kernel through the bridge's device mapping (test_scheduler_bridge.py of
+        the reference checks this round trip)."""
+        buf = (ctypes.c_float * 67)()
+        cnt = ctypes.c_int32()
+        self._check(self._lib.wp_read_bridge_kernel(self._h, buf, 67, ctypes.byref(cnt)))
+        return [float(v) for v in buf[:cnt.value]]

@@ -130,7 +130,7 @@ class ClockSampler:
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
-                 "-lms", "200"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+                 "-lms", "50"], stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
             self.thread = threading.Thread(target=self._read, daemon=True)
             self.thread.start()
         except Exception:
@@ -237,12 +237,13 @@ def time_graph(g, pre, iters):
     return start.elapsed_time(end) / iters  # ms
 
 
-def tp_parity(eng, tpa, device, rank, world, scale):
+def tp_parity(eng, tpa, device, rank, world, scale, idx_dev):
     """Tensor-parallel results of layer 0's q (column-parallel), o and down
-    (row-parallel) against the unsharded result of the same library on one
-    GPU, on identical inputs (every rank draws the full weights from one
-    seed and keeps its shard). Row-parallel partial outputs are summed with
-    an all-reduce, as the base layer's all-reduce would. Returns, on every
+    (row-parallel) against an fp32 torch computation of the unsharded call on
+    the same GPU, on identical inputs (every rank draws the full weights from
+    one seed and keeps its shard). Row-parallel partial outputs (bf16) are
+    summed with an all-reduce, as the base layer's all-reduce would, so they
+    carry one more bf16 rounding than a single-GPU call. Returns, on every
     rank, max-abs error / RMS per projection and whether all ranks hold
     bit-identical full outputs."""
     import torch.distributed as dist
@@ -257,8 +258,11 @@ def tp_parity(eng, tpa, device, rank, world, scale):
         wb = torch.randn(RESIDENT, 1, o, RANK, device=device, dtype=torch.bfloat16, generator=g) * 0.02
         x = torch.randn(TOKENS, d, device=device, dtype=torch.bfloat16, generator=g) * 0.1
         y0 = torch.randn(TOKENS, o, device=device, dtype=torch.bfloat16, generator=g) * 0.1
-        ref = y0.clone()
-        assert eng.add_lora_packed(ref, x, wa, wb, scale)
+        # fp32 reference of the unsharded call on this GPU (plain torch)
+        ids = idx_dev.long()
+        h32 = torch.einsum("td,trd->tr", x.float(), wa[ids, 0].float()) * scale
+        ref = y0.float() + torch.einsum("tr,tor->to", h32, wb[ids, 0].float())
+        del h32
         if kind == "col":
             a, b = rank * (o // world), (rank + 1) * (o // world)
             ys = y0[:, a:b].contiguous()
@@ -278,8 +282,8 @@ def tp_parity(eng, tpa, device, rank, world, scale):
                 full = y0.clone()
                 assert tpa.row_parallel(full, shard_row_input(x, rank, world), shard_row(wa, rank, world), wb, scale)
         torch.cuda.synchronize()
-        rms = float(ref.float().pow(2).mean().sqrt())
-        err = float((full.float() - ref.float()).abs().max()) / rms
+        rms = float(ref.pow(2).mean().sqrt())
+        err = float((full.float() - ref).abs().max()) / rms
         # bit-identity across ranks: compare every rank's output with rank 0's
         r0 = full.clone()
         dist.broadcast(r0, src=0)
@@ -289,7 +293,7 @@ def tp_parity(eng, tpa, device, rank, world, scale):
         out[name] = round(err, 6)
     return {"max_abs_err_over_rms": out, "bound": 2e-2, "ok": all(v <= 2e-2 for v in out.values()) and same,
             "ranks_bit_identical": same, "row_mode": tpa.row_mode,
-            "against": "the unsharded add_lora_packed of the same inputs on this GPU"}
+            "against": "fp32 torch result of the unsharded call on the same inputs and GPU"}
 
 
 def run_ours(args, rank, world, local_rank):
@@ -322,7 +326,7 @@ def run_ours(args, rank, world, local_rank):
 
         tpa = TensorParallelApply(eng, row_mode=args.row_mode)
         eng.build_seg_bounds(idx_dev)
-        parity = tp_parity(eng, tpa, device, rank, world, scale)
+        parity = tp_parity(eng, tpa, device, rank, world, scale, idx_dev)
 
     def run(kinds=("col", "row")):
         def f():
@@ -362,10 +366,12 @@ def run_ours(args, rank, world, local_rank):
             n = sum(1 for c in calls if c[0] == kind)
             per_kind[kind] = time_graph(gk, None, args.steps) * 1e3 / n
             del gk
+    outside_ms = ms - ms_apply  # this rank's time outside the apply graph
     if world > 1:
-        t = torch.tensor([ms, ms_apply, per_kind.get("col", 0.0), per_kind.get("row", 0.0)], device=device)
+        t = torch.tensor([ms, ms_apply, per_kind.get("col", 0.0), per_kind.get("row", 0.0), outside_ms],
+                         device=device)
         torch.distributed.all_reduce(t, op=torch.distributed.ReduceOp.MAX)
-        ms, ms_apply, per_kind["col"], per_kind["row"] = t.tolist()
+        ms, ms_apply, per_kind["col"], per_kind["row"], outside_ms = t.tolist()
 
     # e2e through the public API: token ids from pinned host memory, the step,
     # and a read back of one output row, all on the stream, every step.
@@ -468,7 +474,7 @@ def run_ours(args, rank, world, local_rank):
     }
     if per_kind:
         result["per_kind_us_per_launch"] = {k: round(v, 3) for k, v in per_kind.items()}
-        result["per_kind_us_per_launch"]["outside_graph_us_per_step"] = round((ms - ms_apply) * 1e3, 2)
+        result["per_kind_us_per_launch"]["outside_graph_us_per_step"] = round(outside_ms * 1e3, 2)
     if parity is not None:
         result["tp_parity"] = parity
     del g_full, stack, calls
@@ -813,6 +819,160 @@ def config2_sweep(device, iters=5, ranks=(8, 16, 32, 64), residents=(1, 8, 64, 5
                                                          "us_per_call", "gbs", "frac_of_hbm"], "rows": rows}
 
 
+def config4(device, steps: int = 200, warmup: int = 10, seed: int = 4):
+    """multi-tenant draft-LoRA step with adapter churn.
+    Draft shapes: 12 layers, hidden 768, intermediate 3072; every tenant owns
+    a rank-16 LoRA on q, k, v, o, gate, up, down (84 projections, 6.8 MB per
+    tenant). 1024 tenants live in page-locked host memory (one blob each,
+    6.95 GB) behind a 128-slot GPU AdapterPool. A step applies 32 tenants x 8
+    sequences x 4 lookahead tokens = 1024 tokens through all 84 projections
+    (one build_seg_bounds_pool, the 84 calls replayed from a CUDA graph). Cold
+    tenants arrive as a Poisson process at 0.05 per step (default_rng(4)) and
+    replace a random active tenant one step later.
+
+    Two runs of the same arrival sequence: on demand (the step that first
+    uses a cold tenant copies it; the stream waits) and scheduler-aware
+    prefetch (the arrival is written to the bridge as queued (is_hot) and
+    PrefetchPolicy prefetches it on the pool's copy stream while the current
+    step runs). Reports device us per step (CUDA events on the step stream),
+    warm vs cold steps, cold misses and the prefetch-overlap fraction
+    1 - (cold_prefetch - warm) / (cold_on_demand - warm)."""
+    from adapterslotsplusplus_b200 import AdapterPool, WarpPipeConfig, WarpPipeEngine
+    from adapterslotsplusplus_b200.scheduler_bridge import PrefetchPolicy
+
+    layers, hid, inter, r = 12, 768, 3072, 16
+    tenants_total, slots, active_n, T = 1024, 128, 32, 4 * 8 * 32
+    per_layer = [("q", hid, hid, "h"), ("k", hid, hid, "h"), ("v", hid, hid, "h"), ("o", hid, hid, "a"),
+                 ("gate", hid, inter, "h"), ("up", hid, inter, "h"), ("down", inter, hid, "i")]
+    dims = [(d, o) for _ in range(layers) for _, d, o, _ in per_layer]
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    pool = AdapterPool(eng, slots, dims, rank=r, dtype=torch.bfloat16, max_adapters=tenants_total)
+    sb = pool.slot_bytes
+    # host store: one page-locked allocation, one blob per tenant; contents
+    # from 8 random GPU-made blobs (the copies move full-size blobs)
+    host = torch.empty(tenants_total, sb, dtype=torch.uint8, pin_memory=True)
+    g = torch.Generator(device=device).manual_seed(seed)
+    protos = []
+    for _ in range(8):
+        blob = torch.zeros(sb, dtype=torch.uint8, device=device)
+        for (d, o), (a_off, b_off) in zip(dims, pool.layout):
+            blob[a_off:a_off + r * d * 2].copy_((torch.randn(r * d, device=device, generator=g) * 0.02)
+                                                 .bfloat16().view(torch.uint8))
+            blob[b_off:b_off + o * r * 2].copy_((torch.randn(o * r, device=device, generator=g) * 0.02)
+                                                 .bfloat16().view(torch.uint8))
+        protos.append(blob)
+    for i in range(tenants_total):
+        host[i].copy_(protos[i % 8], non_blocking=True)
+    torch.cuda.synchronize()
+    for i in range(tenants_total):
+        pool.register_host(i, host[i])
+    xs = {"h": torch.randn(T, hid, device=device, dtype=torch.bfloat16, generator=g) * 0.1,
+          "a": torch.randn(T, hid, device=device, dtype=torch.bfloat16, generator=g) * 0.1,
+          "i": torch.randn(T, inter, device=device, dtype=torch.bfloat16, generator=g) * 0.1}
+    ys = [torch.zeros(T, o, device=device, dtype=torch.bfloat16) for _, o in dims]
+    srcs = [src for _ in range(layers) for *_, src in per_layer]
+    idx_buf = torch.zeros(T, dtype=torch.int64, device=device)
+
+    def apply_all():
+        for p in range(len(dims)):
+            pool.add_lora(p, ys[p], xs[srcs[p]], 1.0)
+
+    rng = np.random.default_rng(seed)
+    first_active = [int(v) for v in rng.choice(tenants_total, active_n, replace=False)]
+    total_steps = warmup + steps
+    arrivals = rng.poisson(0.05, total_steps)  # cold arrivals announced at each step
+    arrival_ids = [[int(v) for v in rng.choice(tenants_total, k, replace=False)] if k else [] for k in arrivals]
+    replace_at = [[int(v) for v in rng.integers(0, active_n, k)] if k else [] for k in arrivals]
+
+    def token_ids(active):
+        return torch.as_tensor(np.repeat(np.sort(np.asarray(active)), T // active_n), dtype=torch.int64)
+
+    # capture the 84 apply calls once (the pool's stacks never move)
+    pool.prepare(first_active)
+    idx_buf.copy_(token_ids(first_active))
+    pool.build_seg_bounds(idx_buf)
+    graph = capture(apply_all, warm=1)
+
+    def run(mode):
+        # a fresh pool state per mode: the first active set resident (an empty
+        # step first, so no slot counts as read by the step in flight)
+        torch.cuda.synchronize()
+        pool.prepare([])
+        for i in range(tenants_total):
+            pool.evict(i)
+            pool.register_host(i, host[i])
+        pool.prepare(first_active)
+        torch.cuda.synchronize()
+        policy = PrefetchPolicy(pool, budget=8, min_priority=1.0) if mode == "prefetch" else None
+        active = list(first_active)
+        pending = []  # (position, tenant) to swap in at the next step
+        times, cold_flags, misses = [], [], 0
+        evs = [(torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)) for _ in range(total_steps)]
+        for step in range(total_steps):
+            cold = bool(pending)
+            for pos, tid in pending:
+                if tid not in active:
+                    active[pos] = tid
+            pending = []
+            st, en = evs[step]
+            st.record()
+            m = pool.prepare(active)
+            idx_buf.copy_(token_ids(active), non_blocking=True)
+            pool.build_seg_bounds(idx_buf)
+            graph.replay()
+            en.record()
+            if step >= warmup:
+                misses += m
+                cold_flags.append(cold)
+            # the scheduler admits this step's arrivals; they run next step
+            new = [t for t in arrival_ids[step] if t not in active]
+            pending = list(zip(replace_at[step][:len(new)], new))
+            if policy is not None:
+                hot = {t for _, t in pending}
+                n = tenants_total
+                bridge = {"num_active_adapters": n, "is_hot": [1 if i in hot else 0 for i in range(n)],
+                          "whittle_scores": [0.0] * n, "lambda_hat": [0.0] * n, "gwar_pred_next3": [0.0] * n}
+                policy.tick(bridge, protected=active)
+        torch.cuda.synchronize()
+        times = [evs[i][0].elapsed_time(evs[i][1]) * 1e3 for i in range(warmup, total_steps)]
+        warm = [t for t, c in zip(times, cold_flags) if not c]
+        coldt = [t for t, c in zip(times, cold_flags) if c]
+        return {"us_per_step": round(float(np.mean(times)), 1), "warm_us": round(float(np.median(warm)), 1),
+                "cold_us": round(float(np.mean(coldt)), 1) if coldt else None, "cold_steps": len(coldt),
+                "cold_misses": int(misses), "prefetch_issued": policy.issued if policy else 0}
+
+    # one tenant's host -> device copy, alone
+    cs = torch.cuda.Stream()
+    dst = torch.empty(sb, dtype=torch.uint8, device=device)
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    with torch.cuda.stream(cs):
+        e0.record()
+        for i in range(4):
+            dst.copy_(host[i], non_blocking=True)
+        e1.record()
+    torch.cuda.synchronize()
+    copy_us = e0.elapsed_time(e1) * 1e3 / 4
+
+    on_demand = run("on_demand")
+    prefetch = run("prefetch")
+    overlap = None
+    if on_demand["cold_us"] and prefetch["cold_us"] and on_demand["cold_us"] > on_demand["warm_us"]:
+        overlap = 1.0 - (prefetch["cold_us"] - prefetch["warm_us"]) / (on_demand["cold_us"] - on_demand["warm_us"])
+        overlap = round(max(0.0, min(1.0, overlap)), 3)
+    U = active_n
+    step_bytes = 0
+    for d, o in dims:
+        sb_, eb_ = algorithmic_bytes(U, T, d, o, r)
+        step_bytes += sb_ + eb_
+    del graph, ys, xs, pool, host
+    torch.cuda.empty_cache()
+    return {"config": "4 (draft: 12 layers, h768, i3072, 32 tenants x r16 x 7 projections, 1024 tokens; 1024 "
+                      "host tenants, 128 GPU slots, Poisson cold arrivals 0.05/step, default_rng(4))",
+            "steps": steps, "tenant_bytes": sb, "copy_us_per_tenant": round(copy_us, 1),
+            "step_gb": round(step_bytes / 1e9, 3), "on_demand": on_demand, "prefetch": prefetch,
+            "prefetch_overlap_fraction": overlap}
+
+
 def config3(args, rank, world, local_rank):
     """a Llama-2-13B-shaped stack (40 layers, hidden 5120,
     intermediate 13824), rank 64, bf16, 128 resident adapters, 512 tokens,
@@ -941,6 +1101,8 @@ def main():
     ap.add_argument("--prefill-mix", action="store_true", help="time config 2's prefill mix per kernel and exit")
     ap.add_argument("--config3", action="store_true",
                     help="time BASELINE config 3 (13B, r64, T=512, tensor-parallel over the N GPUs) and exit")
+    ap.add_argument("--config4", action="store_true",
+                    help="time BASELINE config 4 (draft-LoRA churn over a pinned-host pool) and exit")
     ap.add_argument("--row-mode", choices=["partial", "fused", "nccl"], default="partial",
                     help="row-parallel layers under tensor parallelism (N > 1)")
     ap.add_argument("--per-kind", action="store_true", help="also time column/row-parallel launches apart at N = 1")
@@ -952,6 +1114,9 @@ def main():
         return
     if args.prefill_mix:
         print(json.dumps(prefill_mix(torch.device("cuda", 0))), flush=True)
+        return
+    if args.config4:
+        print(json.dumps(config4(torch.device("cuda", 0), steps=args.steps * 10)), flush=True)
         return
     args.warmup = max(args.warmup, 3)
 
@@ -994,6 +1159,7 @@ def main():
         result["strict_order"] = strict_order(device, max(3, args.steps // 2))
         result["fp16_step"] = fp16_step(device, max(3, args.steps // 2))
         result["prefill_mix"] = prefill_mix(device)
+        result["config4"] = config4(device)
     if rank == 0 and world == 1:
         dt, threads = cpu_reference_layers(args.cpu_layers)
         result["cpu_baseline"] = {"value": round(dt * LAYERS * 1e6, 1), "unit": "us/step", "cores": threads,

@@ -235,6 +235,51 @@ int wp_add_lora_expand(wp_handle* h, void* y, const void* H, const void* wb_base
                        int32_t num_adapters, int32_t T, int32_t out_features, int32_t rank, int64_t y_ld,
                        int32_t y_offset, int32_t dtype, void* stream);
 
+/* ---- adapter pool: the live path over a pinned-host store --------------- */
+
+/* The reference stages host adapters only for its registry path
+ * (StagingBufferPool, csrc/memory/staging_buffer.h:29-105, fed by
+ * prefetch_adapter, csrc/pybind/warp_pipe_bindings.cpp:46-64); its live
+ * DSAK path reads device stacks only (csrc/kernels/warp_pipe_r32.cu:263-269).
+ * A pool pages whole adapters -- one tenant's A/B of every LoRA projection of
+ * a model (num_proj projections, projection p: A [rank, d[p]], B [o[p], rank])
+ * -- from caller-owned page-locked host blobs into num_slots GPU slots. The
+ * slots of projection p are a stacked tensor that wp_add_lora takes as is
+ * (wp_pool_stack); wp_build_seg_bounds_pool writes the live table with slot
+ * numbers in place of adapter ids. Adapter ids are 0 .. max_adapters-1. */
+typedef struct wp_pool wp_pool;
+int wp_pool_create(wp_handle* h, int32_t num_slots, int32_t num_proj, int32_t rank, const int32_t* d,
+                   const int32_t* o, int32_t dtype, int32_t max_adapters, wp_pool** out);
+int wp_pool_destroy(wp_pool* p);
+/* Byte offsets of projection proj's A and B inside one slot (and inside a
+ * registered host blob, which has the slot's layout), and the slot size. */
+int wp_pool_layout(wp_pool* p, int32_t proj, int64_t* a_off, int64_t* b_off, int64_t* slot_bytes);
+/* Device stacks of projection proj: wa = [num_slots][1][rank][d] and wb =
+ * [num_slots][1][o][rank] with adapter stride stride0 (elements). */
+int wp_pool_stack(wp_pool* p, int32_t proj, void** wa, void** wb, int64_t* stride0);
+/* Registers adapter_id's host blob (page-locked, slot_bytes, the caller keeps
+ * it alive until wp_pool_evict). Re-registering replaces it. */
+int wp_pool_register_host(wp_pool* p, int32_t adapter_id, const void* blob);
+int wp_pool_evict(wp_pool* p, int32_t adapter_id);
+/* Same semantics as wp_prefetch_adapter / wp_is_prefetch_ready /
+ * wp_release_prefetch, for the pool: copies the adapter into a free or least
+ * recently used slot (never one the current step reads) on the pool's copy
+ * stream and holds it until released; -1 for an unknown id or no free slot. */
+int32_t wp_pool_prefetch(wp_pool* p, int32_t adapter_id);
+int32_t wp_pool_is_ready(wp_pool* p, int32_t adapter_id);
+int wp_pool_release(wp_pool* p, int32_t adapter_id);
+/* Starts a step on `stream`: makes every adapter in ids[0..n) resident
+ * (copies for the cold ones are issued now on the copy stream), makes
+ * `stream` wait for the copies it reads (no host sync), and uploads the slot
+ * map. A slot is overwritten only after the kernels of the steps that read it.
+ * Returns the number of adapters copied here (cold misses), or < 0. */
+int wp_pool_prepare(wp_pool* p, const int32_t* ids, int32_t n, void* stream);
+int wp_pool_stats(wp_pool* p, int64_t* copies, int64_t* bytes, int32_t* resident);
+/* wp_build_seg_bounds with the ids translated to the pool's slots (ids that
+ * are not resident are dropped and raise the device error flag). */
+int wp_build_seg_bounds_pool(wp_handle* h, wp_pool* p, const void* token_lora_indices, int32_t idx_dtype, int32_t T,
+                             void* stream);
+
 /* ---- staging slots / prefetch ------------------------------------------ */
 
 /* Replaces WarpPipeExtension::prefetch_adapter (warp_pipe_bindings.cpp:46-57)
@@ -262,6 +307,40 @@ int wp_release_prefetch(wp_handle* h, int32_t adapter_id);
  * reading it synchronises the device; `clear` resets it). */
 int wp_slot_stats(wp_handle* h, int32_t* num_slots, int32_t* slots_in_use);
 int wp_device_error(wp_handle* h, int32_t clear, int32_t* flag);
+
+/* ---- scheduler bridge ----------------------------------------------------- */
+
+/* Scheduler state for one tick, the fields of the reference's
+ * SchedulerKernelBridge (csrc/bridge/warp_pipe_metadata.h:89-104): per adapter
+ * slot i < num_active_adapters (at most WP_BRIDGE_MAX = 64). */
+#define WP_BRIDGE_MAX 64
+typedef struct wp_bridge {
+  float whittle_scores[WP_BRIDGE_MAX];
+  float t_remaining_ms[WP_BRIDGE_MAX];
+  float gwar_pred_next3[WP_BRIDGE_MAX];
+  float lambda_hat[WP_BRIDGE_MAX];
+  uint8_t burst_active[WP_BRIDGE_MAX];
+  uint8_t promo_eligible[WP_BRIDGE_MAX];
+  uint8_t is_hot[WP_BRIDGE_MAX];
+  uint8_t prefetch_ready[WP_BRIDGE_MAX];
+  uint8_t tile_size_code[WP_BRIDGE_MAX];
+  uint32_t step_id;
+  uint32_t num_active_adapters;
+  uint32_t num_segments;
+  float global_load;
+} wp_bridge;
+
+/* Replaces WarpPipeExtension::write_bridge (warp_pipe_bindings.cpp, engine.py:34-42
+ * of the reference): copies one tick's state into the handle's page-locked,
+ * device-mapped bridge. Fails when num_active_adapters > WP_BRIDGE_MAX. */
+int wp_write_bridge(wp_handle* h, const wp_bridge* b);
+/* Replaces read_bridge_debug (engine.py:34-37): host read of the bridge. */
+int wp_read_bridge(wp_handle* h, wp_bridge* out);
+/* Replaces read_bridge_via_kernel (engine.py:39-42): a kernel reads the bridge
+ * through its device mapping and writes [whittle_scores[0..n), n,
+ * num_segments, step_id] (n + 3 floats) to device memory, which is copied to
+ * out (cap floats); *count = n + 3. Synchronises the handle's device. */
+int wp_read_bridge_kernel(wp_handle* h, float* out, int32_t cap, int32_t* count);
 
 /* ---- tracing and launch plan (no counterpart in the reference) --------- */
 
