@@ -933,6 +933,9 @@ def config4(device, steps: int = 200, warmup: int = 10, seed: int = 4):
                 bridge = {"num_active_adapters": n, "is_hot": [1 if i in hot else 0 for i in range(n)],
                           "whittle_scores": [0.0] * n, "lambda_hat": [0.0] * n, "gwar_pred_next3": [0.0] * n}
                 policy.tick(bridge, protected=active)
+            # a serving loop reads the step's output (sampled draft tokens)
+            # before it schedules the next step
+            en.synchronize()
         torch.cuda.synchronize()
         times = [evs[i][0].elapsed_time(evs[i][1]) * 1e3 for i in range(warmup, total_steps)]
         warm = [t for t, c in zip(times, cold_flags) if not c]
