@@ -976,6 +976,54 @@ def config4(device, steps: int = 200, warmup: int = 10, seed: int = 4):
             "prefetch_overlap_fraction": overlap}
 
 
+def draft_step(device, iters: int = 20):
+    """The multi-tenant draft step of config 4 end to end: a 12-layer draft
+    decoder (hidden 768, 12 heads, intermediate 3072, LM head 32000; random
+    init, bf16) over 32 tenants x 8 sequences x 4 lookahead tokens = 1024
+    tokens, every projection's draft-LoRA (rank 16) applied by one grouped
+    call over a 128-slot AdapterPool, the step replayed from a CUDA graph
+    (adapterslotsplusplus_b200/draft.py). Device us per draft step: base
+    model only, with the grouped LoRA, and with a plain-torch per-token
+    gather of the same adapters (the stock path it replaces)."""
+    from adapterslotsplusplus_b200 import AdapterPool, WarpPipeConfig, WarpPipeEngine
+    from adapterslotsplusplus_b200.draft import DraftDecoder
+
+    tenants, seqs, la, r = 32, 8, 4, 16
+    T = tenants * seqs * la
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    model = DraftDecoder(layers=12, hidden=768, heads=12, inter=3072, vocab=32000, device=device)
+    dims = model.dims()
+    pool = AdapterPool(eng, 128, dims, rank=r, max_adapters=1024)
+    g = torch.Generator(device=device).manual_seed(5)
+    A = [torch.randn(tenants, r, d, device=device, generator=g).mul_(0.02).bfloat16() for d, _ in dims]
+    B = [torch.randn(tenants, o, r, device=device, generator=g).mul_(0.02).bfloat16() for _, o in dims]
+    blobs = []
+    for t in range(tenants):
+        blob = torch.empty(pool.slot_bytes, dtype=torch.uint8, pin_memory=True)
+        pool.fill(blob, [(A[p][t].cpu(), B[p][t].cpu()) for p in range(len(dims))])
+        pool.register_host(t, blob)
+        blobs.append(blob)
+    ids = torch.as_tensor(np.repeat(np.arange(tenants), seqs * la), dtype=torch.int64, device=device)
+    tl = {"ids": ids, "A": A, "B": B}
+    x = torch.randn(T, 768, device=device, generator=g).mul_(0.5).bfloat16()
+    pool.prepare(ids.tolist())
+    pool.build_seg_bounds(ids)
+    out = {}
+    for mode in ("none", "pool", "torch"):
+        gr = capture(lambda: model.forward(x, la, lora=mode, pool=pool, scale=1.0, torch_lora=tl), warm=1)
+        for _ in range(3):
+            gr.replay()
+        out[mode] = round(time_graph(gr, None, iters) * 1e3, 1)
+        del gr
+    del pool, blobs, model, A, B
+    torch.cuda.empty_cache()
+    return {"workload": "draft decoder 12 x (h768, 12 heads, i3072) + LM head 32000, 1024 tokens = 32 tenants x 8 "
+                        "sequences x 4 lookahead, 84 rank-16 LoRA projections, CUDA graph",
+            "us_per_step": {"base_only": out["none"], "grouped_lora": out["pool"], "torch_gather_lora": out["torch"]},
+            "lora_us_per_step": round(out["pool"] - out["none"], 1),
+            "torch_lora_us_per_step": round(out["torch"] - out["none"], 1)}
+
+
 def config3(args, rank, world, local_rank):
     """a Llama-2-13B-shaped stack (40 layers, hidden 5120,
     intermediate 13824), rank 64, bf16, 128 resident adapters, 512 tokens,
@@ -1119,7 +1167,8 @@ def main():
         print(json.dumps(prefill_mix(torch.device("cuda", 0))), flush=True)
         return
     if args.config4:
-        print(json.dumps(config4(torch.device("cuda", 0), steps=args.steps * 10)), flush=True)
+        dev0 = torch.device("cuda", 0)
+        print(json.dumps({"config4": config4(dev0, steps=args.steps * 10), "draft_step": draft_step(dev0)}), flush=True)
         return
     args.warmup = max(args.warmup, 3)
 
@@ -1163,6 +1212,7 @@ def main():
         result["fp16_step"] = fp16_step(device, max(3, args.steps // 2))
         result["prefill_mix"] = prefill_mix(device)
         result["config4"] = config4(device)
+        result["draft_step"] = draft_step(device)
     if rank == 0 and world == 1:
         dt, threads = cpu_reference_layers(args.cpu_layers)
         result["cpu_baseline"] = {"value": round(dt * LAYERS * 1e6, 1), "unit": "us/step", "cores": threads,
