@@ -32,6 +32,12 @@ WP_DTYPE_I64 = 4
 
 WP_TABLE_LIVE = 0
 WP_TABLE_REGISTRY = 1
+WP_TABLE_TILES = 2
+WP_TABLE_SHORT = 3
+
+WP_SEG_DECODE = 0
+WP_SEG_PREFILL = 1
+WP_SEG_AUTO = 2
 
 
 class WpConfig(ctypes.Structure):
@@ -44,6 +50,7 @@ class WpConfig(ctypes.Structure):
         ("use_pdl", ctypes.c_int32),
         ("prefetch_weights", ctypes.c_int32),
         ("kernel", ctypes.c_int32),
+        ("prefill_tokens", ctypes.c_int32),
         ("peer_wait_ms", ctypes.c_int32),
     ]
 
@@ -136,6 +143,7 @@ SIGNATURES = {
     "wp_pool_prepare": (_int, [_vp, ctypes.POINTER(_i32), _i32, _vp]),
     "wp_pool_stats": (_int, [_vp, ctypes.POINTER(_i64), ctypes.POINTER(_i64), ctypes.POINTER(_i32)]),
     "wp_build_seg_bounds_pool": (_int, [_vp, _vp, _vp, _i32, _i32, _vp]),
+    "wp_build_seg_bounds_ex": (_int, [_vp, _vp, _i32, _i32, _i32, _vp]),
     "wp_write_bridge": (_int, [_vp, ctypes.POINTER(WpBridge)]),
     "wp_read_bridge": (_int, [_vp, ctypes.POINTER(WpBridge)]),
     "wp_read_bridge_kernel": (_int, [_vp, ctypes.POINTER(ctypes.c_float), _i32, ctypes.POINTER(_i32)]),

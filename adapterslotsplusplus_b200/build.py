@@ -21,7 +21,7 @@ CSRC = PKG / "csrc"
 INCLUDE = PKG.parent / "include"
 LIB_NAME = "libwp_b200.so"
 LIB_PATH = PKG / LIB_NAME
-SOURCES = ["wp_segment.cu", "wp_apply.cu", "wp_apply_split.cu", "wp_api.cu"]
+SOURCES = ["wp_segment.cu", "wp_apply.cu", "wp_apply_split.cu", "wp_prefill.cu", "wp_api.cu"]
 ARCH = ["-gencode", "arch=compute_100a,code=sm_100a"]
 
 

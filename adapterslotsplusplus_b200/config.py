@@ -31,6 +31,11 @@ class WarpPipeConfig:
     # mma.sync), "split" (balanced: one CTA per SM, equal one-stage items),
     # "tc" (clustered, tcgen05)
     kernel: str = "auto"
+    # build_seg_bounds(prefill=None) sends runs of >= 128 tokens to the
+    # tcgen05 prefill kernels when the step has at least this many tokens
+    # (0 = never, the default: the decode kernel is faster on the measured
+    # prefill mixes; prefill=True selects the prefill kernels explicitly)
+    prefill_tokens: int = 0
     # bound of each in-kernel wait on a tensor-parallel peer (the fused
     # row-parallel exchange), in ms; 0 = 5000
     peer_wait_ms: int = 0

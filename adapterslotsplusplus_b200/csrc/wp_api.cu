@@ -63,6 +63,13 @@ struct wp_handle {
   // live table (build_seg_bounds)
   DevSeg* d_live = nullptr;
   int* d_live_num = nullptr;
+  // prefill mode of the latest build: 128-token tiles of the long runs and
+  // the pieces of the short runs (the full table stays in d_live)
+  DevSeg* d_tiles = nullptr;
+  int* d_tiles_num = nullptr;
+  DevSeg* d_short = nullptr;
+  int* d_short_num = nullptr;
+  bool live_prefill = false;
   int* d_run_starts = nullptr;
   // registry table (build_segments): unsplit host copy + split device copy
   DevSeg* d_reg = nullptr;
@@ -238,10 +245,11 @@ bool encode_a_map(CUtensorMap* m, int dtype, const void* base, int d, int r, int
 
 // B stack [L, o, r] (row stride r, adapter stride `stride0` elements): box
 // r x 128 x 1 with the swizzle whose span is one 2r-byte row (r >= 16).
-bool encode_b_map(CUtensorMap* m, int dtype, const void* base, int o, int r, int64_t L, int64_t stride0) {
+bool encode_b_map(CUtensorMap* m, int dtype, const void* base, int o, int r, int64_t L, int64_t stride0,
+                  uint32_t box_rows = 256) {
   const uint64_t dims[3] = {static_cast<uint64_t>(r), static_cast<uint64_t>(o), static_cast<uint64_t>(L)};
   const uint64_t strides[2] = {static_cast<uint64_t>(r) * 2, static_cast<uint64_t>(stride0) * 2};
-  const uint32_t box[3] = {static_cast<uint32_t>(r), 256, 1};
+  const uint32_t box[3] = {static_cast<uint32_t>(r), box_rows, 1};
   const CUtensorMapSwizzle sw =
       r == 64 ? CU_TENSOR_MAP_SWIZZLE_128B : (r == 32 ? CU_TENSOR_MAP_SWIZZLE_64B : CU_TENSOR_MAP_SWIZZLE_32B);
   return encode_map(m, dtype, 3, base, dims, strides, box, sw);
@@ -250,12 +258,14 @@ bool encode_b_map(CUtensorMap* m, int dtype, const void* base, int o, int r, int
 // Activation rows [T, cols] with row stride ld elements: box 64 x box_rows.
 // Rows of x or y ([T, cols], leading dimension ld): sliced view
 // [cols / 64][T][64] with box {64, box_rows, 4}, else box {64, box_rows}.
-bool encode_rows_map(CUtensorMap* m, int dtype, const void* base, int cols, int T, int64_t ld, int box_rows) {
+bool encode_rows_map(CUtensorMap* m, int dtype, const void* base, int cols, int T, int64_t ld, int box_rows,
+                     int slices = 4) {
   if (sliced(cols)) {
     const uint64_t dims[3] = {static_cast<uint64_t>(wp::kBoxCols), static_cast<uint64_t>(T),
                               static_cast<uint64_t>(cols / wp::kBoxCols)};
     const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(wp::kBoxCols) * 2};
-    const uint32_t box[3] = {static_cast<uint32_t>(wp::kBoxCols), static_cast<uint32_t>(box_rows), 4};
+    const uint32_t box[3] = {static_cast<uint32_t>(wp::kBoxCols), static_cast<uint32_t>(box_rows),
+                             static_cast<uint32_t>(slices)};
     return encode_map(m, dtype, 3, base, dims, strides, box);
   }
   const uint64_t dims[2] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(T)};
@@ -362,6 +372,13 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
   };
   cudaError_t e;
   if ((e = cudaMalloc(&h->d_live, sizeof(DevSeg) * cap)) != cudaSuccess) return bail("live table", e);
+  if ((e = cudaMalloc(&h->d_tiles, sizeof(DevSeg) * (cap / wp::kPrefillTile + 1))) != cudaSuccess)
+    return bail("prefill tile table", e);
+  if ((e = cudaMalloc(&h->d_short, sizeof(DevSeg) * cap)) != cudaSuccess) return bail("short-run table", e);
+  if ((e = cudaMalloc(&h->d_tiles_num, sizeof(int) * 4)) != cudaSuccess) return bail("tile count", e);
+  if ((e = cudaMalloc(&h->d_short_num, sizeof(int) * 4)) != cudaSuccess) return bail("short-run count", e);
+  cudaMemset(h->d_tiles_num, 0, sizeof(int) * 4);
+  cudaMemset(h->d_short_num, 0, sizeof(int) * 4);
   if ((e = cudaMalloc(&h->d_live_num, sizeof(int) * 4)) != cudaSuccess) return bail("live count", e);
   if ((e = cudaMalloc(&h->d_run_starts, sizeof(int) * cap)) != cudaSuccess) return bail("run starts", e);
   if ((e = cudaMalloc(&h->d_reg, sizeof(DevSeg) * (cap + 1))) != cudaSuccess) return bail("registry table", e);
@@ -413,6 +430,10 @@ int wp_destroy(wp_handle* h) {
     if (s.ready) cudaEventDestroy(s.ready);
   if (h->slot_pool) cudaFree(h->slot_pool);
   cudaFree(h->d_live);
+  cudaFree(h->d_tiles);
+  cudaFree(h->d_short);
+  cudaFree(h->d_tiles_num);
+  cudaFree(h->d_short_num);
   cudaFree(h->d_live_num);
   cudaFree(h->d_run_starts);
   cudaFree(h->d_reg);
@@ -737,7 +758,13 @@ void apply_plan(wp_handle* h, int dtype, int r, bool dec, int* cluster, int* gri
 extern "C" {
 
 int wp_build_seg_bounds(wp_handle* h, const void* idx, int32_t idx_dtype, int32_t T, void* stream_v) {
+  return wp_build_seg_bounds_ex(h, idx, idx_dtype, T, WP_SEG_AUTO, stream_v);
+}
+
+int wp_build_seg_bounds_ex(wp_handle* h, const void* idx, int32_t idx_dtype, int32_t T, int32_t flags,
+                           void* stream_v) {
   if (!h) return fail(nullptr, WP_ERR_INVALID, "build_seg_bounds: NULL handle");
+  if (flags < WP_SEG_DECODE || flags > WP_SEG_AUTO) return fail(h, WP_ERR_INVALID, "build_seg_bounds: bad flags %d", flags);
   if (idx_dtype != WP_DTYPE_I32 && idx_dtype != WP_DTYPE_I64)
     return fail(h, WP_ERR_INVALID, "build_seg_bounds: token_lora_indices must be int32 or int64");
   if (T < 0) return fail(h, WP_ERR_INVALID, "build_seg_bounds: negative token count");
@@ -753,9 +780,20 @@ int wp_build_seg_bounds(wp_handle* h, const void* idx, int32_t idx_dtype, int32_
     apply_plan(h, WP_DTYPE_BF16, 32, true, &c, &g);
     h->plan_g = g / std::max(c, 1);
   }
+  const bool prefill =
+      flags == WP_SEG_PREFILL || (flags == WP_SEG_AUTO && h->cfg.prefill_tokens > 0 && T >= h->cfg.prefill_tokens);
+  wp::PrefillTables pf;
+  if (prefill) {
+    pf.tiles = h->d_tiles;
+    pf.tiles_num = h->d_tiles_num;
+    pf.short_segs = h->d_short;
+    pf.short_num = h->d_short_num;
+    pf.min_run = wp::kPrefillMinRun;
+  }
   cudaError_t e = wp::launch_seg_bounds(idx, idx_dtype, T, h->d_live, h->d_live_num, h->d_plan, h->plan_g,
-                                        h->d_run_starts, stream);
+                                        h->d_run_starts, stream, nullptr, 0, nullptr, pf);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "build_seg_bounds launch: %s", cudaGetErrorString(e));
+  h->live_prefill = prefill;
   ++h->launches;
   h->last_was_segmenter = true;
   // the segment count travels to the host asynchronously (outside graph
@@ -773,6 +811,20 @@ int wp_build_seg_bounds(wp_handle* h, const void* idx, int32_t idx_dtype, int32_
 int wp_read_seg_table(wp_handle* h, int32_t which, wp_segment* out, int32_t cap, int32_t* num) {
   if (!h) return fail(nullptr, WP_ERR_INVALID, "read_seg_table: NULL handle");
   DeviceGuard dg(h->device);
+  if (which == WP_TABLE_TILES || which == WP_TABLE_SHORT) {
+    const DevSeg* segs = which == WP_TABLE_TILES ? h->d_tiles : h->d_short;
+    const int* cnt = which == WP_TABLE_TILES ? h->d_tiles_num : h->d_short_num;
+    WP_CUDA(h, cudaDeviceSynchronize());
+    int n = 0;
+    WP_CUDA(h, cudaMemcpy(&n, cnt, sizeof(int), cudaMemcpyDeviceToHost));
+    if (!h->live_prefill) n = 0;
+    if (num) *num = n;
+    const int m = std::min(n, cap);
+    std::vector<DevSeg> tmp(std::max(m, 0));
+    if (m > 0) WP_CUDA(h, cudaMemcpy(tmp.data(), segs, sizeof(DevSeg) * m, cudaMemcpyDeviceToHost));
+    for (int i = 0; i < m; ++i) out[i] = wp_segment{tmp[i].adapter_id, tmp[i].token_start, tmp[i].token_count};
+    return WP_OK;
+  }
   if (which == WP_TABLE_REGISTRY) {
     const int n = static_cast<int>(h->reg_table.size());
     if (num) *num = n;
@@ -1033,6 +1085,56 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   return WP_OK;
 }
 
+// Whether a fused live call goes to the prefill kernels (its long runs) and
+// the decode kernel on the short-run table: the latest build was in prefill
+// mode; rank 16, 32 or 64; d and o multiples of 64 (the sliced tensor maps);
+// y 16-byte addressable; T within the tables; the partial scratch fits.
+// Otherwise the full table goes to the decode kernel.
+bool prefill_eligible(wp_handle* h, int T, int r, int d, int o, const void* y, int64_t y_ld, int y_off,
+                      cudaStream_t stream) {
+  if (!h->live_prefill || T == 0 || h->tp_exchange) return false;
+  if (!(r == 16 || r == 32 || r == 64) || d % 64 != 0 || o % 64 != 0) return false;
+  if (!(al16(y) && y_ld % 8 == 0 && y_off % 8 == 0) || T > h->sync_cap) return false;
+  const int nchunk = (d + wp::kStageK - 1) / wp::kStageK;  // >= the prefill shrink's 1024-column chunks
+  return split_buffers(h, T, nchunk, r, stream);
+}
+
+// The prefill kernels over the tile table. late_wait: the previous kernel on
+// the stream is this call's decode kernel on the short runs (the prefill
+// shrink then runs beside it, see wp_prefill.cu).
+int launch_prefill_call(wp_handle* h, int T, int r, int dtype, const void* x, int64_t x_ld, int d, const void* wa,
+                        int64_t wa_stride, int64_t num_adapters, float scale, void* y, int64_t y_ld, int y_off, int o,
+                        const void* wb, int64_t wb_stride, bool late_wait, cudaStream_t stream) {
+  const int nchunk = (d + wp::kStageK - 1) / wp::kStageK;
+  wp::ApplyArgs a{};
+  a.segs = h->d_tiles;
+  a.num_segs = h->d_tiles_num;
+  a.sync_cap = h->sync_cap / wp::kPrefillTile + 1;
+  a.part = h->d_part;
+  a.pmax = nchunk;
+  a.err = h->d_err;
+  a.d = d;
+  a.o = o;
+  a.y = y;
+  a.y_ld = y_ld;
+  a.y_off = y_off;
+  a.scale = scale;
+  a.pf_late_wait = late_wait && h->cfg.use_pdl != 0 ? 1 : 0;
+  a.trace = h->trace_on ? h->d_trace[1] : nullptr;  // the expand kernel's timeline
+  if (!encode_rows_map(&a.tmap_x128, dtype, x, d, T, x_ld, wp::kPrefillTile) ||
+      !encode_rows_map(&a.tmap_y128, dtype, static_cast<const char*>(y) + static_cast<int64_t>(y_off) * 2, o, T,
+                       y_ld, wp::kPrefillTile, 1) ||
+      !encode_a_map(&a.tmap_a, dtype, wa, d, r, std::max<int64_t>(1, num_adapters), wa_stride) ||
+      !encode_b_map(&a.tmap_b64, dtype, wb, o, r, std::max<int64_t>(1, num_adapters), wb_stride, 64))
+    return fail(h, WP_ERR_CUDA, "prefill: cuTensorMapEncodeTiled failed");
+  wp::LaunchCfg lc{h->num_sms, 1, stream, h->cfg.use_pdl != 0, false};
+  cudaError_t e = wp::launch_prefill(dtype, r, a, lc);
+  if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e));
+  h->launches += 2;
+  h->last_was_segmenter = false;
+  return WP_OK;
+}
+
 }  // namespace
 
 extern "C" {
@@ -1165,9 +1267,20 @@ int wp_add_lora(wp_handle* h, void* y, const void* x, const void* wa_base, int64
   if (!rc) rc = check_expand_args(h, y, y_ld, y_offset, out_features, wb_base, wb_stride0);
   if (rc) return rc;
   DeviceGuard dg(h->device);
+  cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
+  if (prefill_eligible(h, T, rank, d_model, out_features, y, y_ld, y_offset, stream)) {
+    // the short runs on the decode kernel, then the long runs on the prefill
+    // kernels, whose shrink runs beside it (disjoint rows)
+    int rc = do_apply(h, wp::kModeFused, 0, h->d_short, h->d_short_num, T, rank, dtype, x, x_ld, d_model, wa_base,
+                      wa_stride0, num_adapters, scale, y, y_ld, y_offset, out_features, wb_base, wb_stride0, nullptr,
+                      stream);
+    if (rc) return rc;
+    return launch_prefill_call(h, T, rank, dtype, x, x_ld, d_model, wa_base, wa_stride0, num_adapters, scale, y, y_ld,
+                               y_offset, out_features, wb_base, wb_stride0, true, stream);
+  }
   return do_apply(h, wp::kModeFused, 0, h->d_live, h->d_live_num, T, rank, dtype, x, x_ld, d_model, wa_base,
                   wa_stride0, num_adapters, scale, y, y_ld, y_offset, out_features, wb_base, wb_stride0, nullptr,
-                  static_cast<cudaStream_t>(stream_v));
+                  stream);
 }
 
 // Several output slices that share x (vLLM's add_lora_packed_nslice: q/k/v,
@@ -1193,14 +1306,13 @@ int wp_add_lora_slices(wp_handle* h, void* y, const void* x, int32_t nslices, co
   if (rc) return rc;
   DeviceGuard dg(h->device);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
-  if (nslices == 1 || kernel_choice(h) == 2)  // one slice, or the tcgen05 kernel: plain calls
+  if (nslices == 1 || kernel_choice(h) == 2 || h->live_prefill)  // plain calls (prefill tables: per slice)
     for (int s = 0; s < nslices; ++s) {
-      rc = do_apply(h, wp::kModeFused, 0, h->d_live, h->d_live_num, T, rank, dtype, x, x_ld, d_model, wa_bases[s],
-                    wa_strides[s], num_adapters, scale, y, y_ld, y_offsets[s], out_features, wb_bases[s],
-                    wb_strides[s], nullptr, stream);
+      rc = wp_add_lora(h, y, x, wa_bases[s], wa_strides[s], wb_bases[s], wb_strides[s], num_adapters, scale, T,
+                       d_model, out_features, rank, x_ld, y_ld, y_offsets[s], dtype, stream);
       if (rc) return rc;
     }
-  if (nslices == 1 || kernel_choice(h) == 2) return WP_OK;
+  if (nslices == 1 || kernel_choice(h) == 2 || h->live_prefill) return WP_OK;
   if (T == 0) return WP_OK;
   wp::ApplyArgs a{};
   a.segs = h->d_live;
@@ -1769,6 +1881,7 @@ int wp_build_seg_bounds_pool(wp_handle* h, wp_pool* p, const void* idx, int32_t 
   cudaError_t e = wp::launch_seg_bounds(idx, idx_dtype, T, h->d_live, h->d_live_num, h->d_plan, h->plan_g,
                                         h->d_run_starts, stream, p->d_map, p->max_adapters, h->d_err);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "build_seg_bounds_pool launch: %s", cudaGetErrorString(e));
+  h->live_prefill = false;
   ++h->launches;
   h->last_was_segmenter = true;
   return WP_OK;

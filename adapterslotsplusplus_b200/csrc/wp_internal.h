@@ -13,6 +13,10 @@ namespace wp {
 // build_seg_bounds_kernel does (WP_MAX_SEGMENT_TOKENS,
 // csrc/bridge/warp_pipe_metadata.h:22, split at csrc/kernels/warp_pipe_r32.cu:498-511).
 constexpr int kSegTokens = 32;
+// Prefill tiles (tokens per tcgen05 tile, M of the MMAs) and the shortest run
+// the segmenter's prefill mode sends to the prefill kernels.
+constexpr int kPrefillTile = 128;
+constexpr int kPrefillMinRun = 128;
 
 // One entry of a device segment table (32 bytes).
 //   live table (build_seg_bounds): adapter_id/token_start/token_count only; the
@@ -75,6 +79,9 @@ struct ApplyArgs {
   CUtensorMap tmap_y[3];  // y columns [y_off, y_off + o) x T rows, 8 << i rows per box
   CUtensorMap tmap_a;  // live mode: A stack [L, r, d]
   CUtensorMap tmap_b;  // live mode, r >= 16: B stack [L, o, r], box r x 256 x 1, swizzle = 2r bytes
+  CUtensorMap tmap_x128;  // prefill kernels: x [T, d] in 128-row boxes (sliced, {64, 128, 4})
+  CUtensorMap tmap_y128;  // prefill kernels: y columns [y_off, y_off + o), boxes of 128 rows x 64 columns
+  CUtensorMap tmap_b64;  // prefill kernels: B stack [L, o, r], box r x 64 x 1
   // multi-slice calls (nslices > 1, clustered kernel, live mode): slices 1
   // and 2 share x and the table; their A / B stacks and y column ranges
   CUtensorMap tmap_a_x[kMaxSlices - 1];
@@ -99,6 +106,7 @@ struct ApplyArgs {
   int d_sliced;  // tmap_x and the A maps are sliced (d % 64 == 0)
   int o_sliced;  // tmap_y is sliced (o % 64 == 0)
   int prefetch_weights;  // 1: table and weight loads may start before the dependency wait
+  int pf_late_wait;  // prefill shrink: the previous kernel is this call's decode kernel (disjoint rows): wait for it only before exiting
   int* err;
   unsigned long long* trace;  // optional per-CTA phase timestamps (kTraceSlots per CTA), else null
   // split (balanced decode) kernel only
@@ -185,10 +193,27 @@ int apply_split_max_grid(int dtype, int rank);
 int apply_max_grid(int dtype, int rank, int cluster, bool dec);
 
 // idx_dtype: WP_DTYPE_I32 or WP_DTYPE_I64.
+// Prefill mode of the segmenter (wp_segment.cu): tiles of long runs and the
+// pieces of the short ones, besides the full table. tiles == nullptr: off.
+struct PrefillTables {
+  DevSeg* tiles = nullptr;
+  int* tiles_num = nullptr;
+  DevSeg* short_segs = nullptr;
+  int* short_num = nullptr;
+  int min_run = 0;
+};
+
 // slot_map / map_size (optional): translate adapter ids to adapter-pool
 // slots as the table is written (see wp_segment.cu).
 cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs, ClusterPlan* plan,
                               int plan_g, int* run_starts, cudaStream_t stream, const int* slot_map = nullptr,
-                              int map_size = 0, int* err = nullptr);
+                              int map_size = 0, int* err = nullptr, PrefillTables pf = PrefillTables{});
+
+// Prefill kernels (wp_prefill.cu): tcgen05 GEMMs over the tiles of long runs.
+// a.segs / a.num_segs: the tile table; a.part / a.pmax: partials [T, pmax >=
+// ceil(d / 1024), r]; a.tmap_x128: x with 128-row boxes; a.tmap_a / a.tmap_b
+// as for the apply kernel. Ranks 16, 32, 64; d % 64 == 0, o % 64 == 0 and a
+// 16-byte-addressable y.
+cudaError_t launch_prefill(int dtype, int rank, const ApplyArgs& a, const LaunchCfg& lc);
 
 }  // namespace wp

@@ -120,11 +120,15 @@ __device__ void write_cluster_plan(const DevSeg* segs, int nseg, ClusterPlan* pl
 // slot holding it (-1: not resident); table entries then carry the slot,
 // and a run whose adapter is not resident is dropped with kErrBadSegment
 // raised in *err. Runs are found on the original ids either way.
+// pf (optional, prefill mode): besides the full table, runs of at least
+// pf->min_run tokens become tiles of kPrefillTile tokens in pf->tiles, and
+// the pieces of the other runs a second table pf->short_segs (in token
+// order) -- the prefill kernels take the first, the decode kernel the second.
 template <typename I>
 __global__ void __launch_bounds__(kSegThreads, 1)
     seg_bounds_kernel(const I* __restrict__ idx, int T, DevSeg* __restrict__ segs, int* __restrict__ num_segs,
                       int* __restrict__ run_starts, ClusterPlan* __restrict__ plan, int plan_g,
-                      const int* __restrict__ slot_map, int map_size, int* err) {
+                      const int* __restrict__ slot_map, int map_size, int* err, PrefillTables pf) {
   __shared__ int warp_buf[33];
   const int tid = threadIdx.x;
 
@@ -142,7 +146,7 @@ __global__ void __launch_bounds__(kSegThreads, 1)
   __syncthreads();  // run_starts written by other threads of this block
 
   // Pass 2: each run -> ceil(len / 32) pieces, skipping id < 0.
-  int nseg = 0;
+  int nseg = 0, nshort = 0, ntiles = 0;
   for (int base = 0; base < nruns; base += kSegThreads) {
     const int k = base + tid;
     int pieces = 0, start = 0, len = 0;
@@ -174,8 +178,35 @@ __global__ void __launch_bounds__(kSegThreads, 1)
       segs[slot + j] = s;
     }
     nseg += total;
+    if (pf.tiles) {
+      const bool longrun = pieces > 0 && len >= pf.min_run;
+      const int tl = longrun ? (len + kPrefillTile - 1) / kPrefillTile : 0;
+      const int sp = longrun ? 0 : pieces;
+      int tt, ts;
+      const int tslot = ntiles + block_exclusive_scan(tl, warp_buf, &tt);
+      const int sslot = nshort + block_exclusive_scan(sp, warp_buf, &ts);
+      for (int j = 0; j < tl; ++j) {
+        DevSeg s;
+        s.adapter_id = id;
+        s.token_start = start + j * kPrefillTile;
+        s.token_count = min(kPrefillTile, len - j * kPrefillTile);
+        s.alpha = 0.f;
+        s.a = nullptr;
+        s.b = nullptr;
+        pf.tiles[tslot + j] = s;
+      }
+      for (int j = 0; j < sp; ++j) pf.short_segs[sslot + j] = segs[slot + j];
+      ntiles += tt;
+      nshort += ts;
+    }
   }
-  if (tid == 0) *num_segs = nseg;
+  if (tid == 0) {
+    *num_segs = nseg;
+    if (pf.tiles) {
+      *pf.tiles_num = ntiles;
+      *pf.short_num = nshort;
+    }
+  }
   if (plan) {
     __syncthreads();  // the table (global memory, written by this block) is complete
     write_cluster_plan(segs, nseg, plan, plan_g);
@@ -184,13 +215,13 @@ __global__ void __launch_bounds__(kSegThreads, 1)
 
 cudaError_t launch_seg_bounds(const void* idx, int idx_dtype, int T, DevSeg* segs, int* num_segs, ClusterPlan* plan,
                               int plan_g, int* run_starts, cudaStream_t stream, const int* slot_map, int map_size,
-                              int* err) {
+                              int* err, PrefillTables pf) {
   if (idx_dtype == 4) {
     seg_bounds_kernel<int64_t><<<1, kSegThreads, 0, stream>>>(static_cast<const int64_t*>(idx), T, segs, num_segs,
-                                                               run_starts, plan, plan_g, slot_map, map_size, err);
+                                                               run_starts, plan, plan_g, slot_map, map_size, err, pf);
   } else {
     seg_bounds_kernel<int32_t><<<1, kSegThreads, 0, stream>>>(static_cast<const int32_t*>(idx), T, segs, num_segs,
-                                                               run_starts, plan, plan_g, slot_map, map_size, err);
+                                                               run_starts, plan, plan_g, slot_map, map_size, err, pf);
   }
   return cudaGetLastError();
 }

@@ -61,6 +61,7 @@ class WarpPipeEngine:
             use_pdl=1 if self.config.use_pdl else 0,
             prefetch_weights=1 if self.config.prefetch_weights else 0,
             kernel={"auto": 0, "cluster": 1, "split": 2, "tc": 3}[self.config.kernel],
+            prefill_tokens=int(self.config.prefill_tokens),
             peer_wait_ms=int(self.config.peer_wait_ms),
         )
         handle = ctypes.c_void_p()
@@ -152,10 +153,13 @@ class WarpPipeEngine:
                                         int(H.size(0)), dt, _stream_ptr(Y.device)))
 
     # -- live path (engine.py:28-32, 56-62) --------------------------------------
-    def build_seg_bounds(self, token_lora_indices) -> bool:
+    def build_seg_bounds(self, token_lora_indices, prefill: Optional[bool] = None) -> bool:
         """Builds the step's segment table on the device, once per step, ahead
         of every add_lora call of that step. Returns False only when the token
-        count exceeds config.max_tokens."""
+        count exceeds config.max_tokens. prefill: True sends runs of >= 128
+        tokens of one adapter to the tcgen05 prefill kernels, False keeps the
+        decode table only, None (default) decides by the token count
+        (config.prefill_tokens)."""
         if not token_lora_indices.is_cuda:
             raise RuntimeError("build_seg_bounds: token_lora_indices must be a CUDA tensor")
         idx = token_lora_indices
@@ -163,8 +167,9 @@ class WarpPipeEngine:
             idx = idx.to(torch.int64)
         idx = idx.contiguous()
         code = _lib.WP_DTYPE_I64 if idx.dtype == torch.int64 else _lib.WP_DTYPE_I32
-        rc = self._check(self._lib.wp_build_seg_bounds(self._h, idx.data_ptr(), code, int(idx.numel()),
-                                                       _stream_ptr(idx.device)))
+        flags = _lib.WP_SEG_AUTO if prefill is None else (_lib.WP_SEG_PREFILL if prefill else _lib.WP_SEG_DECODE)
+        rc = self._check(self._lib.wp_build_seg_bounds_ex(self._h, idx.data_ptr(), code, int(idx.numel()), flags,
+                                                          _stream_ptr(idx.device)))
         return rc == _lib.WP_OK
 
     def add_lora_packed(self, y, x, wa_t_all, wb_t_all, scale) -> bool:
@@ -330,8 +335,11 @@ class WarpPipeEngine:
     # -- readbacks ---------------------------------------------------------------
     def read_seg_table(self, which: str = "live") -> List[Tuple[int, int, int]]:
         """(adapter_id, token_start, token_count) of every entry of the live
-        (build_seg_bounds) or registry (build_segments) table. Synchronises."""
-        code = _lib.WP_TABLE_LIVE if which == "live" else _lib.WP_TABLE_REGISTRY
+        (build_seg_bounds), registry (build_segments), "tiles" (prefill-mode
+        128-token tiles) or "short" (prefill-mode short-run pieces) table.
+        Synchronises."""
+        code = {"live": _lib.WP_TABLE_LIVE, "registry": _lib.WP_TABLE_REGISTRY, "tiles": _lib.WP_TABLE_TILES,
+                "short": _lib.WP_TABLE_SHORT}[which]
         n = ctypes.c_int32()
         self._check(self._lib.wp_read_seg_table(self._h, code, None, 0, ctypes.byref(n)))
         buf = (_lib.WpSegment * max(n.value, 1))()

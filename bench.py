@@ -734,11 +734,13 @@ def run_reference(args, rank, world):
     }
 
 
-def prefill_mix(device, kernels=("auto", "cluster", "split"), iters=10):
+def prefill_mix(device, iters=10):
     """BASELINE config 2's prefill mix on one 4096 -> 4096 projection: 4096
-    tokens in 8 contiguous 512-token runs (8 adapters), rank 32, bf16. Per
-    kernel: device us per call (CUDA graph of one call, 8 rotating weight
-    sets) and the HBM GB/s of its algorithmic bytes."""
+    tokens in 8 contiguous 512-token runs (8 adapters), rank 32, bf16. Device
+    us per call (CUDA graph of one call over 8 rotating weight sets) and the
+    HBM GB/s of its algorithmic bytes, for the tcgen05 prefill path (runs as
+    128-token GEMM tiles, build_seg_bounds(prefill=True)) and for the decode
+    kernels on 32-token pieces (prefill=False)."""
     from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
 
     T, n_ad = 4096, 8
@@ -750,10 +752,12 @@ def prefill_mix(device, kernels=("auto", "cluster", "split"), iters=10):
     x = torch.randn(T, HIDDEN, device=device, dtype=torch.bfloat16, generator=g) * 0.1
     y = torch.zeros(T, HIDDEN, device=device, dtype=torch.bfloat16)
     sb, eb = algorithmic_bytes(n_ad, T, HIDDEN, HIDDEN, RANK)
+    hbm = measured_peaks().get("hbm_gbs") or 6650.0
     out = {}
-    for kern in kernels:
+    for name, kern, prefill in (("tcgen05_prefill", "auto", True), ("decode_cluster", "cluster", False),
+                                ("decode_split", "split", False)):
         eng = WarpPipeEngine(WarpPipeConfig(max_tokens=T, prefetch_weights=True, kernel=kern), device=device)
-        eng.build_seg_bounds(torch.as_tensor(ids, device=device))
+        eng.build_seg_bounds(torch.as_tensor(ids, device=device), prefill=prefill)
 
         def step():
             for wa, wb in sets:
@@ -761,11 +765,33 @@ def prefill_mix(device, kernels=("auto", "cluster", "split"), iters=10):
 
         gr = capture(step, warm=1)
         ms = time_graph(gr, None, iters) / len(sets)
-        out[kern] = {"us_per_call": round(ms * 1e3, 2), "gbs": round((sb + eb) / (ms * 1e-3) / 1e9, 1),
-                     "kernel": eng.last_apply_kernel()}
+        gbs = (sb + eb) / (ms * 1e-3) / 1e9
+        out[name] = {"us_per_call": round(ms * 1e3, 2), "gbs": round(gbs, 1), "frac_of_hbm": round(gbs / hbm, 3)}
         del gr, eng
     return {"tokens": T, "runs": f"{n_ad} x {T // n_ad}", "d": HIDDEN, "o": HIDDEN, "rank": RANK,
-            "algorithmic_mb": round((sb + eb) / 1e6, 1), "per_kernel": out}
+            "algorithmic_mb": round((sb + eb) / 1e6, 1), "per_path": out}
+
+
+def prefill_profile_case(args):
+    """A few prefill-path launches of config 2's mix (for profilers)."""
+    from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
+
+    device = torch.device("cuda", 0)
+    T, n_ad = 4096, 8
+    ids = np.repeat(np.arange(n_ad), T // n_ad).astype(np.int64)
+    g = torch.Generator(device=device).manual_seed(3)
+    sets = [(torch.randn(n_ad, 1, RANK, HIDDEN, device=device, dtype=torch.bfloat16, generator=g) * 0.02,
+             torch.randn(n_ad, 1, HIDDEN, RANK, device=device, dtype=torch.bfloat16, generator=g) * 0.02)
+            for _ in range(4)]
+    x = torch.randn(T, HIDDEN, device=device, dtype=torch.bfloat16, generator=g) * 0.1
+    y = torch.zeros(T, HIDDEN, device=device, dtype=torch.bfloat16)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=T, prefetch_weights=True), device=device)
+    eng.build_seg_bounds(torch.as_tensor(ids, device=device), prefill=True)
+    for i in range(args.launches):
+        wa, wb = sets[i % len(sets)]
+        eng.add_lora_packed(y, x, wa, wb, 16.0 / RANK)
+    torch.cuda.synchronize()
+    print(json.dumps({"prefill_profile_case": "8 x 512 tokens, d = o = 4096, r32", "calls": args.launches}))
 
 
 def config2_sweep(device, iters=5, ranks=(8, 16, 32, 64), residents=(1, 8, 64, 512), tokens=(1, 16, 256, 4096),
@@ -1150,6 +1176,8 @@ def main():
     ap.add_argument("--kernel", choices=["auto", "cluster", "split", "tc"], default="auto",
                     help="apply kernel of --profile-case")
     ap.add_argument("--prefill-mix", action="store_true", help="time config 2's prefill mix per kernel and exit")
+    ap.add_argument("--prefill-profile", action="store_true",
+                    help="run --launches prefill-path calls of config 2's mix (for profilers) and exit")
     ap.add_argument("--config3", action="store_true",
                     help="time BASELINE config 3 (13B, r64, T=512, tensor-parallel over the N GPUs) and exit")
     ap.add_argument("--config4", action="store_true",
@@ -1165,6 +1193,9 @@ def main():
         return
     if args.prefill_mix:
         print(json.dumps(prefill_mix(torch.device("cuda", 0))), flush=True)
+        return
+    if args.prefill_profile:
+        prefill_profile_case(args)
         return
     if args.config4:
         dev0 = torch.device("cuda", 0)

@@ -49,6 +49,13 @@ extern "C" {
 /* which segment table wp_read_seg_table returns */
 #define WP_TABLE_LIVE 0     /* built by wp_build_seg_bounds */
 #define WP_TABLE_REGISTRY 1 /* built by wp_build_segments   */
+#define WP_TABLE_TILES 2    /* prefill mode: 128-token tiles of the long runs */
+#define WP_TABLE_SHORT 3    /* prefill mode: pieces of the short runs */
+
+/* segment table modes of wp_build_seg_bounds_ex */
+#define WP_SEG_DECODE 0  /* pieces of at most 32 tokens only (the reference's table) */
+#define WP_SEG_PREFILL 1 /* also: runs of >= 128 tokens as 128-token tiles for the tcgen05 prefill kernels */
+#define WP_SEG_AUTO 2    /* prefill mode when T >= wp_config.prefill_tokens > 0 (the default of wp_build_seg_bounds) */
 
 typedef struct wp_handle wp_handle;
 
@@ -69,6 +76,9 @@ typedef struct wp_config {
                                 "split", "dec", "tc"), 1 = clustered decode (mma.sync),
                                 2 = balanced decode ("split": one CTA per SM, equal
                                 one-stage items), 3 = clustered tcgen05 */
+  int32_t prefill_tokens;    /* WP_SEG_AUTO switches to prefill mode at this many tokens
+                                (> 0; 0 = never, the default: on B200 the decode kernel is
+                                faster on the measured prefill mixes) */
   int32_t peer_wait_ms;      /* bound of each in-kernel wait on a tensor-parallel peer
                                 (wp_add_lora_row_parallel); 0 = 5000 ms. On expiry the
                                 kernel sets WP_ERR_DEVICE_TIMEOUT's flag and returns. */
@@ -150,6 +160,18 @@ int wp_build_segments(wp_handle* h, const int32_t* sorted_adapter_ids, const int
  * only when T exceeds max_tokens; the reference's cap is 256. */
 int wp_build_seg_bounds(wp_handle* h, const void* token_lora_indices, int32_t idx_dtype, int32_t T,
                         void* stream);
+
+/* wp_build_seg_bounds with an explicit mode (flags: WP_SEG_DECODE,
+ * WP_SEG_PREFILL, WP_SEG_AUTO). In prefill mode the full table is built as
+ * usual and, besides it, the runs of at least 128 tokens of one adapter
+ * become 128-token tiles; a following wp_add_lora / wp_add_lora_slices then
+ * runs them as tcgen05 GEMMs (M = 128 tokens, accumulators in TMEM) and the
+ * short runs on the decode kernel (calls that the prefill kernels do not
+ * cover -- rank 8, d or o not a multiple of 64, unaligned y -- take
+ * the full table on the decode kernel). The reference has no prefill path:
+ * it caps segments at 32 tokens (csrc/bridge/warp_pipe_metadata.h:22). */
+int wp_build_seg_bounds_ex(wp_handle* h, const void* token_lora_indices, int32_t idx_dtype, int32_t T, int32_t flags,
+                           void* stream);
 
 /* Allocation-free segmenter (no counterpart in the reference). For callers
  * that may not allocate device memory at all -- e.g. a plugin running inside
