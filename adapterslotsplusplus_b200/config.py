@@ -28,8 +28,7 @@ class WarpPipeConfig:
     # cap on persistent CTAs per SM of the apply kernel (0 = as many as fit)
     ctas_per_sm: int = 0
     # apply kernel of fused live-mode calls: "auto", "cluster" (clustered,
-    # mma.sync), "split" (balanced: one CTA per SM, equal one-stage items),
-    # "tc" (clustered, tcgen05)
+    # mma.sync), "split" (balanced: one CTA per SM, equal one-stage items)
     kernel: str = "auto"
     # build_seg_bounds(prefill=None) sends runs of >= 128 tokens to the
     # tcgen05 prefill kernels when the step has at least this many tokens

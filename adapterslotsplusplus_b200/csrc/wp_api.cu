@@ -351,7 +351,7 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
   if (cfg.slot_bytes <= 0) cfg.slot_bytes = static_cast<int64_t>(2) * 64 * 16384 * 2;
   cfg.slot_bytes = (cfg.slot_bytes + 255) / 256 * 256;
   if (cfg.ctas_per_sm < 0) cfg.ctas_per_sm = 0;
-  if (cfg.kernel < 0 || cfg.kernel > 3) return fail(nullptr, WP_ERR_INVALID, "wp_create: kernel must be 0..3");
+  if (cfg.kernel < 0 || cfg.kernel > 2) return fail(nullptr, WP_ERR_INVALID, "wp_create: kernel must be 0..2");
 
   int ndev = 0;
   if (cudaGetDeviceCount(&ndev) != cudaSuccess || ndev == 0)
@@ -753,7 +753,7 @@ int wp_build_segments(wp_handle* h, const int32_t* ids, const int32_t* offs, int
 
 }  // extern "C"
 namespace {
-void apply_plan(wp_handle* h, int dtype, int r, bool dec, int* cluster, int* grid);
+void apply_plan(wp_handle* h, int dtype, int r, int* cluster, int* grid);
 }  // namespace
 extern "C" {
 
@@ -777,7 +777,7 @@ int wp_build_seg_bounds_ex(wp_handle* h, const void* idx, int32_t idx_dtype, int
     // rank plans the same cluster count on B200, and a launch whose count
     // differs ignores the assignment
     int c = 1, g = 1;
-    apply_plan(h, WP_DTYPE_BF16, 32, true, &c, &g);
+    apply_plan(h, WP_DTYPE_BF16, 32, &c, &g);
     h->plan_g = g / std::max(c, 1);
   }
   const bool prefill =
@@ -853,13 +853,13 @@ namespace {
 // Cluster size and persistent grid of the apply kernel for (dtype, rank):
 // the largest cluster whose co-resident grid keeps at least 95% of the CTAs
 // that the best cluster size achieves (cached per handle).
-void apply_plan(wp_handle* h, int dtype, int r, bool dec, int* cluster, int* grid) {
-  const int key = (dec ? 8 : 0) + (dtype == WP_DTYPE_BF16 ? 4 : 0) + (r == 8 ? 0 : r == 16 ? 1 : r == 32 ? 2 : 3);
+void apply_plan(wp_handle* h, int dtype, int r, int* cluster, int* grid) {
+  const int key = (dtype == WP_DTYPE_BF16 ? 4 : 0) + (r == 8 ? 0 : r == 16 ? 1 : r == 32 ? 2 : 3);
   if (h->plan_grid[key] == 0) {
     const int sizes[4] = {8, 4, 2, 1};
     int g[4], best = 0;
     for (int i = 0; i < 4; ++i) {
-      g[i] = wp::apply_max_grid(dtype, r, sizes[i], dec);
+      g[i] = wp::apply_max_grid(dtype, r, sizes[i]);
       if (h->cfg.ctas_per_sm > 0) g[i] = std::min(g[i], h->num_sms * h->cfg.ctas_per_sm / sizes[i] * sizes[i]);
       best = std::max(best, g[i]);
     }
@@ -885,13 +885,11 @@ void apply_plan(wp_handle* h, int dtype, int r, bool dec, int* cluster, int* gri
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
 // Kernel choice (wp_config.kernel; 0 = automatic, or WP_KERNEL when set, a
-// tuning knob): 1 = clustered decode (mma.sync), 2 = balanced decode
-// ("split") for fused live-mode calls, 3 = clustered tcgen05. Returns 0 for
-// split, 1 for clustered decode, 2 for clustered tcgen05, -1 for automatic.
+// tuning knob): 1 = clustered, 2 = balanced ("split") for fused live-mode
+// calls. Returns 0 for split, 1 for clustered, -1 for automatic.
 int kernel_choice(const wp_handle* h) {
   static const int env = [] {
     const char* e = std::getenv("WP_KERNEL");
-    if (e && std::strcmp(e, "tc") == 0) return 2;
     if (e && std::strcmp(e, "split") == 0) return 0;
     if (e && (std::strcmp(e, "dec") == 0 || std::strcmp(e, "cluster") == 0)) return 1;
     return -1;
@@ -899,7 +897,6 @@ int kernel_choice(const wp_handle* h) {
   switch (h->cfg.kernel) {
     case 1: return 1;
     case 2: return 0;
-    case 3: return 2;
     default: return env;
   }
 }
@@ -946,7 +943,6 @@ bool auto_split(wp_handle* h, cudaStream_t stream, int T, int64_t num_adapters, 
   const double cost_split = 9.2 + 0.9 * per_cta;
   return cost_split < cost_cluster;
 }
-bool use_decode_kernel(const wp_handle* h) { return kernel_choice(h) != 2; }
 
 // Makes the split kernel's buffers hold T tokens of nchunk partials of rank r.
 // Outside stream capture they grow as needed (at least doubling); under
@@ -1048,7 +1044,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   bool want_split = kernel_choice(h) == 0 && !h->tp_exchange;
   if (kernel_choice(h) < 0 && mode == wp::kModeFused && !registry && !h->tp_exchange) {
     int c0 = 1, g0 = 1;
-    apply_plan(h, dtype, r, true, &c0, &g0);
+    apply_plan(h, dtype, r, &c0, &g0);
     want_split = auto_split(h, stream, T, num_adapters, g0 / std::max(c0, 1), c0, d, o);
   }
   if (mode == wp::kModeFused && !registry && want_split && T <= h->sync_cap && split_fits) {
@@ -1062,7 +1058,7 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
       a.pmax = nchunk;
       a.sync_cap = h->sync_cap;
       a.scale = scale;
-      wp::LaunchCfg lc{h->split_grid[key], 1, stream, pdl, true};
+      wp::LaunchCfg lc{h->split_grid[key], 1, stream, pdl};
       cudaError_t e = wp::launch_apply_split(dtype, r, a, lc);
       if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "apply launch (split): %s", cudaGetErrorString(e));
       h->last_kernel = 0;
@@ -1072,14 +1068,13 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
     }
   }
   int cluster = 1, grid = 1;
-  const bool dec = use_decode_kernel(h) || h->tp_exchange;  // the peer exchange lives in the decode variant
-  apply_plan(h, dtype, r, dec, &cluster, &grid);
+  apply_plan(h, dtype, r, &cluster, &grid);
   a.split_len = round_up((std::max(d, 1) + cluster - 1) / cluster, wp::kStageK);
   a.oslice = round_up((std::max(o, 1) + cluster - 1) / cluster, wp::kStageCols);
-  wp::LaunchCfg lc{grid, cluster, stream, pdl, dec};
+  wp::LaunchCfg lc{grid, cluster, stream, pdl};
   cudaError_t e = wp::launch_apply(dtype, r, a, lc);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "apply launch: %s", cudaGetErrorString(e));
-  h->last_kernel = dec ? 1 : 2;
+  h->last_kernel = 1;
   ++h->launches;
   h->last_was_segmenter = false;
   return WP_OK;
@@ -1127,7 +1122,7 @@ int launch_prefill_call(wp_handle* h, int T, int r, int dtype, const void* x, in
       !encode_a_map(&a.tmap_a, dtype, wa, d, r, std::max<int64_t>(1, num_adapters), wa_stride) ||
       !encode_b_map(&a.tmap_b64, dtype, wb, o, r, std::max<int64_t>(1, num_adapters), wb_stride, 64))
     return fail(h, WP_ERR_CUDA, "prefill: cuTensorMapEncodeTiled failed");
-  wp::LaunchCfg lc{h->num_sms, 1, stream, h->cfg.use_pdl != 0, false};
+  wp::LaunchCfg lc{h->num_sms, 1, stream, h->cfg.use_pdl != 0};
   cudaError_t e = wp::launch_prefill(dtype, r, a, lc);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "prefill launch: %s", cudaGetErrorString(e));
   h->launches += 2;
@@ -1306,13 +1301,13 @@ int wp_add_lora_slices(wp_handle* h, void* y, const void* x, int32_t nslices, co
   if (rc) return rc;
   DeviceGuard dg(h->device);
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
-  if (nslices == 1 || kernel_choice(h) == 2 || h->live_prefill)  // plain calls (prefill tables: per slice)
+  if (nslices == 1 || h->live_prefill)  // plain calls (prefill tables: per slice)
     for (int s = 0; s < nslices; ++s) {
       rc = wp_add_lora(h, y, x, wa_bases[s], wa_strides[s], wb_bases[s], wb_strides[s], num_adapters, scale, T,
                        d_model, out_features, rank, x_ld, y_ld, y_offsets[s], dtype, stream);
       if (rc) return rc;
     }
-  if (nslices == 1 || kernel_choice(h) == 2 || h->live_prefill) return WP_OK;
+  if (nslices == 1 || h->live_prefill) return WP_OK;
   if (T == 0) return WP_OK;
   wp::ApplyArgs a{};
   a.segs = h->d_live;
@@ -1360,10 +1355,10 @@ int wp_add_lora_slices(wp_handle* h, void* y, const void* x, int32_t nslices, co
   const bool pdl = h->cfg.use_pdl != 0;
   a.prefetch_weights = !pdl || (h->cfg.prefetch_weights != 0 && !h->last_was_segmenter);
   int cluster = 1, grid = 1;
-  apply_plan(h, dtype, rank, true, &cluster, &grid);
+  apply_plan(h, dtype, rank, &cluster, &grid);
   a.split_len = round_up((std::max<int>(d_model, 1) + cluster - 1) / cluster, wp::kStageK);
   a.oslice = round_up((std::max<int>(out_features, 1) + cluster - 1) / cluster, wp::kStageCols);
-  wp::LaunchCfg lc{grid, cluster, stream, pdl, true};
+  wp::LaunchCfg lc{grid, cluster, stream, pdl};
   cudaError_t e = wp::launch_apply(dtype, rank, a, lc);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "add_lora_slices launch: %s", cudaGetErrorString(e));
   h->last_kernel = 1;
@@ -1405,7 +1400,7 @@ int wp_apply_plan(wp_handle* h, int32_t dtype, int32_t rank, int32_t* cluster, i
   if (!rank_ok(rank) || !dtype16(dtype)) return fail(h, WP_ERR_INVALID, "apply_plan: bad rank or dtype");
   DeviceGuard dg(h->device);
   int c = 0, g = 0;
-  apply_plan(h, dtype, rank, use_decode_kernel(h), &c, &g);
+  apply_plan(h, dtype, rank, &c, &g);
   if (cluster) *cluster = c;
   if (grid) *grid = g;
   return WP_OK;
@@ -1875,7 +1870,7 @@ int wp_build_seg_bounds_pool(wp_handle* h, wp_pool* p, const void* idx, int32_t 
   cudaStream_t stream = static_cast<cudaStream_t>(stream_v);
   if (h->plan_g == 0) {
     int c = 1, g = 1;
-    apply_plan(h, WP_DTYPE_BF16, 32, true, &c, &g);
+    apply_plan(h, WP_DTYPE_BF16, 32, &c, &g);
     h->plan_g = g / std::max(c, 1);
   }
   cudaError_t e = wp::launch_seg_bounds(idx, idx_dtype, T, h->d_live, h->d_live_num, h->d_plan, h->plan_g,

@@ -178,7 +178,6 @@ struct LaunchCfg {
   int cluster;
   cudaStream_t stream;
   bool pdl;
-  bool dec;  // decode variant (mma.sync in the compute warps) instead of tcgen05
 };
 
 // dtype: 0 = f16, 1 = bf16 (WP_DTYPE_*). Launches the clustered apply kernel
@@ -190,7 +189,7 @@ int apply_split_max_grid(int dtype, int rank);
 
 // Largest co-resident persistent grid for the apply kernel of (dtype, rank)
 // with clusters of `cluster` CTAs (0 if that cluster size cannot be scheduled).
-int apply_max_grid(int dtype, int rank, int cluster, bool dec);
+int apply_max_grid(int dtype, int rank, int cluster);
 
 // idx_dtype: WP_DTYPE_I32 or WP_DTYPE_I64.
 // Prefill mode of the segmenter (wp_segment.cu): tiles of long runs and the

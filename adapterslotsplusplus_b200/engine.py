@@ -60,7 +60,7 @@ class WarpPipeEngine:
             ctas_per_sm=int(self.config.ctas_per_sm),
             use_pdl=1 if self.config.use_pdl else 0,
             prefetch_weights=1 if self.config.prefetch_weights else 0,
-            kernel={"auto": 0, "cluster": 1, "split": 2, "tc": 3}[self.config.kernel],
+            kernel={"auto": 0, "cluster": 1, "split": 2}[self.config.kernel],
             prefill_tokens=int(self.config.prefill_tokens),
             peer_wait_ms=int(self.config.peer_wait_ms),
         )

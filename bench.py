@@ -1173,7 +1173,7 @@ def main():
     ap.add_argument("--profile-case", choices=["q", "gate", "down"], default=None,
                     help="run a few launches of one projection (for profilers) and exit")
     ap.add_argument("--launches", type=int, default=12, help="launches of --profile-case")
-    ap.add_argument("--kernel", choices=["auto", "cluster", "split", "tc"], default="auto",
+    ap.add_argument("--kernel", choices=["auto", "cluster", "split"], default="auto",
                     help="apply kernel of --profile-case")
     ap.add_argument("--prefill-mix", action="store_true", help="time config 2's prefill mix per kernel and exit")
     ap.add_argument("--prefill-profile", action="store_true",
