@@ -136,6 +136,7 @@ struct ApplyCfg {
   static constexpr int SMEM = FIXED + STAGES * STAGE;
   static_assert(STAGES >= 2 && STAGES <= 8 && SMEM <= kSmemMax, "shared memory budget");
   static_assert(32 * PITCH * 4 >= kComputeWarps * 128, "the P tile holds one scratch row per compute warp");
+  static_assert(32 * PITCH * 4 >= kTraceSlots * 8, "the P tile holds the staged trace record");
   static_assert(PW >= 4 * kSnakeMax * 4, "the partial slots hold the table-ordering scratch");
 };
 
@@ -244,7 +245,6 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   uint64_t* cbar = reinterpret_cast<uint64_t*>(smem + 256);
   volatile int* s_bad = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS);
   volatile int* s_issued = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS + 4);
-  volatile int* s_armed = reinterpret_cast<volatile int*>(smem + C::OFF_FLAGS + 8);  // stages armed by the producer
   int4* sdesc = reinterpret_cast<int4*>(smem + C::OFF_DESC);
   float* Ps = reinterpret_cast<float*>(smem + C::OFF_P);
   float* Hs = reinterpret_cast<float*>(smem + C::OFF_H);
@@ -268,6 +268,22 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const int G = static_cast<int>(cluster_count_x());
   std::conditional_t<TR, Trace, TraceOff> tr;
   tr.init(a.trace, tid == 0);
+  // The plan words of this cluster are loaded first thing: the load's latency
+  // (long while the previous kernel streams at full bandwidth) overlaps the
+  // barrier set-up below. Threads 0-2: header, count, half; threads 32..:
+  // the descriptors of the cluster's rounds.
+  const bool use_plan = nslices <= 1 && a.plan != nullptr;
+  int4 plan_word = make_int4(0, 0, 0, 0);
+  if (use_plan && cid < kPlanMaxClusters) {
+    if (tid == 0) plan_word = __ldcg(&a.plan->hdr);
+    if (tid == 1) plan_word.x = __ldcg(&a.plan->count[cid]);
+    if (tid == 2) plan_word.x = __ldcg(&a.plan->half[cid]);
+    if (tid >= 32 && tid < 32 + 2 * kPlanRounds) {
+      const int j = tid - 32;
+      const int slot = min((j >> 1) * G + cid, kPlanRounds * kPlanMaxClusters - 1);
+      plan_word = __ldcg(reinterpret_cast<const int4*>(&a.plan->seg[slot]) + (j & 1));
+    }
+  }
 
   if (tid == 0) {
     for (int s = 0; s < S; ++s) {
@@ -282,7 +298,6 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
     *s_bad = 0;
     *s_issued = 0;
-    *s_armed = 0;
     fence_mbar_init();
   }
   if (producer && lane == 0) {
@@ -336,14 +351,10 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   };
   auto read_plan = [&]() -> bool {
     int4* sh = reinterpret_cast<int4*>(Ps);  // scratch: header, count, half
-    if (tid == 0) sh[0] = __ldcg(&a.plan->hdr);
-    if (tid == 1) reinterpret_cast<int*>(sh + 1)[0] = __ldcg(&a.plan->count[min(cid, kPlanMaxClusters - 1)]);
-    if (tid == 2) reinterpret_cast<int*>(sh + 1)[1] = __ldcg(&a.plan->half[min(cid, kPlanMaxClusters - 1)]);
-    if (tid >= 32 && tid < 32 + 2 * kPlanRounds) {
-      const int j = tid - 32;
-      const int slot = min((j >> 1) * G + cid, kPlanRounds * kPlanMaxClusters - 1);
-      sdesc[j] = __ldcg(reinterpret_cast<const int4*>(&a.plan->seg[slot]) + (j & 1));
-    }
+    if (tid == 0) sh[0] = plan_word;
+    if (tid == 1) reinterpret_cast<int*>(sh + 1)[0] = plan_word.x;
+    if (tid == 2) reinterpret_cast<int*>(sh + 1)[1] = plan_word.x;
+    if (tid >= 32 && tid < 32 + 2 * kPlanRounds) sdesc[tid - 32] = plan_word;
     __syncthreads();
     const int4 hdr = sh[0];
     const int count = reinterpret_cast<const int*>(sh + 1)[0];
@@ -364,7 +375,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const int S_sl = nslices > 1 ? nslices : 1;
   int nseg_t = 0;  // segments of the table (not virtual)
   auto read_table = [&]() {
-    if (S_sl == 1 && a.plan && read_plan()) return;
+    if (use_plan && read_plan()) return;
     TableView tv{0, -1, oB0, nB, 0};
     table_fallback<R>(a, S_sl, do_ex, G, cid, q, CL, sdesc, reinterpret_cast<int*>(Pw), &tv);
     nmine = tv.nmine;
@@ -399,7 +410,17 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     tr.dep();
     read_table();
   }
-  if (tid == 0) trace_mark_t<TR>(a.trace, 7);
+  // tracing: the record is staged in the P tile (free after the table read)
+  unsigned long long* trc = nullptr;
+  if constexpr (TR) {
+    if (a.trace) {
+      trc = reinterpret_cast<unsigned long long*>(Ps);
+      for (int i = tid; i < kTraceSlots; i += kThreads) trc[i] = 0ull;
+    }
+    __syncthreads();
+    tr.stage(trc);
+  }
+  if (tid == 0) trace_rec_mark<TR>(trc, 7);
   const int total = nmine * ups;
 
 
@@ -489,21 +510,24 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     // ======================= producer warp ===================================
     if (lane == 0) {
       const uint64_t ef = l2_evict_first_policy();  // adapter weights stream through L2 once
-      trace_mark_t<TR>(a.trace, 9);
+      trace_rec_mark<TR>(trc, 9);
       // with prefetched weights the first `first` units get their weights
       // before the dependency wait (their activations come from the store
       // thread); otherwise the dependency was met before the table was read
       bool met = !a.prefetch_weights;
       int u = 0, stage = 0;
       uint32_t round = 0;  // u = round * S + stage
-      for (int sj = 0; sj < nmine && !*s_bad; ++sj) {
+      // The first `first` units are armed whatever happens: with prefetched
+      // weights the store thread loads their activations unconditionally, and
+      // the drain after an error waits for every armed stage.
+      for (int sj = 0; sj < nmine && !(*s_bad && u >= first); ++sj) {
         const SegTma g = seg_tma(desc(sj));
         for (int sub = 0; sub < ups; ++sub) {
           if (!met && u == first) {
-            trace_mark_t<TR>(a.trace, 8);
+            trace_rec_mark<TR>(trc, 8);
             pdl_wait_prior();
             pdl_launch_dependents();
-            trace_mark_t<TR>(a.trace, 6);
+            trace_rec_mark<TR>(trc, 6);
             met = true;
           }
           if (u >= S) {
@@ -512,14 +536,9 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           }
           uint8_t* st = stage_base + stage * C::STAGE;
           issue_w(g, sub, st, &full[stage], ef);
-          if (met) {
-            issue_x(g, sub, st, &full[stage]);
-          } else {
-            __threadfence_block();
-            *s_armed = u + 1;  // the store thread may load this stage's activations
-          }
-          trace_unit_t<TR>(a.trace, u, 7);
-          if (u == 0) trace_mark_t<TR>(a.trace, 10);
+          if (met) issue_x(g, sub, st, &full[stage]);
+          trace_rec_unit<TR>(trc, u, 7);
+          if (u == 0) trace_rec_mark<TR>(trc, 10);
           *s_issued = u + 1;
           ++u;
           if (++stage == S) {
@@ -529,10 +548,10 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         }
       }
       if (!met) {
-        trace_mark_t<TR>(a.trace, 8);
+        trace_rec_mark<TR>(trc, 8);
         pdl_wait_prior();
         pdl_launch_dependents();
-        trace_mark_t<TR>(a.trace, 6);
+        trace_rec_mark<TR>(trc, 6);
       }
     } else if (a.prefetch_weights) {
       pdl_wait_prior();
@@ -552,23 +571,15 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
     if (lane != 0) return;
     if (a.prefetch_weights) {
-      // the first stages' activations, as soon as the dependency is met
+      // The first stages' activations, as soon as the dependency is met,
+      // whether or not the producer has armed their barriers yet: bytes that
+      // land first take the barrier's transaction count below zero (its
+      // range is +-(2^20 - 1)), and the phase cannot complete before the
+      // producer's arrival, which adds the stage's full byte count.
       int u = 0;
-      for (int sj = 0; sj < nmine && u < first && !*s_bad; ++sj) {
+      for (int sj = 0; sj < nmine && u < first; ++sj) {
         const SegTma g = seg_tma(desc(sj));
-        for (int sub = 0; sub < ups && u < first; ++sub, ++u) {
-          bool armed = *s_armed > u;
-          for (int spin = 0; !armed && spin < (1 << 22); ++spin) {
-            __nanosleep(32);
-            armed = *s_armed > u;
-          }
-          if (!armed) {
-            *s_bad = 1;
-            if (a.err) atomicOr(a.err, kErrWaitTimeout);
-            break;
-          }
-          issue_x(g, sub, stage_base + u * C::STAGE, &full[u]);
-        }
+        for (int sub = 0; sub < ups && u < first; ++sub, ++u) issue_x(g, sub, stage_base + u * C::STAGE, &full[u]);
       }
     }
     if (!do_ex) return;

@@ -63,8 +63,21 @@ __device__ __forceinline__ void trace_unit_t(unsigned long long* base, int u, in
   if constexpr (TR) trace_unit(base, u, k);
 }
 
+// The same marks into a per-CTA record (a shared-memory staging copy).
+template <bool TR>
+__device__ __forceinline__ void trace_rec_mark(unsigned long long* rec, int k) {
+  if constexpr (TR)
+    if (rec) rec[8 + k] = global_timer_ns();
+}
+template <bool TR>
+__device__ __forceinline__ void trace_rec_unit(unsigned long long* rec, int u, int k) {
+  if constexpr (TR)
+    if (rec && u >= 0 && u < kTraceUnits) rec[8 + kTraceSegMarks + kTraceMarks * u + k] = global_timer_ns();
+}
+
 struct TraceOff {
   __device__ void init(unsigned long long*, bool) {}
+  __device__ void stage(unsigned long long*) {}
   __device__ void dep() {}
   __device__ unsigned long long before_wait() { return 0ull; }
   __device__ void after_wait(unsigned long long) {}
@@ -75,11 +88,21 @@ struct TraceOff {
 
 struct Trace {
   unsigned long long* rec = nullptr;
+  unsigned long long* grec = nullptr;  // global record when `rec` is a shared-memory staging copy
   unsigned long long t_start = 0, t_dep = 0, t_first = 0, waited = 0, units = 0;
   __device__ void init(unsigned long long* base, bool me) {
     if (base && me) {
       rec = base + blockIdx.x * kTraceSlots;
       t_start = global_timer_ns();
+    }
+  }
+  // Marks go to `srec` (kTraceSlots zeroed values in shared memory) from now
+  // on and are copied to the global record by finish(): a global store per
+  // mark would make the fences that follow marks wait for it.
+  __device__ void stage(unsigned long long* srec) {
+    if (rec) {
+      grec = rec;
+      rec = srec;
     }
   }
   __device__ void dep() {
@@ -114,6 +137,10 @@ struct Trace {
       rec[3] = global_timer_ns();
       rec[4] = units;
       rec[5] = waited;
+      if (grec) {
+        __threadfence_block();
+        for (int i = 0; i < kTraceSlots; ++i) grec[i] = static_cast<volatile unsigned long long*>(rec)[i];
+      }
     }
   }
 };

@@ -71,11 +71,10 @@ typedef struct wp_config {
                                 that the kernel right before an apply call never writes the
                                 adapter weights (true in serving: weights are static during
                                 a step). 0 = strict stream order. */
-  int32_t kernel;            /* apply kernel of fused live-mode calls: 0 = default (clustered
-                                decode variant, or the WP_KERNEL environment variable:
-                                "split", "dec", "tc"), 1 = clustered decode (mma.sync),
-                                2 = balanced decode ("split": one CTA per SM, equal
-                                one-stage items), 3 = clustered tcgen05 */
+  int32_t kernel;            /* apply kernel of fused live-mode calls: 0 = default (automatic,
+                                or the WP_KERNEL environment variable: "split", "cluster"),
+                                1 = clustered decode (mma.sync), 2 = balanced decode
+                                ("split": one CTA per SM, equal one-stage items) */
   int32_t prefill_tokens;    /* WP_SEG_AUTO switches to prefill mode at this many tokens
                                 (> 0; 0 = never, the default: on B200 the decode kernel is
                                 faster on the measured prefill mixes) */
