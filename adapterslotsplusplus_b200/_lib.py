@@ -52,6 +52,7 @@ class WpConfig(ctypes.Structure):
         ("kernel", ctypes.c_int32),
         ("prefill_tokens", ctypes.c_int32),
         ("peer_wait_ms", ctypes.c_int32),
+        ("prefetch_inputs", ctypes.c_int32),
     ]
 
 
@@ -117,6 +118,7 @@ SIGNATURES = {
     "wp_slot_stats": (_int, [_vp, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "wp_device_error": (_int, [_vp, _i32, ctypes.POINTER(_i32)]),
     "wp_trace_enable": (_int, [_vp, _i32]),
+    "wp_note_input_write": (_int, [_vp]),
     "wp_trace_read": (_int, [_vp, _i32, ctypes.POINTER(ctypes.c_uint64), _i32, ctypes.POINTER(_i32)]),
     "wp_apply_plan": (_int, [_vp, _i32, _i32, ctypes.POINTER(_i32), ctypes.POINTER(_i32)]),
     "wp_tp_unique_id_bytes": (_i32, []),

@@ -38,3 +38,8 @@ class WarpPipeConfig:
     # bound of each in-kernel wait on a tensor-parallel peer (the fused
     # row-parallel exchange), in ms; 0 = 5000
     peer_wait_ms: int = 0
+    # with prefetch_weights: a fused live call loads x and runs its shrink
+    # before the previous kernel on the stream has finished (only its y
+    # loads wait). Only valid when that kernel never writes the call's x
+    # (serving: it is the base layer's GEMM, which writes y).
+    prefetch_inputs: bool = False

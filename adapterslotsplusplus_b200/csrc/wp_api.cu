@@ -130,6 +130,7 @@ struct wp_handle {
   // launch bookkeeping
   int64_t launches = 0;
   bool last_was_segmenter = false;
+  bool input_written = false;  // wp_note_input_write: the next apply call's x was just written
 
   // tensor parallel
   ncclComm_t comm = nullptr;
@@ -1036,6 +1037,12 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   // caller's promise (prefetch_weights) that the preceding kernel writes no
   // adapter weights, and a preceding kernel that is not the segmenter.
   a.prefetch_weights = !pdl || (h->cfg.prefetch_weights != 0 && !h->last_was_segmenter);
+  // x as well (fused live calls): the caller's further promise
+  // (prefetch_inputs) that the preceding kernel writes no x, unless it said
+  // otherwise for this call (wp_note_input_write)
+  a.prefetch_inputs = pdl && a.prefetch_weights && h->cfg.prefetch_inputs != 0 && !h->input_written &&
+                      mode == wp::kModeFused && !registry && !h->tp_exchange && a.y_tma;
+  h->input_written = false;
   const int nchunk = (d + wp::kStageK - 1) / wp::kStageK;
   const int64_t nchunk_max = std::max<int64_t>(nchunk, (o + wp::kStageCols - 1) / wp::kStageCols);
   // the split kernel's item arithmetic is 32-bit (items x grid < 2^31) and its
@@ -1354,6 +1361,8 @@ int wp_add_lora_slices(wp_handle* h, void* y, const void* x, int32_t nslices, co
   }
   const bool pdl = h->cfg.use_pdl != 0;
   a.prefetch_weights = !pdl || (h->cfg.prefetch_weights != 0 && !h->last_was_segmenter);
+  a.prefetch_inputs = pdl && a.prefetch_weights && h->cfg.prefetch_inputs != 0 && !h->input_written && a.y_tma;
+  h->input_written = false;
   int cluster = 1, grid = 1;
   apply_plan(h, dtype, rank, &cluster, &grid);
   a.split_len = round_up((std::max<int>(d_model, 1) + cluster - 1) / cluster, wp::kStageK);
@@ -1364,6 +1373,12 @@ int wp_add_lora_slices(wp_handle* h, void* y, const void* x, int32_t nslices, co
   h->last_kernel = 1;
   ++h->launches;
   h->last_was_segmenter = false;
+  return WP_OK;
+}
+
+int wp_note_input_write(wp_handle* h) {
+  if (!h) return fail(nullptr, WP_ERR_INVALID, "note_input_write: NULL handle");
+  h->input_written = true;
   return WP_OK;
 }
 

@@ -317,6 +317,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   }
   __syncthreads();
   cluster_sync_hw();  // every CTA's cluster barrier is initialised before anyone arrives on it
+  unsigned long long t_synced = 0;  // tracing: after the set-up
+  if constexpr (TR) t_synced = global_timer_ns();
 
   const bool do_sh = LF || (a.mode & kModeShrink) != 0;
   const bool do_ex = LF || (a.mode & kModeExpand) != 0;
@@ -419,6 +421,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
     __syncthreads();
     tr.stage(trc);
+    if (trc && tid == 0) trc[8 + 4] = t_synced;  // mark 4: set-up done (mark 7: table read)
   }
   if (tid == 0) trace_rec_mark<TR>(trc, 7);
   const int total = nmine * ups;
@@ -506,14 +509,20 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
   };
   const int first = min(S, total);  // stages issued before any is consumed
+  // x of the shrink units may load before the dependency wait (fused live
+  // calls whose caller promised that the previous kernel writes no x)
+  const bool xpre = LF != 0 && !TPX && a.prefetch_weights && a.prefetch_inputs;
   if (warp == kProducerWarp) {
     // ======================= producer warp ===================================
     if (lane == 0) {
       const uint64_t ef = l2_evict_first_policy();  // adapter weights stream through L2 once
       trace_rec_mark<TR>(trc, 9);
-      // with prefetched weights the first `first` units get their weights
-      // before the dependency wait (their activations come from the store
-      // thread); otherwise the dependency was met before the table was read
+      // With prefetched weights the first `first` units get their weights
+      // before the dependency wait, and their activations come from the
+      // store thread once it is met; with prefetched inputs the x of every
+      // shrink unit is loaded here without waiting, and only a y (expand
+      // unit) needs the dependency. Without prefetch the dependency was met
+      // before the table was read.
       bool met = !a.prefetch_weights;
       int u = 0, stage = 0;
       uint32_t round = 0;  // u = round * S + stage
@@ -523,7 +532,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       for (int sj = 0; sj < nmine && !(*s_bad && u >= first); ++sj) {
         const SegTma g = seg_tma(desc(sj));
         for (int sub = 0; sub < ups; ++sub) {
-          if (!met && u == first) {
+          const bool x_free = xpre && sub < nA;  // activations that need no dependency wait
+          if (!met && u >= first && !x_free) {
             trace_rec_mark<TR>(trc, 8);
             pdl_wait_prior();
             pdl_launch_dependents();
@@ -536,7 +546,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           }
           uint8_t* st = stage_base + stage * C::STAGE;
           issue_w(g, sub, st, &full[stage], ef);
-          if (met) issue_x(g, sub, st, &full[stage]);
+          if (met || x_free) issue_x(g, sub, st, &full[stage]);
           trace_rec_unit<TR>(trc, u, 7);
           if (u == 0) trace_rec_mark<TR>(trc, 10);
           *s_issued = u + 1;
@@ -576,10 +586,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       // land first take the barrier's transaction count below zero (its
       // range is +-(2^20 - 1)), and the phase cannot complete before the
       // producer's arrival, which adds the stage's full byte count.
+      // (with prefetched inputs the producer has loaded the shrink units' x)
       int u = 0;
       for (int sj = 0; sj < nmine && u < first; ++sj) {
         const SegTma g = seg_tma(desc(sj));
-        for (int sub = 0; sub < ups && u < first; ++sub, ++u) issue_x(g, sub, stage_base + u * C::STAGE, &full[u]);
+        for (int sub = 0; sub < ups && u < first; ++sub, ++u)
+          if (!(xpre && sub < nA)) issue_x(g, sub, stage_base + u * C::STAGE, &full[u]);
       }
     }
     if (!do_ex) return;
@@ -615,11 +627,18 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   }
 
   // ======================== compute warps ======================================
-  if (a.prefetch_weights) {
-    pdl_wait_prior();
-    pdl_launch_dependents();
-    tr.dep();
-  }
+  // With prefetched inputs the shrink and the exchange run before the
+  // dependency is met; it is awaited before the first expand stage.
+  bool cdep = !a.prefetch_weights;
+  auto compute_dep = [&]() {
+    if (!cdep) {
+      pdl_wait_prior();
+      pdl_launch_dependents();
+      tr.dep();
+      cdep = true;
+    }
+  };
+  if (!xpre) compute_dep();
   // tensor parallelism: the epoch of this launch's peer exchange (after the
   // dependency wait, so the previous launch's advance is visible)
   const int tp_epoch = TPX ? __ldcg(&a.tp_seq[0]) + 1 : 0;
@@ -896,6 +915,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
 
     if (!do_ex || nB == 0) continue;
+    compute_dep();
     T* yg = static_cast<T*>(a.y);
     {
       // ---- 3. expand over this CTA's slice of o. Transposed: D^T[o, t] =

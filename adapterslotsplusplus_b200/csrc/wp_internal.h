@@ -106,6 +106,7 @@ struct ApplyArgs {
   int d_sliced;  // tmap_x and the A maps are sliced (d % 64 == 0)
   int o_sliced;  // tmap_y is sliced (o % 64 == 0)
   int prefetch_weights;  // 1: table and weight loads may start before the dependency wait
+  int prefetch_inputs;  // 1 (fused live calls): x loads and the shrink may also run before it
   int pf_late_wait;  // prefill shrink: the previous kernel is this call's decode kernel (disjoint rows): wait for it only before exiting
   int* err;
   unsigned long long* trace;  // optional per-CTA phase timestamps (kTraceSlots per CTA), else null
@@ -157,17 +158,17 @@ struct TpMail {
   }
 };
 
-// Per-CTA trace record (globaltimer ns): start, after the dependency wait,
-// first stage ready, end, stages consumed, ns consumers spent waiting for
-// stages, ns the producer spent waiting for free stages, 0; eight marks of the
-// first segment (8: shrink accumulator ready, 9: after the first cluster
-// barrier, 10: after the second, 11: H tiles written, 12: first shrink stage
-// landed (MMA warp), 13: last shrink MMA issued, 14: producer past the
-// dependency wait, 15: table read, 16: producer before the dependency wait,
-// 17-19: unused); then, for the first kTraceUnits stages, 8 timestamps each: before the stage wait, after
-// it, then four phase marks (for an expand stage: MMA done, results in shared
-// memory, after the barrier, results stored; then the MMA warp's commit and
-// the producer's issue of that stage).
+// Per-CTA trace record (globaltimer ns) of the clustered apply kernel:
+// start, after the dependency wait (compute warps), first stage ready, end,
+// stages consumed, ns consumers spent waiting for stages, 0, 0; twelve marks
+// (8: shrink of the first segment done, 9: its partials received from the
+// cluster, 10: its H complete, 11: its partials pushed, 12: set-up done, 13:
+// unused, 14: producer past the dependency wait, 15: table read, 16:
+// producer before the dependency wait, 17: producer start, 18: first unit
+// issued, 19: unused); then, for the first kTraceUnits stages that thread 0
+// consumes, 8 timestamps each: before the stage wait, after it, four phase
+// marks (expand: y in the accumulators, MMAs done, results in shared memory,
+// stage released), 0, and the producer's issue of that stage-unit.
 constexpr int kTraceUnits = 16;
 constexpr int kTraceMarks = 8;
 constexpr int kTraceSegMarks = 12;

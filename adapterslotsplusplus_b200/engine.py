@@ -63,6 +63,7 @@ class WarpPipeEngine:
             kernel={"auto": 0, "cluster": 1, "split": 2}[self.config.kernel],
             prefill_tokens=int(self.config.prefill_tokens),
             peer_wait_ms=int(self.config.peer_wait_ms),
+            prefetch_inputs=1 if self.config.prefetch_inputs else 0,
         )
         handle = ctypes.c_void_p()
         _lib.check(self._lib.wp_create(ctypes.byref(cfg), ctypes.byref(handle)), None)
@@ -207,12 +208,20 @@ class WarpPipeEngine:
             raise RuntimeError("add_lora: y_slice_size must equal wb_t_all.size(-2)")
         if y_offset is None and y_slice_size is None and out_features != int(y2d.size(1)):
             raise RuntimeError("add_lora_packed: y.size(-1) must equal wb_t_all.size(-2)")
+        if x2d.data_ptr() != x.data_ptr():
+            self.note_input_write()  # reshape copied x: the copy is the kernel right before the apply
         self._check(self._lib.wp_add_lora(
             self._h, y2d.data_ptr(), x2d.data_ptr(), wa_t_all.data_ptr(), int(wa_t_all.stride(0)),
             wb_t_all.data_ptr(), int(wb_t_all.stride(0)), int(wa_t_all.size(0)), float(scale), T, d_model,
             out_features, rank,
             int(x2d.stride(0)), int(y2d.stride(0)), off, dt, _stream_ptr(x.device)))
         return True
+
+    def note_input_write(self) -> None:
+        """The kernel just enqueued on the current stream wrote the next apply
+        call's x (e.g. a copy): with prefetch_inputs that call still loads x
+        only after the preceding kernel has finished."""
+        self._check(self._lib.wp_note_input_write(self._h))
 
     def add_lora_packed_nslice(self, y, x, lora_a_stacked, lora_b_stacked, scale, output_slices) -> bool:
         """vLLM's PunicaWrapper.add_lora_packed_nslice in one launch: slice s
@@ -242,6 +251,8 @@ class WarpPipeEngine:
         if sum(int(w) for w in output_slices) > int(y2d.size(1)):
             raise RuntimeError("add_lora_packed_nslice: output_slices exceed y's width")
         offs = [sum(int(w) for w in output_slices[:s]) for s in range(n)]
+        if x2d.data_ptr() != x.data_ptr():
+            self.note_input_write()  # reshape copied x right before the apply
         for g in range(0, n, 3):
             k = min(3, n - g)
             A, B = lora_a_stacked[g:g + k], lora_b_stacked[g:g + k]

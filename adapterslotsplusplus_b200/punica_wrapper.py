@@ -50,15 +50,16 @@ def _get_engine() -> WarpPipeEngine:
 
     Serving contract: adapter weights are not written while a step runs
     (vLLM loads them between steps), and the kernel right before a LoRA call
-    is the base layer's GEMM. So the engine runs with prefetch_weights: each
-    apply launch starts streaming its adapter weights while the preceding
-    kernel finishes (programmatic dependent launch). Activations are always
-    read after that kernel completes."""
+    is the base layer's GEMM, which reads x and writes y. So the engine runs
+    with prefetch_weights and prefetch_inputs: each apply launch streams its
+    adapter weights and x, and runs its shrink, while the preceding kernel
+    finishes (programmatic dependent launch); y is read after that kernel
+    completes."""
     global _engine
     if _engine is None:
         from .config import WarpPipeConfig
 
-        _engine = WarpPipeEngine(WarpPipeConfig(prefetch_weights=True))
+        _engine = WarpPipeEngine(WarpPipeConfig(prefetch_weights=True, prefetch_inputs=True))
     return _engine
 
 

@@ -37,15 +37,17 @@ _engine = None
 
 def _get_engine():
     """Lazy singleton (the engine allocates device memory). Runs with
-    prefetch_weights: vLLM writes the LoRA stacks only between steps, so an
-    apply launch may start streaming adapter weights while the preceding
-    kernel (the base layer's GEMM) finishes; activations are read after it."""
+    prefetch_weights and prefetch_inputs: vLLM writes the LoRA stacks only
+    between steps, and the kernel right before a LoRA call is the base
+    layer's GEMM (it reads x and writes y), so an apply launch may stream
+    adapter weights and x, and run its shrink, while that GEMM finishes; y is
+    read after it."""
     global _engine
     if _engine is None:
         from .config import WarpPipeConfig
         from .engine import WarpPipeEngine
 
-        _engine = WarpPipeEngine(WarpPipeConfig(prefetch_weights=True))
+        _engine = WarpPipeEngine(WarpPipeConfig(prefetch_weights=True, prefetch_inputs=True))
     return _engine
 
 
@@ -61,6 +63,8 @@ def apply_lora_linear(engine, y: torch.Tensor, x: torch.Tensor, lora_a_stacked: 
     x2 = x.reshape(-1, x.size(-1))
     if not add_inputs:
         y2.zero_()
+    if x2.data_ptr() != x.data_ptr():
+        engine.note_input_write()  # the reshape copied x right before the apply (prefetch_inputs)
     widths = [int(w) for w in output_slices]
     if len(set(widths)) == 1 and len(widths) > 1 and sum(widths) == y2.size(1):
         if not engine.add_lora_packed_nslice(y2, x2, list(lora_a_stacked), list(lora_b_stacked), scale, widths):

@@ -301,12 +301,14 @@ def run_ours(args, rank, world, local_rank):
 
     device = torch.device("cuda", local_rank)
     torch.cuda.set_device(device)
-    # prefetch_weights: the serving contract (adapter weights are static during
-    # a step) lets each apply launch start streaming weights while the
-    # previous launch finishes. The serving hooks (punica_wrapper.py,
-    # vllm_punica.py) build their engine with the same setting; the step
-    # without it is reported as `strict_order`.
-    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    # prefetch_weights + prefetch_inputs: the serving contract (adapter
+    # weights are static during a step, and the kernel right before a LoRA
+    # call never writes its x) lets each apply launch stream weights and x,
+    # and run its shrink, while the previous launch finishes. The serving
+    # hooks (punica_wrapper.py, vllm_punica.py) build their engine with the
+    # same settings; the step without them is reported as `strict_order`,
+    # with weights only as `weights_prefetch_only`.
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True, prefetch_inputs=True), device=device)
     plan = eng.apply_plan(torch.bfloat16, RANK)
     scale = 16.0 / RANK
 
@@ -490,7 +492,7 @@ def fp16_step(device, steps):
     (`--impl reference`, key `reference_gpu`) times on the same workload."""
     from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
 
-    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True, prefetch_inputs=True), device=device)
     idx = torch.as_tensor(make_ids(RESIDENT), device=device)
     stack = Stack(device, RESIDENT, dtype=torch.float16)
     calls = list(stack.calls())
@@ -509,12 +511,14 @@ def fp16_step(device, steps):
     return {"us_per_step": round(ms * 1e3, 2), "dtype": "fp16"}
 
 
-def strict_order(device, steps):
-    """The step with prefetch_weights off (strict stream order: no load of a
-    launch starts before the previous launch has finished)."""
+def strict_order(device, steps, prefetch_weights=False):
+    """The step without the serving contract's prefetch: prefetch_weights off
+    (strict stream order: no load of a launch starts before the previous
+    launch has finished), or weights only (x and the shrink wait for the
+    previous launch)."""
     from adapterslotsplusplus_b200 import WarpPipeConfig, WarpPipeEngine
 
-    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=False), device=device)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=prefetch_weights), device=device)
     ids = make_ids(RESIDENT)
     idx = torch.as_tensor(ids, device=device)
     stack = Stack(device, RESIDENT)
@@ -532,7 +536,7 @@ def strict_order(device, steps):
     ms = time_graph(g, lambda: eng.build_seg_bounds(idx), steps)
     del g, stack, calls, eng
     torch.cuda.empty_cache()
-    return {"us_per_step": round(ms * 1e3, 2), "prefetch_weights": False}
+    return {"us_per_step": round(ms * 1e3, 2), "prefetch_weights": prefetch_weights, "prefetch_inputs": False}
 
 
 def fused_slices(eng, device, steps):
@@ -756,7 +760,7 @@ def prefill_mix(device, iters=10):
     out = {}
     for name, kern, prefill in (("tcgen05_prefill", "auto", True), ("decode_cluster", "cluster", False),
                                 ("decode_split", "split", False)):
-        eng = WarpPipeEngine(WarpPipeConfig(max_tokens=T, prefetch_weights=True, kernel=kern), device=device)
+        eng = WarpPipeEngine(WarpPipeConfig(max_tokens=T, prefetch_weights=True, prefetch_inputs=True, kernel=kern), device=device)
         eng.build_seg_bounds(torch.as_tensor(ids, device=device), prefill=prefill)
 
         def step():
@@ -785,7 +789,7 @@ def prefill_profile_case(args):
             for _ in range(4)]
     x = torch.randn(T, HIDDEN, device=device, dtype=torch.bfloat16, generator=g) * 0.1
     y = torch.zeros(T, HIDDEN, device=device, dtype=torch.bfloat16)
-    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=T, prefetch_weights=True), device=device)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=T, prefetch_weights=True, prefetch_inputs=True), device=device)
     eng.build_seg_bounds(torch.as_tensor(ids, device=device), prefill=True)
     for i in range(args.launches):
         wa, wb = sets[i % len(sets)]
@@ -806,7 +810,7 @@ def config2_sweep(device, iters=5, ranks=(8, 16, 32, 64), residents=(1, 8, 64, 5
 
     d = o = HIDDEN
     hbm = measured_peaks().get("hbm_gbs") or 6650.0
-    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True, prefetch_inputs=True), device=device)
     rows = []
     g = torch.Generator(device=device).manual_seed(2)
     for r in ranks:
@@ -871,7 +875,7 @@ def config4(device, steps: int = 200, warmup: int = 10, seed: int = 4):
     per_layer = [("q", hid, hid, "h"), ("k", hid, hid, "h"), ("v", hid, hid, "h"), ("o", hid, hid, "a"),
                  ("gate", hid, inter, "h"), ("up", hid, inter, "h"), ("down", inter, hid, "i")]
     dims = [(d, o) for _ in range(layers) for _, d, o, _ in per_layer]
-    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True, prefetch_inputs=True), device=device)
     pool = AdapterPool(eng, slots, dims, rank=r, dtype=torch.bfloat16, max_adapters=tenants_total)
     sb = pool.slot_bytes
     # host store: one page-locked allocation, one blob per tenant; contents
@@ -1016,7 +1020,7 @@ def draft_step(device, iters: int = 20):
 
     tenants, seqs, la, r = 32, 8, 4, 16
     T = tenants * seqs * la
-    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True, prefetch_inputs=True), device=device)
     model = DraftDecoder(layers=12, hidden=768, heads=12, inter=3072, vocab=32000, device=device)
     dims = model.dims()
     pool = AdapterPool(eng, 128, dims, rank=r, max_adapters=1024)
@@ -1065,7 +1069,7 @@ def config3(args, rank, world, local_rank):
              ("o", hid, hid, "attn", "row"), ("gate", hid, inter, "h", "col"), ("up", hid, inter, "h", "col"),
              ("down", inter, hid, "inter", "row")]
     device = torch.device("cuda", local_rank)
-    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True), device=device)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True, prefetch_inputs=True), device=device)
     g = torch.Generator(device=device).manual_seed(3 + 1000 * rank)
     sets = []
     for _ in range(4):
@@ -1145,7 +1149,7 @@ def profile_case(args):
     shapes = {"q": (HIDDEN, HIDDEN), "gate": (HIDDEN, INTER), "down": (INTER, HIDDEN)}
     d, o = shapes[args.profile_case]
     device = torch.device("cuda", 0)
-    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True, kernel=args.kernel), device=device)
+    eng = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True, prefetch_inputs=True, kernel=args.kernel), device=device)
     g = torch.Generator(device=device).manual_seed(0)
     sets = [(torch.randn(RESIDENT, 1, RANK, d, device=device, dtype=torch.bfloat16, generator=g) * 0.02,
              torch.randn(RESIDENT, 1, o, RANK, device=device, dtype=torch.bfloat16, generator=g) * 0.02)
@@ -1240,6 +1244,7 @@ def main():
             result["config2_sweep"] = config2_sweep(device)
         result["fused_slices"] = fused_slices(eng, device, max(3, args.steps // 2))
         result["strict_order"] = strict_order(device, max(3, args.steps // 2))
+        result["weights_prefetch_only"] = strict_order(device, max(3, args.steps // 2), prefetch_weights=True)
         result["fp16_step"] = fp16_step(device, max(3, args.steps // 2))
         result["prefill_mix"] = prefill_mix(device)
         result["config4"] = config4(device)

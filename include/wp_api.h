@@ -81,6 +81,13 @@ typedef struct wp_config {
   int32_t peer_wait_ms;      /* bound of each in-kernel wait on a tensor-parallel peer
                                 (wp_add_lora_row_parallel); 0 = 5000 ms. On expiry the
                                 kernel sets WP_ERR_DEVICE_TIMEOUT's flag and returns. */
+  int32_t prefetch_inputs;   /* with use_pdl and prefetch_weights: a fused live call loads its
+                                x and runs its whole shrink phase before the previous kernel
+                                on the stream finishes; only the y loads wait for it. The
+                                caller promises that the kernel right before each apply call
+                                never writes that call's x (serving: it is the base layer's
+                                GEMM, which reads x and writes y); wp_note_input_write lifts
+                                the promise for one call. Not used with tensor parallelism. */
 } wp_config;
 
 /* One entry of the segment table, as read back by wp_read_seg_table.
@@ -213,6 +220,12 @@ int wp_shrink(wp_handle* h, const void* X, void* H, int32_t d_model, int32_t ran
  * H: device [T, r] fp32; Y: device [T, o] (dtype), updated in place. */
 int wp_expand(wp_handle* h, const void* H, void* Y, int32_t out_features, int32_t rank, int32_t T,
               int32_t dtype, void* stream);
+
+/* The kernel the caller just enqueued on the stream wrote the next apply
+ * call's x (e.g. a copy that made it contiguous): that call loads x only
+ * after the dependency wait, whatever prefetch_inputs says. No reference
+ * counterpart (the reference has no programmatic dependent launch). */
+int wp_note_input_write(wp_handle* h);
 
 /* Replaces WarpPipeExtension::add_lora_packed (warp_pipe_bindings.cpp:195-234)
  * -> bgmv_shrink_dsak_kernel + bgmv_expand_dsak_kernel (warp_pipe_r32.cu:280-423),
