@@ -262,8 +262,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const bool registry = !LF && a.registry != 0;
   const bool y_tma = LF || a.y_tma != 0;
   const int nslices = LF == 1 ? 1 : a.nslices;
+  // the live fused instantiations (not the peer-exchange one) run only with
+  // clusters of 2 and sliced tensor maps (the launcher sends other calls to
+  // the general instantiation): their code is compiled for exactly that
+  constexpr bool kFast = LF != 0 && !TPX;
   const uint32_t q = cluster_ctarank();
-  const uint32_t CL = cluster_nctarank();
+  const uint32_t CL = kFast ? 2u : cluster_nctarank();
   const int cid = static_cast<int>(cluster_id_x());
   const int G = static_cast<int>(cluster_count_x());
   std::conditional_t<TR, Trace, TraceOff> tr;
@@ -332,7 +336,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   // decode variant: the y box of an expand stage goes back to global memory
   // with one tensor store when its rows are exactly the segment's rows
   auto y_by_tma = [&](int n) -> bool {
-    return y_tma && a.o_sliced && (n == 8 || n == 16 || n == 32);
+    return y_tma && (kFast || a.o_sliced) && (n == 8 || n == 16 || n == 32);
   };
 
   // ---- segment table of this cluster (all threads) -------------------------
@@ -469,7 +473,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     if (sub < nA) {
       const int k0 = kA0 + sub * C::KC;
       mbar_arrive_expect_tx(bar, 4 * C::ABOX + 4 * g.box_bytes);
-      if (a.d_sliced) {
+      if (kFast || a.d_sliced) {
         tma_load_4d_ef(st, g.amap, 0, 0, k0 / kBoxCols, g.aid, bar, ef);
       } else {
 #pragma unroll
@@ -492,7 +496,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   auto issue_x = [&](const SegTma& g, int sub, uint8_t* st, uint64_t* bar) {
     if (sub < nA) {
       const int k0 = kA0 + sub * C::KC;
-      if (a.d_sliced) {
+      if (kFast || a.d_sliced) {
         tma_load_3d(st + 4 * C::ABOX, g.xmap, 0, g.tok, k0 / kBoxCols, bar);
       } else {
 #pragma unroll
@@ -500,7 +504,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       }
     } else if (y_tma) {
       const int oc = oB0 + (sub - nA) * C::W;
-      if (a.o_sliced) {
+      if (kFast || a.o_sliced) {
         tma_load_3d(st, g.ymap, 0, g.tok, oc / kBoxCols, bar);
       } else {
 #pragma unroll
@@ -1172,12 +1176,14 @@ struct ApplyKernel {
 template <typename T, int R>
 cudaError_t apply_variant(const ApplyArgs& a, const LaunchCfg& lc) {
   const bool live_fused = a.mode == kModeFused && !a.registry && a.y_tma;
-  const int lf = live_fused ? (a.nslices > 1 ? 2 : 1) : 0;
   if (a.tp_world > 1) {
     // row-parallel exchange over peer memory (untraced): live fused single-slice calls
-    if (lf != 1) return cudaErrorInvalidValue;
+    if (!live_fused || a.nslices > 1) return cudaErrorInvalidValue;
     return ApplyKernel<T, R, false, 1, true>::launch(a, lc);
   }
+  // the live fused instantiations are compiled for clusters of 2 and sliced maps
+  const bool fast = live_fused && lc.cluster == 2 && a.d_sliced && a.o_sliced;
+  const int lf = fast ? (a.nslices > 1 ? 2 : 1) : 0;
   if (a.trace) return lf == 1 ? ApplyKernel<T, R, true, 1>::launch(a, lc) : ApplyKernel<T, R, true, 0>::launch(a, lc);
   if (lf == 1) return ApplyKernel<T, R, false, 1>::launch(a, lc);
   if (lf == 2) return ApplyKernel<T, R, false, 2>::launch(a, lc);

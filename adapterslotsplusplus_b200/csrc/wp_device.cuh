@@ -268,6 +268,16 @@ __device__ __forceinline__ uint32_t cluster_count_x() {
 }
 
 // Hardware cluster barrier (all threads of every CTA of the cluster).
+// Arrives on named barrier `id` (of `nthreads`) without waiting.
+__device__ __forceinline__ void named_arrive(int id, int nthreads) {
+  asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
+}
+
+// Split cluster barrier: arrive (whole warp, converged; releases this
+// thread's prior writes to the cluster) and, later, wait (per thread).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+__device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
+
 __device__ __forceinline__ void cluster_sync_hw() {
   asm volatile("barrier.cluster.arrive.release.aligned;\n\tbarrier.cluster.wait.acquire.aligned;" ::: "memory");
 }
