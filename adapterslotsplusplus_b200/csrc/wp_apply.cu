@@ -272,18 +272,19 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const int G = static_cast<int>(cluster_count_x());
   std::conditional_t<TR, Trace, TraceOff> tr;
   tr.init(a.trace, tid == 0);
-  // The plan words of this cluster are loaded first thing: the load's latency
-  // (long while the previous kernel streams at full bandwidth) overlaps the
-  // barrier set-up below. Threads 0-2: header, count, half; threads 32..:
-  // the descriptors of the cluster's rounds.
+  // The plan words of this cluster are loaded first thing, by the store warp
+  // (idle at start-up; lane 0: header, 1: count, 2: half, 3..: the
+  // descriptors of the cluster's rounds): the load's latency (long while the
+  // previous kernel streams at full bandwidth) overlaps the barrier set-up
+  // below, and thread 0's barrier-init fence does not wait for it.
   const bool use_plan = nslices <= 1 && a.plan != nullptr;
   int4 plan_word = make_int4(0, 0, 0, 0);
-  if (use_plan && cid < kPlanMaxClusters) {
-    if (tid == 0) plan_word = __ldcg(&a.plan->hdr);
-    if (tid == 1) plan_word.x = __ldcg(&a.plan->count[cid]);
-    if (tid == 2) plan_word.x = __ldcg(&a.plan->half[cid]);
-    if (tid >= 32 && tid < 32 + 2 * kPlanRounds) {
-      const int j = tid - 32;
+  if (use_plan && cid < kPlanMaxClusters && warp == kStoreWarp) {
+    if (lane == 0) plan_word = __ldcg(&a.plan->hdr);
+    if (lane == 1) plan_word.x = __ldcg(&a.plan->count[cid]);
+    if (lane == 2) plan_word.x = __ldcg(&a.plan->half[cid]);
+    if (lane >= 3 && lane < 3 + 2 * kPlanRounds) {
+      const int j = lane - 3;
       const int slot = min((j >> 1) * G + cid, kPlanRounds * kPlanMaxClusters - 1);
       plan_word = __ldcg(reinterpret_cast<const int4*>(&a.plan->seg[slot]) + (j & 1));
     }
@@ -320,7 +321,14 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
   }
   __syncthreads();
-  cluster_sync_hw();  // every CTA's cluster barrier is initialised before anyone arrives on it
+  unsigned long long t_init = 0;  // tracing: barriers initialised
+  if constexpr (TR) t_init = global_timer_ns();
+  // Split cluster barrier: everyone arrives now (releasing the barrier
+  // initialisation); the compute warps wait only before their first remote
+  // operation on a peer's barriers (the exchange, or the closing cluster
+  // barrier), the producer and store warps on their way out. Waiting here
+  // would cost the time the partner CTA takes to start.
+  cluster_arrive();
   unsigned long long t_synced = 0;  // tracing: after the set-up
   if constexpr (TR) t_synced = global_timer_ns();
 
@@ -357,10 +365,12 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   };
   auto read_plan = [&]() -> bool {
     int4* sh = reinterpret_cast<int4*>(Ps);  // scratch: header, count, half
-    if (tid == 0) sh[0] = plan_word;
-    if (tid == 1) reinterpret_cast<int*>(sh + 1)[0] = plan_word.x;
-    if (tid == 2) reinterpret_cast<int*>(sh + 1)[1] = plan_word.x;
-    if (tid >= 32 && tid < 32 + 2 * kPlanRounds) sdesc[tid - 32] = plan_word;
+    if (warp == kStoreWarp) {
+      if (lane == 0) sh[0] = plan_word;
+      if (lane == 1) reinterpret_cast<int*>(sh + 1)[0] = plan_word.x;
+      if (lane == 2) reinterpret_cast<int*>(sh + 1)[1] = plan_word.x;
+      if (lane >= 3 && lane < 3 + 2 * kPlanRounds) sdesc[lane - 3] = plan_word;
+    }
     __syncthreads();
     const int4 hdr = sh[0];
     const int count = reinterpret_cast<const int*>(sh + 1)[0];
@@ -425,7 +435,9 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     }
     __syncthreads();
     tr.stage(trc);
-    if (trc && tid == 0) trc[8 + 4] = t_synced;  // mark 4: set-up done (mark 7: table read)
+    if (trc && tid == 0) {
+      trc[8 + 4] = t_synced;  // mark 4: set-up done (mark 7: table read)
+    }
   }
   if (tid == 0) trace_rec_mark<TR>(trc, 7);
   const int total = nmine * ups;
@@ -518,7 +530,10 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const bool xpre = LF != 0 && !TPX && a.prefetch_weights && a.prefetch_inputs;
   if (warp == kProducerWarp) {
     // ======================= producer warp ===================================
-    if (lane == 0) {
+    // Lanes 1-31 leave at once: a lane blocked in a dependency or cluster wait
+    // holds up the whole warp, lane 0's pre-dependency issue included.
+    if (lane != 0) return;
+    {
       const uint64_t ef = l2_evict_first_policy();  // adapter weights stream through L2 once
       trace_rec_mark<TR>(trc, 9);
       // With prefetched weights the first `first` units get their weights
@@ -535,6 +550,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       // the drain after an error waits for every armed stage.
       for (int sj = 0; sj < nmine && !(*s_bad && u >= first); ++sj) {
         const SegTma g = seg_tma(desc(sj));
+        if constexpr (TR)
+          if (trc && sj == 0) trc[8 + 11] = global_timer_ns();  // mark 11: first segment's TMA parameters
         for (int sub = 0; sub < ups; ++sub) {
           const bool x_free = xpre && sub < nA;  // activations that need no dependency wait
           if (!met && u >= first && !x_free) {
@@ -549,6 +566,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
             if (*s_bad) break;
           }
           uint8_t* st = stage_base + stage * C::STAGE;
+          if constexpr (TR)
+            if (trc && u == 0) trc[8 + 5] = global_timer_ns();  // mark 5: first unit's issue starts
           issue_w(g, sub, st, &full[stage], ef);
           if (met || x_free) issue_x(g, sub, st, &full[stage]);
           trace_rec_unit<TR>(trc, u, 7);
@@ -567,10 +586,8 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         pdl_launch_dependents();
         trace_rec_mark<TR>(trc, 6);
       }
-    } else if (a.prefetch_weights) {
-      pdl_wait_prior();
-      pdl_launch_dependents();
     }
+    cluster_wait();  // completes the start-up cluster barrier
     return;
   }
 
@@ -579,11 +596,11 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
     // For every expand stage whose y box is stored by TMA: wait until the
     // compute warps have written it (ydone), store it, wait until the store
     // has read shared memory, then free the stage for the producer.
+    if (lane != 0) return;  // idle lanes leave (see the producer warp)
     if (a.prefetch_weights) {
       pdl_wait_prior();
       pdl_launch_dependents();
     }
-    if (lane != 0) return;
     if (a.prefetch_weights) {
       // The first stages' activations, as soon as the dependency is met,
       // whether or not the producer has armed their barriers yet: bytes that
@@ -598,7 +615,10 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
           if (!(xpre && sub < nA)) issue_x(g, sub, stage_base + u * C::STAGE, &full[u]);
       }
     }
-    if (!do_ex) return;
+    if (!do_ex) {
+      cluster_wait();
+      return;
+    }
     uint32_t ypar = 0u;
     int u = 0;
     for (int sj = 0; sj < nmine; ++sj) {
@@ -627,6 +647,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       }
     }
     bulk_wait_all();
+    cluster_wait();
     return;
   }
 
@@ -650,6 +671,13 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const int c = lane & 3;
   int kc = 0;  // next stage-unit
   uint32_t cph = 0;  // cluster barrier phase
+  bool peers_ready = false;  // the start-up cluster barrier has been waited for
+  auto wait_peers = [&]() {
+    if (!peers_ready) {
+      cluster_wait();
+      peers_ready = true;
+    }
+  };
   // Wait for stage `kc` (calling threads only), with the optional trace.
   auto wait_full = [&](int stage) -> bool {
     if (*s_bad) return false;
@@ -779,6 +807,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       // its own sums in registers. A slot of a segment parity is rewritten
       // only after every peer has released it (rx_free). Every CTA adds the
       // ranks' partials in rank order, so all of them get the same H.
+      wait_peers();  // the peer's receive slots and barriers are initialised
       const int par = sj & 1;
       const uint32_t use = static_cast<uint32_t>(sj >> 1);  // uses of this parity so far
       float* rx = Rx + par * C::CLMAX * C::PSLOT;
@@ -1083,6 +1112,7 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   // was consumed, and the releases of the last two segments are not sent.
   // No data crosses this barrier, so it needs no release fence (a fence
   // would wait for this thread's outstanding y stores).
+  wait_peers();
   if (CL > 1 && !cluster_barrier_relaxed_bounded(cbar, cph, CL, kBarCompute, kComputeThreads, a.err)) *s_bad = 1;
   if (*s_bad) {
     // drain: copies may still be in flight into stages issued but not consumed

@@ -290,7 +290,10 @@ __global__ void __launch_bounds__(kSThreads, 1) split_kernel(const __grid_consta
   const int first = min(S, U);  // stages issued before any is consumed
   if (warp == kSProducer) {
     // =========================== producer ====================================
-    if (lane == 0) {
+    // Lanes 1-31 leave at once: a lane blocked in the dependency wait would
+    // hold up the whole warp, lane 0's pre-dependency issue included.
+    if (lane != 0) return;
+    {
       const uint64_t ef = l2_evict_first_policy();
       if (a.prefetch_weights) {
         // the store thread loads these stages' activations as soon as the
@@ -331,9 +334,6 @@ __global__ void __launch_bounds__(kSThreads, 1) split_kernel(const __grid_consta
           ++s;
         }
       }
-    } else if (a.prefetch_weights) {
-      pdl_wait_prior();
-      pdl_launch_dependents();
     }
     return;
   }

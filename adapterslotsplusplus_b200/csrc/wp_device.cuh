@@ -273,9 +273,11 @@ __device__ __forceinline__ void named_arrive(int id, int nthreads) {
   asm volatile("bar.arrive %0, %1;" ::"r"(id), "r"(nthreads) : "memory");
 }
 
-// Split cluster barrier: arrive (whole warp, converged; releases this
-// thread's prior writes to the cluster) and, later, wait (per thread).
-__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.release.aligned;" ::: "memory"); }
+// Split cluster barrier: arrive (whole warp, converged; relaxed: the
+// barrier initialisation it publishes is released by
+// fence.mbarrier_init.release.cluster, and a release arrive would also wait
+// for this thread's loads in flight) and, later, wait (per thread).
+__device__ __forceinline__ void cluster_arrive() { asm volatile("barrier.cluster.arrive.relaxed.aligned;" ::: "memory"); }
 __device__ __forceinline__ void cluster_wait() { asm volatile("barrier.cluster.wait.acquire;" ::: "memory"); }
 
 __device__ __forceinline__ void cluster_sync_hw() {

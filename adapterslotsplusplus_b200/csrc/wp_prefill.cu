@@ -318,7 +318,10 @@ __global__ void __launch_bounds__(kPfExThreads, 1) prefill_expand_kernel(const _
   const uint32_t tbase = *s_tmem;
 
   if (warp == kPfExProd) {
-    if (lane == 0) {
+    // Lanes 1-31 leave at once: a lane blocked in the dependency wait would
+    // hold up the whole warp, lane 0's pre-dependency issue included.
+    if (lane != 0) return;
+    {
       prefetch_tmap(&a.tmap_b64);
       prefetch_tmap(&a.tmap_y128);
       const uint64_t ef = l2_evict_first_policy();
@@ -343,9 +346,6 @@ __global__ void __launch_bounds__(kPfExThreads, 1) prefill_expand_kernel(const _
         pdl_wait_prior();
         pdl_launch_dependents();
       }
-    } else {
-      pdl_wait_prior();
-      pdl_launch_dependents();
     }
     return;
   }
