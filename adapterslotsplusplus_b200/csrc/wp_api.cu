@@ -904,13 +904,16 @@ int kernel_choice(const wp_handle* h) {
 
 // Automatic choice for a fused live-mode call, from a cost model of the two
 // decode kernels fitted to B200 measurements (rank 32, bf16, 256 tokens,
-// 1-512 resident adapters; us per launch inside a CUDA graph):
-//   clustered: ~2.1 + 0.49 x (pipeline stages of the busiest CTA), where a
+// 1-512 resident adapters, q / gate / down shapes; us per launch inside a
+// CUDA graph):
+//   clustered: ~2.0 + 0.33 x (pipeline stages of the busiest CTA), where a
 //     segment's CTA pair streams half of d each and a helper pair halves the
 //     output columns when clusters are left over;
 //   balanced ("split"): ~9.2 + 0.9 x (stages per CTA with every segment's
 //     stages spread over the whole grid) -- its flag exchange through L2
 //     costs a fixed ~7 us more.
+// On the measured shapes the clustered kernel is always the faster one; the
+// balanced kernel wins only for a few segments of a very large d or o.
 // The segment count is the latest segmenter's (read without a sync); before
 // one has landed, the bound min(T, A + ceil(T / 32)) for A adapters among T
 // tokens stands in.
@@ -939,7 +942,7 @@ bool auto_split(wp_handle* h, cudaStream_t stream, int T, int64_t num_adapters, 
   } else {
     busiest = (nseg + clusters - 1) / clusters * (nA + nB);
   }
-  const double cost_cluster = 2.1 + 0.49 * static_cast<double>(busiest);
+  const double cost_cluster = 2.0 + 0.33 * static_cast<double>(busiest);
   const double per_cta = static_cast<double>(nseg * (stages(d) + stages(o))) / static_cast<double>(h->num_sms);
   const double cost_split = 9.2 + 0.9 * per_cta;
   return cost_split < cost_cluster;
