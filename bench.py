@@ -241,9 +241,10 @@ def tp_parity(eng, tpa, device, rank, world, scale, idx_dev):
     """Tensor-parallel results of layer 0's q (column-parallel), o and down
     (row-parallel) against an fp32 torch computation of the unsharded call on
     the same GPU, on identical inputs (every rank draws the full weights from
-    one seed and keeps its shard). Row-parallel partial outputs (bf16) are
-    summed with an all-reduce, as the base layer's all-reduce would, so they
-    carry one more bf16 rounding than a single-GPU call. Returns, on every
+    one seed and keeps its shard). Row-parallel partial outputs (bf16, as the
+    kernel wrote them) are summed in fp32 with an all-reduce, as the base
+    layer's all-reduce would; the rounding of that sum back to bf16 is the
+    base model's, not the LoRA kernel's, and is left out. Returns, on every
     rank, max-abs error / RMS per projection and whether all ranks hold
     bit-identical full outputs."""
     import torch.distributed as dist
@@ -277,7 +278,7 @@ def tp_parity(eng, tpa, device, rank, world, scale, idx_dev):
                 assert tpa.row_parallel(yp, shard_row_input(x, rank, world), shard_row(wa, rank, world), wb, scale)
                 ypf = yp.float()
                 dist.all_reduce(ypf)
-                full = ypf.to(torch.bfloat16)
+                full = ypf
             else:
                 full = y0.clone()
                 assert tpa.row_parallel(full, shard_row_input(x, rank, world), shard_row(wa, rank, world), wb, scale)
