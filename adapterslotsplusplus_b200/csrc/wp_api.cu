@@ -104,8 +104,10 @@ struct wp_handle {
   int nseg_hint = -1;
   int last_kernel = -1;  // wp_last_apply_kernel
   // the segmenter's per-cluster assignment of the live table for plan_g clusters
+  // [0]: clusters of the common launch; [1]: clusters of 4 (few-segment calls)
   wp::ClusterPlan* d_plan = nullptr;
   int plan_g = 0;
+  int plan_g4 = 0;  // clusters of the clusters-of-4 launch (0: none)
   int sync_cap = 0;
   int split_grid[8] = {};
 
@@ -395,8 +397,8 @@ int wp_create(const wp_config* cfg_in, wp_handle** out) {
   if ((e = cudaMalloc(&h->d_sync, sizeof(int) * 3 * cap)) != cudaSuccess) return bail("segment counters", e);
   if ((e = cudaHostAlloc(&h->h_nseg, sizeof(int) * 4, cudaHostAllocDefault)) != cudaSuccess)
     return bail("segment count buffer", e);
-  if ((e = cudaMalloc(&h->d_plan, sizeof(wp::ClusterPlan))) != cudaSuccess) return bail("cluster plan", e);
-  cudaMemset(h->d_plan, 0, sizeof(wp::ClusterPlan));
+  if ((e = cudaMalloc(&h->d_plan, 2 * sizeof(wp::ClusterPlan))) != cudaSuccess) return bail("cluster plan", e);
+  cudaMemset(h->d_plan, 0, 2 * sizeof(wp::ClusterPlan));
   cudaEventCreateWithFlags(&h->nseg_ready, cudaEventDisableTiming);
   cudaMemset(h->d_sync, 0, sizeof(int) * 3 * cap);
   h->sync_cap = cap;
@@ -755,6 +757,7 @@ int wp_build_segments(wp_handle* h, const int32_t* ids, const int32_t* offs, int
 }  // extern "C"
 namespace {
 void apply_plan(wp_handle* h, int dtype, int r, int* cluster, int* grid);
+int plan_clusters4(wp_handle* h);
 }  // namespace
 extern "C" {
 
@@ -780,6 +783,7 @@ int wp_build_seg_bounds_ex(wp_handle* h, const void* idx, int32_t idx_dtype, int
     int c = 1, g = 1;
     apply_plan(h, WP_DTYPE_BF16, 32, &c, &g);
     h->plan_g = g / std::max(c, 1);
+    h->plan_g4 = plan_clusters4(h);
   }
   const bool prefill =
       flags == WP_SEG_PREFILL || (flags == WP_SEG_AUTO && h->cfg.prefill_tokens > 0 && T >= h->cfg.prefill_tokens);
@@ -791,8 +795,9 @@ int wp_build_seg_bounds_ex(wp_handle* h, const void* idx, int32_t idx_dtype, int
     pf.short_num = h->d_short_num;
     pf.min_run = wp::kPrefillMinRun;
   }
-  cudaError_t e = wp::launch_seg_bounds(idx, idx_dtype, T, h->d_live, h->d_live_num, h->d_plan, h->plan_g,
-                                        h->d_run_starts, stream, nullptr, 0, nullptr, pf);
+  cudaError_t e = wp::launch_seg_bounds(idx, idx_dtype, T, h->d_live, h->d_live_num, h->d_plan,
+                                        h->plan_g | (h->plan_g4 << 16), h->d_run_starts, stream, nullptr, 0, nullptr,
+                                        pf);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "build_seg_bounds launch: %s", cudaGetErrorString(e));
   h->live_prefill = prefill;
   ++h->launches;
@@ -885,6 +890,21 @@ void apply_plan(wp_handle* h, int dtype, int r, int* cluster, int* grid) {
 
 int round_up(int v, int m) { return (v + m - 1) / m * m; }
 
+// Clusters of the clusters-of-4 launch (bf16, rank 32: the same count for
+// every rank and dtype on B200), within the plan's capacity; 0 when off
+// (WP_CLUSTER4=0, a tuning knob) or not schedulable.
+int plan_clusters4(wp_handle* h) {
+  static const bool off = [] {
+    const char* e = std::getenv("WP_CLUSTER4");
+    return e && std::strcmp(e, "0") == 0;
+  }();
+  if (off) return 0;
+  int g = wp::apply_max_grid4(WP_DTYPE_BF16, 32);
+  if (h->cfg.ctas_per_sm > 0) g = std::min(g, h->num_sms * h->cfg.ctas_per_sm / 4 * 4);
+  g = std::min(g / 4, wp::kPlanMaxClusters);
+  return g >= 2 ? g : 0;
+}
+
 // Kernel choice (wp_config.kernel; 0 = automatic, or WP_KERNEL when set, a
 // tuning knob): 1 = clustered, 2 = balanced ("split") for fused live-mode
 // calls. Returns 0 for split, 1 for clustered, -1 for automatic.
@@ -917,8 +937,9 @@ int kernel_choice(const wp_handle* h) {
 // The segment count is the latest segmenter's (read without a sync); before
 // one has landed, the bound min(T, A + ceil(T / 32)) for A adapters among T
 // tokens stands in.
-bool auto_split(wp_handle* h, cudaStream_t stream, int T, int64_t num_adapters, int clusters, int cluster, int d,
-                int o) {
+// The latest segmenter's segment count, once its copy to pinned memory has
+// landed (checked without a sync, outside stream capture); -1 before.
+int nseg_latest(wp_handle* h, cudaStream_t stream) {
   cudaStreamCaptureStatus cs = cudaStreamCaptureStatusNone;
   if (h->nseg_pending && cudaStreamIsCapturing(stream, &cs) == cudaSuccess && cs == cudaStreamCaptureStatusNone &&
       cudaEventQuery(h->nseg_ready) == cudaSuccess) {
@@ -926,7 +947,12 @@ bool auto_split(wp_handle* h, cudaStream_t stream, int T, int64_t num_adapters, 
     h->nseg_pending = false;
   }
   cudaGetLastError();  // a not-ready query is not an error
-  int64_t nseg = h->nseg_hint;
+  return h->nseg_hint;
+}
+
+bool auto_split(wp_handle* h, cudaStream_t stream, int T, int64_t num_adapters, int clusters, int cluster, int d,
+                int o) {
+  int64_t nseg = nseg_latest(h, stream);
   if (nseg < 0) nseg = std::min<int64_t>(T, std::max<int64_t>(num_adapters, 1) + (T + wp::kSegTokens - 1) / wp::kSegTokens);
   if (nseg <= 0 || clusters <= 0) return false;
   const int64_t cl = std::max(cluster, 1);
@@ -1079,12 +1105,26 @@ int do_apply(wp_handle* h, int mode, int registry, const DevSeg* segs, const int
   }
   int cluster = 1, grid = 1;
   apply_plan(h, dtype, r, &cluster, &grid);
+  // Few segments (no more than the clusters of 4): clusters of 4 spread each
+  // segment's shrink and expand over four CTAs instead of two, which halves
+  // the busiest CTA's stages; with more segments a cluster would hold two.
+  // The segment count is the latest segmenter's (see auto_split).
+  if (cluster == 2 && h->plan_g4 > 0 && mode == wp::kModeFused && !registry && !h->tp_exchange && !h->trace_on &&
+      r <= 32 && a.y_tma && sliced(d) && sliced(o) && a.plan != nullptr) {
+    const int64_t nseg = nseg_latest(h, stream);
+    const int min_cols = 4 * wp::kStageCols;  // a cluster's output columns split four ways
+    if (nseg > 0 && nseg < h->plan_g4 && o >= 2 * min_cols && d >= min_cols) {
+      cluster = 4;
+      grid = 4 * h->plan_g4;
+      a.plan = h->d_plan + 1;
+    }
+  }
   a.split_len = round_up((std::max(d, 1) + cluster - 1) / cluster, wp::kStageK);
   a.oslice = round_up((std::max(o, 1) + cluster - 1) / cluster, wp::kStageCols);
   wp::LaunchCfg lc{grid, cluster, stream, pdl};
   cudaError_t e = wp::launch_apply(dtype, r, a, lc);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "apply launch: %s", cudaGetErrorString(e));
-  h->last_kernel = 1;
+  h->last_kernel = cluster == 4 ? 3 : 1;
   ++h->launches;
   h->last_was_segmenter = false;
   return WP_OK;
@@ -1890,9 +1930,11 @@ int wp_build_seg_bounds_pool(wp_handle* h, wp_pool* p, const void* idx, int32_t 
     int c = 1, g = 1;
     apply_plan(h, WP_DTYPE_BF16, 32, &c, &g);
     h->plan_g = g / std::max(c, 1);
+    h->plan_g4 = plan_clusters4(h);
   }
-  cudaError_t e = wp::launch_seg_bounds(idx, idx_dtype, T, h->d_live, h->d_live_num, h->d_plan, h->plan_g,
-                                        h->d_run_starts, stream, p->d_map, p->max_adapters, h->d_err);
+  cudaError_t e = wp::launch_seg_bounds(idx, idx_dtype, T, h->d_live, h->d_live_num, h->d_plan,
+                                        h->plan_g | (h->plan_g4 << 16), h->d_run_starts, stream, p->d_map,
+                                        p->max_adapters, h->d_err);
   if (e != cudaSuccess) return fail(h, WP_ERR_CUDA, "build_seg_bounds_pool launch: %s", cudaGetErrorString(e));
   h->live_prefill = false;
   ++h->launches;

@@ -108,7 +108,9 @@ struct IntC {
   static constexpr int value = N;
 };
 
-template <int R>
+// CLM: cluster ranks the receive slots serve (2; 4 for the clusters-of-4
+// instantiation of few-segment calls).
+template <int R, int CLM = 2>
 struct ApplyCfg {
   static constexpr int KC = kStageK;  // d elements per shrink stage (4 boxes)
   static constexpr int W = kStageCols;  // output columns per expand stage (4 boxes)
@@ -128,7 +130,7 @@ struct ApplyCfg {
   static constexpr int PSLOT = 32 * PITCH;
   static constexpr int PW = 8 * PSLOT * 4;
   // receive slots of the cluster exchange, [2 segment parities][CLMAX ranks]
-  static constexpr int CLMAX = 2;
+  static constexpr int CLMAX = CLM;
   static constexpr int RX = 2 * CLMAX * PSLOT * 4;
   static constexpr int FIXED = OFF_END + PW + RX + 1024;
   static constexpr int FIT = (kSmemMax - FIXED) / STAGE;
@@ -230,11 +232,13 @@ __device__ __noinline__ void table_fallback(const ApplyArgs& a, int S_sl, bool d
 
 // LF: the live fused call with a tensor-map-aligned y (the serving hot path),
 // compiled without the other modes' branches; 1 = one slice, 2 = several
-// slices (add_lora_packed_nslice). TR: per-CTA timeline trace. TPX:
-// row-parallel exchange over tensor-parallel peers' memory.
+// slices (add_lora_packed_nslice), 4 = one slice on clusters of 4 (calls
+// with fewer segments than clusters of 4: each segment's shrink and expand
+// spread over four CTAs). TR: per-CTA timeline trace. TPX: row-parallel
+// exchange over tensor-parallel peers' memory.
 template <typename T, int R, bool TR, int LF, bool TPX = false>
 __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constant__ ApplyArgs a) {
-  using C = ApplyCfg<R>;
+  using C = ApplyCfg<R, LF == 4 ? 4 : 2>;
   using E = Elem<T>;
   constexpr int S = C::STAGES;
   constexpr int PITCH = C::PITCH;
@@ -261,13 +265,13 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
   const bool producer = warp == kProducerWarp;
   const bool registry = !LF && a.registry != 0;
   const bool y_tma = LF || a.y_tma != 0;
-  const int nslices = LF == 1 ? 1 : a.nslices;
+  const int nslices = (LF == 1 || LF == 4) ? 1 : a.nslices;
   // the live fused instantiations (not the peer-exchange one) run only with
   // clusters of 2 and sliced tensor maps (the launcher sends other calls to
   // the general instantiation): their code is compiled for exactly that
   constexpr bool kFast = LF != 0 && !TPX;
   const uint32_t q = cluster_ctarank();
-  const uint32_t CL = kFast ? 2u : cluster_nctarank();
+  const uint32_t CL = kFast ? (LF == 4 ? 4u : 2u) : cluster_nctarank();
   const int cid = static_cast<int>(cluster_id_x());
   const int G = static_cast<int>(cluster_count_x());
   std::conditional_t<TR, Trace, TraceOff> tr;
@@ -1146,7 +1150,7 @@ namespace {
 
 template <typename T, int R, bool TR, int LF, bool TPX = false>
 struct ApplyKernel {
-  using C = ApplyCfg<R>;
+  using C = ApplyCfg<R, LF == 4 ? 4 : 2>;
   static bool prepare() {
     static std::atomic<uint64_t> done{0};
     int dev = 0;
@@ -1215,6 +1219,9 @@ cudaError_t apply_variant(const ApplyArgs& a, const LaunchCfg& lc) {
   const bool fast = live_fused && lc.cluster == 2 && a.d_sliced && a.o_sliced;
   const int lf = fast ? (a.nslices > 1 ? 2 : 1) : 0;
   if (a.trace) return lf == 1 ? ApplyKernel<T, R, true, 1>::launch(a, lc) : ApplyKernel<T, R, true, 0>::launch(a, lc);
+  // few-segment calls on clusters of 4 (ranks 8-32; the host picks it)
+  if (lf == 0 && live_fused && lc.cluster == 4 && a.d_sliced && a.o_sliced && a.nslices <= 1 && R <= 32 && !a.trace)
+    return ApplyKernel<T, R <= 32 ? R : 32, false, 4>::launch(a, lc);
   if (lf == 1) return ApplyKernel<T, R, false, 1>::launch(a, lc);
   if (lf == 2) return ApplyKernel<T, R, false, 2>::launch(a, lc);
   return ApplyKernel<T, R, false, 0>::launch(a, lc);
@@ -1250,6 +1257,16 @@ cudaError_t launch_apply(int dtype, int rank, const ApplyArgs& a, const LaunchCf
 
 int apply_max_grid(int dtype, int rank, int cluster) {
   return dtype == 1 ? max_grid_by_rank<__nv_bfloat16>(rank, cluster) : max_grid_by_rank<__half>(rank, cluster);
+}
+
+int apply_max_grid4(int dtype, int rank) {
+  if (rank > 32) return 0;
+  switch (rank) {
+    case 8: return dtype == 1 ? ApplyKernel<__nv_bfloat16, 8, false, 4>::max_grid(4) : ApplyKernel<__half, 8, false, 4>::max_grid(4);
+    case 16: return dtype == 1 ? ApplyKernel<__nv_bfloat16, 16, false, 4>::max_grid(4) : ApplyKernel<__half, 16, false, 4>::max_grid(4);
+    case 32: return dtype == 1 ? ApplyKernel<__nv_bfloat16, 32, false, 4>::max_grid(4) : ApplyKernel<__half, 32, false, 4>::max_grid(4);
+    default: return 0;
+  }
 }
 
 }  // namespace wp

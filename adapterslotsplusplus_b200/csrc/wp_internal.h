@@ -191,6 +191,8 @@ int apply_split_max_grid(int dtype, int rank);
 // Largest co-resident persistent grid for the apply kernel of (dtype, rank)
 // with clusters of `cluster` CTAs (0 if that cluster size cannot be scheduled).
 int apply_max_grid(int dtype, int rank, int cluster);
+// co-resident CTAs of the clusters-of-4 live fused instantiation (ranks 8-32; else 0)
+int apply_max_grid4(int dtype, int rank);
 
 // idx_dtype: WP_DTYPE_I32 or WP_DTYPE_I64.
 // Prefill mode of the segmenter (wp_segment.cu): tiles of long runs and the

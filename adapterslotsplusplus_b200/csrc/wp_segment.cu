@@ -208,8 +208,14 @@ __global__ void __launch_bounds__(kSegThreads, 1)
     }
   }
   if (plan) {
+    // plan_g: clusters of the common launch (low 16 bits) and, when nonzero,
+    // of the clusters-of-4 launch of few-segment calls (high bits; plan + 1)
     __syncthreads();  // the table (global memory, written by this block) is complete
-    write_cluster_plan(segs, nseg, plan, plan_g);
+    write_cluster_plan(segs, nseg, plan, plan_g & 0xffff);
+    if (plan_g >> 16) {
+      __syncthreads();
+      write_cluster_plan(segs, nseg, plan + 1, plan_g >> 16);
+    }
   }
 }
 

@@ -372,7 +372,14 @@ class WarpPipeEngine:
         """Name of the kernel of the latest apply launch ("split_kernel" or
         "apply_kernel"), or "" before the first one."""
         k = int(self._lib.wp_last_apply_kernel(self._h))
-        return {0: "split_kernel", 1: "apply_kernel", 2: "apply_kernel"}.get(k, "")
+        return {0: "split_kernel", 1: "apply_kernel", 2: "apply_kernel", 3: "apply_kernel"}.get(k, "")
+
+    def last_apply_cluster(self) -> int:
+        """Cluster size of the latest clustered apply launch: 4 for a fused
+        live call with fewer segments than clusters of 4, else 2 (0 for the
+        balanced kernel or before the first launch)."""
+        k = int(self._lib.wp_last_apply_kernel(self._h))
+        return {1: 2, 2: 2, 3: 4}.get(k, 0)
 
     def kernel_launches(self) -> int:
         return int(self._lib.wp_kernel_launch_count(self._h))

@@ -118,8 +118,9 @@ const char* wp_last_error(const wp_handle* h);
 int wp_rank_supported(int32_t rank);
 
 /* Kernel of the latest apply launch: 0 = balanced decode ("split_kernel"),
- * 1 = clustered decode ("apply_kernel", mma.sync variant), 2 = clustered
- * tcgen05 ("apply_kernel"), -1 = none yet. For reports and profiling. */
+ * 1 = clustered decode ("apply_kernel", clusters of 2), 3 = clustered decode
+ * on clusters of 4 (fused live calls with few segments), -1 = none yet.
+ * For reports and profiling. */
 int32_t wp_last_apply_kernel(const wp_handle* h);
 
 /* Number of kernels this handle has launched so far (all entry points). */
