@@ -115,18 +115,40 @@ def measured_peaks() -> dict:
 
 
 class ClockSampler:
-    """nvidia-smi SM clocks and throttle reasons sampled every 200 ms."""
+    """SM clocks and throttle reasons of GPU `index`, sampled every ~5 ms
+    through NVML (read-only queries) while the `with` block runs: the timed
+    region of a step is tens of ms, shorter than nvidia-smi's start-up.
+    Falls back to `nvidia-smi -lms 50` when NVML is not importable."""
 
     FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
               "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
               "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+    # NVML clock-event reason bits (nvml.h)
+    REASONS = {"sw_power_cap": 0x4, "hw_slowdown": 0x8, "sw_thermal_slowdown": 0x20, "hw_thermal_slowdown": 0x40}
 
     def __init__(self, index: int):
         self.index = index
         self.proc = None
+        self.nvml = None
+        self.stop = threading.Event()
+        self.samples: list[tuple[float, int]] = []  # (SM MHz, reason bits)
+        self.max_mhz = None
         self.lines: list[str] = []
 
     def __enter__(self):
+        try:
+            import pynvml
+
+            pynvml.nvmlInit()
+            h = pynvml.nvmlDeviceGetHandleByIndex(self.index)
+            self.max_mhz = float(pynvml.nvmlDeviceGetMaxClockInfo(h, pynvml.NVML_CLOCK_SM))
+            self.nvml = (pynvml, h)
+            self.samples.append(self._nvml_sample())
+            self.thread = threading.Thread(target=self._poll, daemon=True)
+            self.thread.start()
+            return self
+        except Exception:
+            self.nvml = None
         try:
             self.proc = subprocess.Popen(
                 ["nvidia-smi", "-i", str(self.index), f"--query-gpu={self.FIELDS}", "--format=csv,noheader,nounits",
@@ -137,11 +159,35 @@ class ClockSampler:
             self.proc = None
         return self
 
+    def _nvml_sample(self):
+        pynvml, h = self.nvml
+        mhz = float(pynvml.nvmlDeviceGetClockInfo(h, pynvml.NVML_CLOCK_SM))
+        try:
+            bits = int(pynvml.nvmlDeviceGetCurrentClocksEventReasons(h))
+        except AttributeError:
+            bits = int(pynvml.nvmlDeviceGetCurrentClocksThrottleReasons(h))
+        return mhz, bits
+
+    def _poll(self):
+        while not self.stop.wait(0.005):
+            try:
+                self.samples.append(self._nvml_sample())
+            except Exception:
+                return
+
     def _read(self):
         for line in self.proc.stdout:
             self.lines.append(line.strip())
 
     def __exit__(self, *exc):
+        if self.nvml is not None:
+            self.stop.set()
+            self.thread.join(timeout=1)
+            try:
+                self.samples.append(self._nvml_sample())
+                self.nvml[0].nvmlShutdown()
+            except Exception:
+                pass
         if self.proc is not None:
             self.proc.terminate()
             try:
@@ -150,7 +196,12 @@ class ClockSampler:
                 self.proc.kill()
 
     def summary(self) -> dict:
-        sm, mx, reasons = [], None, set()
+        sm, mx, reasons = [], self.max_mhz, set()
+        for mhz, bits in self.samples:
+            sm.append(mhz)
+            for n, b in self.REASONS.items():
+                if bits & b:
+                    reasons.add(n)
         names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
         for ln in self.lines:
             parts = [p.strip() for p in ln.split(",")]
@@ -165,7 +216,7 @@ class ClockSampler:
                 if v.lower() == "active":
                     reasons.add(n)
         return {"sm_mhz": float(np.median(sm)) if sm else None, "sm_max_mhz": mx, "reasons": sorted(reasons),
-                "samples": len(sm)}
+                "samples": len(sm), "source": "nvml" if self.nvml is not None else "nvidia-smi"}
 
 
 # ---------------------------------------------------------------------------
