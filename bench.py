@@ -1208,13 +1208,14 @@ def profile_case(args):
             for _ in range(8)]
     x = torch.randn(TOKENS, d, device=device, dtype=torch.bfloat16, generator=g) * 0.1
     y = torch.zeros(TOKENS, o, device=device, dtype=torch.bfloat16)
-    eng.build_seg_bounds(torch.as_tensor(make_ids(RESIDENT), device=device))
+    eng.build_seg_bounds(torch.as_tensor(make_ids(args.profile_resident), device=device))
     torch.cuda.synchronize()
     for i in range(args.launches):
         wa, wb = sets[i % len(sets)]
         eng.add_lora_packed(y, x, wa, wb, 16.0 / RANK)
     torch.cuda.synchronize()
     print(json.dumps({"profile_case": args.profile_case, "launches": args.launches, "kernel": eng.last_apply_kernel(),
+                      "cluster": eng.last_apply_cluster(), "resident": args.profile_resident,
                       "d": d, "o": o, "tokens": TOKENS, "rank": RANK}), flush=True)
 
 
@@ -1228,6 +1229,8 @@ def main():
     ap.add_argument("--cpu-layers", type=int, default=2, help="layers in the cpu_baseline sample")
     ap.add_argument("--profile-case", choices=["q", "gate", "down"], default=None,
                     help="run a few launches of one projection (for profilers) and exit")
+    ap.add_argument("--profile-resident", type=int, default=RESIDENT,
+                    help="resident adapters of --profile-case (Zipf routing over them)")
     ap.add_argument("--launches", type=int, default=12, help="launches of --profile-case")
     ap.add_argument("--kernel", choices=["auto", "cluster", "split"], default="auto",
                     help="apply kernel of --profile-case")
