@@ -127,11 +127,19 @@ struct ApplyCfg {
   static constexpr bool BTMA = R >= 16;  // B as swizzled tensor boxes (rank 8: one linear bulk copy)
   static constexpr uint32_t SWZ_MASK = R == 64 ? 0x70u : (R == 32 ? 0x30u : 0x10u);
   // shrink partials of the 8 compute warps (32 tokens x PITCH floats each) for the cross-warp sum
-  static constexpr int PSLOT = 32 * PITCH;
-  static constexpr int PW = 8 * PSLOT * 4;
-  // receive slots of the cluster exchange, [2 segment parities][CLMAX ranks]
+  static constexpr int PSLOT = 32 * PITCH;  // one segment's partial (32 token rows)
+  // The eight compute warps' partials are added in passes of PROWS token
+  // rows (one slot of PROWS rows per warp): fewer rows per pass leave more
+  // shared memory to the stage ring (rank 32: 6 stages instead of 5; rank
+  // 64: 3 instead of 2), at two more barriers per extra pass.
+  static constexpr int PROWS = R == 64 ? 16 : (R == 32 ? 8 : 32);
+  static constexpr int PWSLOT = PROWS * PITCH;
+  static constexpr int PW = 8 * PWSLOT * 4;
+  // receive slots of the cluster exchange, [2 segment parities][CLMAX - 1
+  // peers]: rank i's partial in slot i (i below this CTA's rank) or i - 1
   static constexpr int CLMAX = CLM;
-  static constexpr int RX = 2 * CLMAX * PSLOT * 4;
+  static constexpr int RXSLOTS = CLMAX - 1;
+  static constexpr int RX = 2 * RXSLOTS * PSLOT * 4;
   static constexpr int FIXED = OFF_END + PW + RX + 1024;
   static constexpr int FIT = (kSmemMax - FIXED) / STAGE;
   static constexpr int STAGES = FIT > 8 ? 8 : FIT;
@@ -789,56 +797,71 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
         default: shrink_units(IntC<4>{}); break;
       }
       tr.seg(0, sj);
-      // cross-warp sum: every warp parks its partial in a slot of its own;
-      // the eight slots are added per element below, in a fixed order
-      {
-        float* dst = Pw + warp * C::PSLOT;
-#pragma unroll
-        for (int mt = 0; mt < MT; ++mt)
-#pragma unroll
-          for (int j = 0; j < 4; ++j)
-#pragma unroll
-            for (int e = 0; e < 4; ++e) {
-              const int r = mt * 16 + g + (e >> 1) * 8;
-              const int t = j * 8 + 2 * c + (e & 1);
-              if (r < R) dst[t * PITCH + r] = acc[mt][j][e];
-            }
-      }
-      named_sync(kBarCompute, kComputeThreads);
-      // ---- 2. cluster exchange (push): each thread sums the eight slots of
-      // its elements and pushes them by st.async into this CTA's slot of
-      // every peer, completing bytes on the peer's rx_full barrier; it keeps
-      // its own sums in registers. A slot of a segment parity is rewritten
-      // only after every peer has released it (rx_free). Every CTA adds the
-      // ranks' partials in rank order, so all of them get the same H.
+      // ---- 2. cross-warp sum and cluster exchange (push), in passes of
+      // PROWS token rows: every warp parks the pass's rows of its partial in
+      // a slot of its own; each thread adds the eight slots of its elements
+      // in a fixed order and pushes the sums by st.async into this CTA's
+      // receive slot on every peer, completing bytes on the peer's rx_full
+      // barrier; it keeps its own sums in registers. A receive slot of a
+      // segment parity is rewritten only after every peer has released it
+      // (rx_free). Every CTA adds the ranks' partials in rank order, so all
+      // of them get the same H.
       wait_peers();  // the peer's receive slots and barriers are initialised
       const int par = sj & 1;
       const uint32_t use = static_cast<uint32_t>(sj >> 1);  // uses of this parity so far
-      float* rx = Rx + par * C::CLMAX * C::PSLOT;
+      float* rx = Rx + par * C::RXSLOTS * C::PSLOT;
+      // this CTA's receive slot of rank i's partial (i != q), and its own slot on rank i
+      auto rslot = [&](uint32_t i) -> uint32_t { return i < q ? i : i - 1; };
+      auto tslot = [&](uint32_t i) -> uint32_t { return q < i ? q : q - 1; };
       if (CL > 1 && use > 0 && !*s_bad && !mbar_wait_cluster_bounded(&rx_free[par], (use - 1) & 1, a.err)) *s_bad = 1;
       constexpr int Q4 = R / 4;  // 16-byte chunks per partial row
-      constexpr int KE = (32 * Q4 + kComputeThreads - 1) / kComputeThreads;  // elements per thread at most
+      constexpr int PR = C::PROWS;
+      constexpr int NP = 32 / PR;  // passes at most
+      constexpr int KE = (PR * Q4 + kComputeThreads - 1) / kComputeThreads;  // elements per thread and pass
       const int nch = n * Q4;
-      float4 own[KE];
-      if (!*s_bad) {
+      const int npass = (n + PR - 1) / PR;
+      float4 own[NP][KE];
 #pragma unroll
-        for (int k = 0; k < KE; ++k) {
-          const int e4 = tid + k * kComputeThreads;
-          if (e4 < nch) {
-            const int off = (e4 / Q4) * PITCH + (e4 % Q4) * 4;
-            float4 p[8];
+      for (int pp = 0; pp < NP; ++pp) {
+        if (pp < npass) {
+          if (pp > 0) named_sync(kBarCompute, kComputeThreads);  // the previous pass has read the slots
+          {
+            float* dst = Pw + warp * C::PWSLOT;
 #pragma unroll
-            for (int w = 0; w < 8; ++w) p[w] = *reinterpret_cast<const float4*>(Pw + w * C::PSLOT + off);
-            float4 v;
-            v.x = ((p[0].x + p[1].x) + (p[2].x + p[3].x)) + ((p[4].x + p[5].x) + (p[6].x + p[7].x));
-            v.y = ((p[0].y + p[1].y) + (p[2].y + p[3].y)) + ((p[4].y + p[5].y) + (p[6].y + p[7].y));
-            v.z = ((p[0].z + p[1].z) + (p[2].z + p[3].z)) + ((p[4].z + p[5].z) + (p[6].z + p[7].z));
-            v.w = ((p[0].w + p[1].w) + (p[2].w + p[3].w)) + ((p[4].w + p[5].w) + (p[6].w + p[7].w));
-            own[k] = v;
-            const uint32_t mine = smem_u32(rx + q * C::PSLOT + off);
-            for (uint32_t i = 1; i < CL; ++i) {
-              const uint32_t peer = (q + i) % CL;
-              st_async_v4(mapa(mine, peer), v, mapa(smem_u32(&rx_full[par]), peer));
+            for (int mt = 0; mt < MT; ++mt)
+#pragma unroll
+              for (int jj = 0; jj < PR / 8; ++jj)
+#pragma unroll
+                for (int e = 0; e < 4; ++e) {
+                  const int r = mt * 16 + g + (e >> 1) * 8;
+                  const int t = jj * 8 + 2 * c + (e & 1);  // row within the pass
+                  if (r < R) dst[t * PITCH + r] = acc[mt][pp * (PR / 8) + jj][e];
+                }
+          }
+          named_sync(kBarCompute, kComputeThreads);
+          if (!*s_bad) {
+            const int nq = min(PR, n - pp * PR) * Q4;
+#pragma unroll
+            for (int k = 0; k < KE; ++k) {
+              const int e4 = tid + k * kComputeThreads;
+              if (e4 < nq) {
+                const int offw = (e4 / Q4) * PITCH + (e4 % Q4) * 4;
+                float4 p[8];
+#pragma unroll
+                for (int w = 0; w < 8; ++w) p[w] = *reinterpret_cast<const float4*>(Pw + w * C::PWSLOT + offw);
+                float4 v;
+                v.x = ((p[0].x + p[1].x) + (p[2].x + p[3].x)) + ((p[4].x + p[5].x) + (p[6].x + p[7].x));
+                v.y = ((p[0].y + p[1].y) + (p[2].y + p[3].y)) + ((p[4].y + p[5].y) + (p[6].y + p[7].y));
+                v.z = ((p[0].z + p[1].z) + (p[2].z + p[3].z)) + ((p[4].z + p[5].z) + (p[6].z + p[7].z));
+                v.w = ((p[0].w + p[1].w) + (p[2].w + p[3].w)) + ((p[4].w + p[5].w) + (p[6].w + p[7].w));
+                own[pp][k] = v;
+                const int off = pp * PR * PITCH + offw;  // in the segment's partial
+                for (uint32_t i = 1; i < CL; ++i) {
+                  const uint32_t peer = (q + i) % CL;
+                  const uint32_t slot = smem_u32(rx + tslot(peer) * C::PSLOT + off);
+                  st_async_v4(mapa(slot, peer), v, mapa(smem_u32(&rx_full[par]), peer));
+                }
+              }
             }
           }
         }
@@ -849,27 +872,34 @@ __global__ void __launch_bounds__(kThreads, 1) apply_kernel(const __grid_constan
       tr.seg(1, sj);
       if (!*s_bad) {
 #pragma unroll
-        for (int k = 0; k < KE; ++k) {
-          const int e4 = tid + k * kComputeThreads;
-          if (e4 < nch) {
-            const int t = e4 / Q4;
-            const int off = t * PITCH + (e4 % Q4) * 4;
-            float4 sum = q == 0 ? own[k] : *reinterpret_cast<const float4*>(rx + off);
-            for (uint32_t i = 1; i < CL; ++i) {
-              const float4 v = i == q ? own[k] : *reinterpret_cast<const float4*>(rx + i * C::PSLOT + off);
-              sum.x += v.x;
-              sum.y += v.y;
-              sum.z += v.z;
-              sum.w += v.w;
-            }
-            sum.x *= alpha;
-            sum.y *= alpha;
-            sum.z *= alpha;
-            sum.w *= alpha;
-            if (do_ex) {
-              *reinterpret_cast<float4*>(Hs + off) = sum;
-            } else {
-              *reinterpret_cast<float4*>(a.h + static_cast<int64_t>(s.token_start + t) * R + (e4 % Q4) * 4) = sum;
+        for (int pp = 0; pp < NP; ++pp) {
+          if (pp < npass) {
+            const int nq = min(PR, n - pp * PR) * Q4;
+#pragma unroll
+            for (int k = 0; k < KE; ++k) {
+              const int e4 = tid + k * kComputeThreads;
+              if (e4 < nq) {
+                const int t = pp * PR + e4 / Q4;
+                const int off = t * PITCH + (e4 % Q4) * 4;
+                float4 sum = q == 0 ? own[pp][k] : *reinterpret_cast<const float4*>(rx + rslot(0) * C::PSLOT + off);
+                for (uint32_t i = 1; i < CL; ++i) {
+                  const float4 v =
+                      i == q ? own[pp][k] : *reinterpret_cast<const float4*>(rx + rslot(i) * C::PSLOT + off);
+                  sum.x += v.x;
+                  sum.y += v.y;
+                  sum.z += v.z;
+                  sum.w += v.w;
+                }
+                sum.x *= alpha;
+                sum.y *= alpha;
+                sum.z *= alpha;
+                sum.w *= alpha;
+                if (do_ex) {
+                  *reinterpret_cast<float4*>(Hs + off) = sum;
+                } else {
+                  *reinterpret_cast<float4*>(a.h + static_cast<int64_t>(s.token_start + t) * R + (e4 % Q4) * 4) = sum;
+                }
+              }
             }
           }
         }
