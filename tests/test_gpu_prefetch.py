@@ -73,6 +73,24 @@ def test_prefetch_matches_strict_order(cuda, graph, resident, T):
         assert torch.equal(w, g_)
 
 
+@pytest.mark.parametrize("graph", [False, True])
+@pytest.mark.parametrize("rank", [8, 16, 32, 64])
+@pytest.mark.parametrize("resident,T", [(64, 4096), (512, 256), (4, 64)])
+def test_prefetch_ranks_and_segments_per_cluster(cuda, graph, rank, resident, T):
+    """Every rank (stage rings of 3 to 8 stages) with one and with several
+    segments per cluster: the prefetched first stages, the shrink run before
+    the dependency and the expand stages after it share one ring."""
+    dev = torch.device("cuda", 0)
+    calls = _calls(dev, T, r=rank, n_adapters=max(resident, 1), seed=rank)
+    ids = torch.as_tensor(zipf_ids(resident, T, seed=11), device=dev)
+    strict = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=False))
+    pre = WarpPipeEngine(WarpPipeConfig(max_tokens=4096, prefetch_weights=True, prefetch_inputs=True))
+    want = _run(strict, calls, ids, graph)
+    got = _run(pre, calls, ids, graph)
+    for w, g_ in zip(want, got):
+        assert torch.equal(w, g_)
+
+
 def test_input_written_by_previous_kernel(cuda):
     """x of the second call is the first call's output: note_input_write
     keeps the second call's x loads behind the first call."""
