@@ -10,9 +10,10 @@
 // One launch does both halves of one LoRA layer call. The grid is persistent
 // (a fixed number of co-resident CTAs, so the launch can be captured in a CUDA
 // graph) and organised in thread-block clusters of CL CTAs (CL = 2 on B200);
-// the segmenter's ClusterPlan gives each cluster its segments (whole
-// segments on the lowest clusters, helper clusters that take half of the
-// output columns of the largest segments when clusters are left over). For one
+// the segmenter's ClusterPlan gives each cluster its segments (when clusters
+// are left over, the largest segments, at most kPlanMaxHelpers, get a helper
+// cluster that takes half of their output columns; these pairs take the
+// lowest clusters, the whole segments follow). For one
 // segment the CL CTAs of the cluster
 //   1. split d in CL slices: CTA q streams A[:, slice q] and x[segment rows,
 //      slice q] and accumulates a [r x <=32] fp32 partial;
@@ -155,11 +156,11 @@ struct ApplyCfg {
 // production path reads the plan and never runs this code, which keeps it
 // out of the instruction cache. Segments per cluster, for small tables
 // (decode) ordered by decreasing token count. Fewer segments than clusters:
-// the largest segments get a helper cluster each, and the pair splits the
-// segment's output columns (both clusters run the shrink; the second reads A
-// mostly from L2); the whole segments take the lowest clusters, which the
-// hardware dispatches first (with programmatic dependent launch they also
-// start first). More segments than clusters: "snake" dealing (round r gives
+// the largest segments (at most kPlanMaxHelpers) get a helper cluster each,
+// and the pair splits the segment's output columns (both clusters run the
+// shrink; the second reads A mostly from L2); the helper pairs take the
+// lowest clusters, which the hardware dispatches first (with programmatic
+// dependent launch they also start first), the whole segments follow. More segments than clusters: "snake" dealing (round r gives
 // cluster c the segment at sorted position r*G + c or r*G + G-1-c,
 // alternating, with the last, partial round running forward), pairing large
 // segments with small ones. Larger tables go round robin (cluster c takes c,
@@ -203,13 +204,14 @@ __device__ __noinline__ void table_fallback(const ApplyArgs& a, int S_sl, bool d
   const int osplit = (((a.o + 1) / 2) + C::W - 1) / C::W * C::W;  // first column of a segment's second half
   if (do_ex && G > 1 && nseg > 0 && nseg < G && nseg <= kSortMax && a.o - osplit >= static_cast<int>(CL) * C::W) {
     sort_by_size();
-    const int helpers = min(nseg, G - nseg);
+    const int helpers = min(min(nseg, G - nseg), kPlanMaxHelpers);
     const int V = nseg + helpers;
-    const int solo = nseg - helpers;  // whole segments first (lowest clusters start first), then helper pairs
+    // helper pairs first (lowest clusters start first), then whole segments
     tv->nmine = cid < V ? 1 : 0;
     if (tv->nmine) {
-      const int pos = cid < solo ? helpers + cid : (cid - solo) >> 1;
-      const int half = cid < solo ? -1 : ((cid - solo) & 1);
+      const bool pair = cid < 2 * helpers;
+      const int pos = pair ? cid >> 1 : cid - helpers;
+      const int half = pair ? (cid & 1) : -1;
       tv->seg_half = half;
       const int ob = half == 1 ? osplit : 0;
       const int olen = half < 0 ? a.o : (half == 0 ? osplit : a.o - osplit);

@@ -44,13 +44,22 @@ constexpr int kStageCols = 256;
 // Per-cluster work assignment of the clustered apply kernel, computed once
 // per step by the segmenter for one cluster count G: segments ordered by
 // decreasing token count; mode 1 (fewer segments than clusters) gives the
-// largest segments a helper cluster that takes half of their output columns,
-// mode 2 (up to kPlanMaxSegs segments) deals them in snake order; mode 0:
-// no plan (the kernel deals round robin). Slot r * G + c holds round r of
+// largest segments (at most kPlanMaxHelpers) a helper cluster that takes half
+// of their output columns, the helper pairs on the lowest clusters; mode 2
+// (up to kPlanMaxSegs segments) deals them in snake order; mode 0: no plan
+// (the kernel deals round robin). Slot r * G + c holds round r of
 // cluster c.
 constexpr int kPlanRounds = 4;
 constexpr int kPlanMaxClusters = 160;
 constexpr int kPlanMaxSegs = 128;
+// Helper pairs per plan. The helper pairs hold the largest segments and go
+// first (the hardware dispatches low clusters first); measured on the
+// config-1 step at 8 / 32 / 64 / 128 resident adapters, 8 pairs first beat
+// every pair the free clusters allow placed after the whole segments
+// (1.43 / 1.83 / 2.13 / 2.63 ms against 1.46 / 1.86 / 2.17 / 2.81 ms):
+// more pairs first push the 16-stage whole segments to the clusters that
+// start last, fewer leave the largest segments whole.
+constexpr int kPlanMaxHelpers = 8;
 struct ClusterPlan {
   int4 hdr;  // x: mode, y: segments, z: G, w: helper count (mode 1)
   int count[kPlanMaxClusters];  // segments of cluster c

@@ -59,8 +59,8 @@ __device__ __forceinline__ int block_exclusive_scan(int v, int* warp_buf, int* t
 // Pass 3: the clustered apply kernel's per-cluster assignment for G
 // clusters (ClusterPlan). Segments are ranked by decreasing token count
 // (ties by position); fewer segments than clusters: position p of the
-// first `helpers` goes to clusters 2p and 2p + 1 (output-column halves),
-// the rest to one cluster each; more: round r gives cluster c the segment
+// first `helpers` (at most kPlanMaxHelpers) goes to clusters 2p and 2p + 1
+// (output-column halves), the rest to one cluster each after them; more: round r gives cluster c the segment
 // at position r*G + c (r*G + G-1-c on odd rounds).
 __device__ void write_cluster_plan(const DevSeg* segs, int nseg, ClusterPlan* plan, int G) {
   __shared__ int order[kPlanMaxSegs];
@@ -69,7 +69,7 @@ __device__ void write_cluster_plan(const DevSeg* segs, int nseg, ClusterPlan* pl
   if (G > 1 && G <= kPlanMaxClusters && nseg > 0 && nseg <= kPlanMaxSegs && nseg != G &&
       (nseg + G - 1) / G <= kPlanRounds)
     mode = nseg < G ? 1 : 2;
-  const int helpers = mode == 1 ? min(nseg, G - nseg) : 0;
+  const int helpers = mode == 1 ? min(min(nseg, G - nseg), kPlanMaxHelpers) : 0;
   if (mode) {
     if (tid < nseg) {
       const int ct = segs[tid].token_count;
@@ -85,15 +85,14 @@ __device__ void write_cluster_plan(const DevSeg* segs, int nseg, ClusterPlan* pl
       plan->half[c] = -1;
       int n = 0;
       if (mode == 1) {
-        // the unhelped segments (whole output range, the most work) go to
-        // the lowest clusters, which the hardware dispatches first; the helper
-        // pairs of the largest segments follow
+        // the helper pairs of the largest segments take the lowest
+        // clusters, which the hardware dispatches first; the whole segments
+        // follow in decreasing size
         const int V = nseg + helpers;
-        const int solo = nseg - helpers;
         if (c < V) {
-          const int j = c - solo;
-          const int pos = c < solo ? helpers + c : j >> 1;
-          plan->half[c] = c < solo ? -1 : (j & 1);
+          const bool pair = c < 2 * helpers;
+          const int pos = pair ? c >> 1 : c - helpers;
+          plan->half[c] = pair ? (c & 1) : -1;
           plan->seg[c] = segs[order[pos]];
           n = 1;
         }
